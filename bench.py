@@ -1,0 +1,416 @@
+"""Benchmark: Soft-DTW DP cells/s, forward + backward, on the headline workload (B=256 pairs per GPU,
+N=M=512, d=64, fp32, gamma=0.1, no band): ``SoftDTW(gamma=0.1)(X, Y).sum().backward()`` with X requiring
+grad — the cost matrix, the forward wavefront, the backward wavefront and the grad_X contraction.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload NAME]
+
+One process per GPU (torchrun for N > 1). Each rank processes its own seeded batch of B pairs (weak
+scaling: per-GPU work is fixed; no collective on the data path). Prints ONE JSON line on rank 0.
+
+* value       cells processed by all ranks / max over ranks of the summed per-step device time
+              (CUDA events around each step; L2 flushed between steps, outside the timed events)
+* e2e         the same metric through the public API with inputs in pinned host memory: H2D copy of
+              X and Y, the step, D2H read of the loss, all inside the timed region
+* roofline    the dominant kernel (by device time per step), timed alone through the C ABI with CUDA
+              events on its stream; algorithmic bytes per DP cell / duration vs measured HBM bandwidth
+* cpu_baseline  the reference's own CPU operator (compiled from its source, oracle/_ref) driven by the
+              reference's module glue, on a bounded sample of the same workload, all host threads
+* --impl reference: that same CPU path as the reference arm (rank 0 only)
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+from torchsoftdtw_b200.workloads import WORKLOADS, make_inputs  # noqa: E402  (pure torch, no native load)
+
+L2_FLUSH_BYTES = 256 << 20
+
+
+# ---------------------------------------------------------------------------------------------------
+def dist_env():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", str(rank)))
+    return rank, world, local
+
+
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 100 ms in the background."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.idx = gpu_index
+        self.tmp = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(gpu_index), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=self.tmp, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        self.marks = []
+
+    def mark(self):
+        self.tmp.flush()
+        self.marks.append(self._count())
+
+    def _count(self):
+        try:
+            with open(self.tmp.name) as f:
+                return sum(1 for _ in f)
+        except OSError:
+            return 0
+
+    def stop(self):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+        with open(self.tmp.name) as f:
+            rows = [r.strip().split(", ") for r in f if r.strip()]
+        os.unlink(self.tmp.name)
+        return rows
+
+    @staticmethod
+    def summarize(rows, first: int):
+        sel = rows[first:] if len(rows) > first else rows[-3:]
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in sel:
+            try:
+                sm.append(float(r[1]))
+                mx = float(r[2])
+                for k, v in zip(names, r[5:9]):
+                    if v.strip() == "Active":
+                        reasons.add(k)
+            except (ValueError, IndexError):
+                continue
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------------------------------
+# The reference's CPU path (timed baseline and reference arm)
+# ---------------------------------------------------------------------------------------------------
+class _RefAutograd(torch.autograd.Function):
+    """The reference's SoftDTWAutograd glue (softdtw.py:33-48) over its compiled CPU operator."""
+
+    ops = None
+
+    @staticmethod
+    def forward(ctx, D, lx, ly, gamma, bw):
+        costs, R = _RefAutograd.ops.forward(D, lx, ly, gamma, bw)
+        ctx.save_for_backward(D, R, lx, ly)
+        ctx.gamma, ctx.bw = gamma, bw
+        return costs
+
+    @staticmethod
+    def backward(ctx, g):
+        D, R, lx, ly = ctx.saved_tensors
+        E = _RefAutograd.ops.backward(D, R, lx, ly, ctx.gamma, ctx.bw)
+        return g.unsqueeze(-1).unsqueeze(-1) * E, None, None, None, None
+
+
+def reference_cpu_step(X, Y, lx, ly, w):
+    from torchsoftdtw_b200.distances import pairwise_l2_squared  # same expression as the reference's
+
+    Xr = X.detach().requires_grad_(True)
+    D = pairwise_l2_squared(Xr, Y)
+    costs = _RefAutograd.apply(D, lx, ly, w.gamma, w.bandwidth)
+    if w.normalize:
+        costs = costs / (lx + ly - 1).to(costs.dtype)
+    costs.sum().backward()
+    return Xr.grad
+
+
+def cpu_reference_measure(w, sample_pairs: int, steps: int, warmup: int, min_seconds: float = 0.0):
+    """Cells/s of the reference CPU path on `sample_pairs` pairs of the workload, all host threads."""
+    from oracle import oracle as O
+    from torchsoftdtw_b200.workloads import count_cells
+
+    if not O.ref_available():
+        O.build()
+    _RefAutograd.ops = O.load_ref()
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    X, Y, lx, ly, _ = make_inputs(w.name, seed=1000, batch=sample_pairs)
+    cells = count_cells(lx, ly, w.bandwidth)
+    for _ in range(warmup):
+        reference_cpu_step(X, Y, lx, ly, w)
+    times = []
+    t_total = 0.0
+    while len(times) < steps or t_total < min_seconds:
+        t0 = time.perf_counter()
+        reference_cpu_step(X, Y, lx, ly, w)
+        dt = time.perf_counter() - t0
+        times.append(dt)
+        t_total += dt
+    mean = sum(times) / len(times)
+    return {"value": cells / mean, "unit": "cells/s", "cores": threads, "kind": "reference",
+            "sample": f"{sample_pairs} pairs of the {w.name} workload ({cells} cells) per step, "
+                      f"{len(times)} steps, module fwd+bwd (pairwise_l2_squared + reference CPU op + autograd)",
+            "s_per_step": mean}
+
+
+def run_reference_arm(args, w, rank):
+    if rank != 0:
+        return
+    sample = args.cpu_sample
+    r = cpu_reference_measure(w, sample, max(args.steps, 1), max(args.warmup, 1))
+    line = {
+        "impl": "reference", "metric": metric_name(w), "value": r["value"], "unit": "cells/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": r["s_per_step"] * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": dtype_name(w), "data": "synthetic",
+        "config": config_of(w, args.gpus),
+        "cpu_baseline": {k: r[k] for k in ("value", "unit", "cores", "kind", "sample")},
+        "e2e": {"value": r["value"], "unit": "cells/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------------------------------
+def metric_name(w):
+    return f"Soft-DTW DP cells/sec fwd+bwd (B={w.B},N={w.N},M={w.M},d={w.d} {dtype_name(w)})"
+
+
+def dtype_name(w):
+    return "f64" if w.dtype == torch.float64 else "f32"
+
+
+def config_of(w, world):
+    return {"workload": w.name, "pairs_per_gpu": w.B, "global_batch": w.B * world, "N": w.N, "M": w.M, "d": w.d,
+            "gamma": w.gamma, "bandwidth": w.bandwidth, "normalize": w.normalize,
+            "parallelism": f"batch-shard x{world}", "step": "SoftDTW(X,Y).sum().backward(), grad_X only",
+            "l2": "flushed between timed steps (256 MiB write, outside the timed events)"}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", default="medium", choices=sorted(WORKLOADS))
+    ap.add_argument("--cpu-sample", type=int, default=16, help="pairs per CPU-baseline step")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile", action="store_true", help="small run for profilers: no extras, few steps")
+    args = ap.parse_args()
+    rank, world, local = dist_env()
+    w = WORKLOADS[args.workload]
+
+    if args.impl == "reference":
+        run_reference_arm(args, w, rank)
+        return
+
+    import torch.distributed as dist
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    import torchsoftdtw_b200 as T
+    from torchsoftdtw_b200.workloads import count_cells
+
+    X, Y, lx, ly, _ = make_inputs(w.name, seed=rank)
+    cells_rank = count_cells(lx, ly, w.bandwidth)
+    Xd, Yd, lxd, lyd = X.to(dev), Y.to(dev), lx.to(dev), ly.to(dev)
+    Xd.requires_grad_(True)
+    module = T.SoftDTW(gamma=w.gamma, bandwidth=w.bandwidth, normalize=w.normalize)
+    flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
+
+    def step():
+        Xd.grad = None
+        loss = module(Xd, Yd, lxd, lyd).sum()
+        loss.backward()
+        return loss
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+
+    for _ in range(max(args.warmup, 1)):
+        step()
+    torch.cuda.synchronize()
+    T.check_errors(dev)
+
+    sampler = None if args.profile else ClockSampler(local)
+    steps = args.steps
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    if sampler:
+        time.sleep(0.3)
+        sampler.mark()
+    barrier()
+    torch.cuda.synchronize()
+    for k in range(steps):
+        flush.fill_(float(k))
+        starts[k].record()
+        step()
+        ends[k].record()
+    torch.cuda.synchronize()
+    barrier()
+    if sampler:
+        sampler.mark()
+    ms_rank = sum(s.elapsed_time(e) for s, e in zip(starts, ends))
+    T.check_errors(dev)
+    ms_t = torch.tensor([ms_rank], dtype=torch.float64, device=dev)
+    cells_t = torch.tensor([float(cells_rank)], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
+        dist.all_reduce(cells_t, op=dist.ReduceOp.SUM)
+    ms_max = float(ms_t.item())
+    total_cells = float(cells_t.item())
+    value = total_cells * steps / (ms_max / 1e3)
+    # kernels of this library per step: pairwise_l2, fill R, forward wavefront, backward wavefront, grad_X
+    launches_per_step = 5
+
+    result = {
+        "metric": metric_name(w), "value": value, "unit": "cells/s", "n_gpus": world, "steps": steps,
+        "warmup": args.warmup, "ms_per_step": ms_max / steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": dtype_name(w), "data": "synthetic (seeded N(0,1) per rank; no dataset)",
+        "config": config_of(w, world), "gpu_launches": launches_per_step * steps,
+    }
+    if args.profile:
+        if rank == 0:
+            print(json.dumps(result), flush=True)
+        if world > 1:
+            dist.destroy_process_group()
+        return
+
+    # ---- e2e through the public API with host buffers ----------------------------------------------
+    Xh = X.pin_memory()
+    Yh = Y.pin_memory()
+    loss_h = torch.empty((), dtype=torch.float32).pin_memory()
+    e2e_steps = max(10, steps // 4)
+    barrier()
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(e2e_steps):
+        Xs = Xh.to(dev, non_blocking=True).requires_grad_(True)
+        Ys = Yh.to(dev, non_blocking=True)
+        loss = module(Xs, Ys, lxd, lyd).sum()
+        loss.backward()
+        loss_h.copy_(loss.detach(), non_blocking=True)
+    e1.record()
+    torch.cuda.synchronize()
+    barrier()
+    e2e_ms = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
+    e2e_value = total_cells * e2e_steps / (float(e2e_ms.item()) / 1e3)
+    result["e2e"] = {"value": e2e_value, "unit": "cells/s",
+                     "h2d_bytes_per_step": Xh.numel() * Xh.element_size() + Yh.numel() * Yh.element_size(),
+                     "d2h_bytes_per_step": loss_h.element_size()}
+
+    # ---- per-kernel device time through the C ABI (dominant kernel -> roofline) --------------------
+    kt = kernel_times(T, Xd.detach(), Yd, lxd, lyd, w, dev, flush)
+    clocks = sampler.summarize(sampler.stop(), sampler.marks[0]) if sampler else None
+    if rank == 0:
+        hbm, peak_kind = peaks()
+        name, ms = max(kt.items(), key=lambda kv: kv[1])
+        bytes_per_cell = ALGO_BYTES[name] * (8 if w.dtype == torch.float64 else 4)
+        achieved = cells_rank * bytes_per_cell / (ms / 1e3) / 1e9
+        result["roofline"] = {"bound": "hbm", "kernel": name, "achieved": achieved, "peak": hbm,
+                              "unit": "GB/s", "frac": achieved / hbm, "traffic": None,
+                              "peak_source": peak_kind,
+                              "algorithmic_bytes_per_cell": bytes_per_cell, "launch_ms": ms,
+                              "per_kernel_ms": kt}
+        result["clocks"] = clocks
+        if not args.no_cpu_baseline and world == 1:
+            r = cpu_reference_measure(w, args.cpu_sample, 2, 1, min_seconds=10.0)
+            result["cpu_baseline"] = {k: r[k] for k in ("value", "unit", "cores", "kind", "sample")}
+        print(json.dumps(result), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+# Algorithmic DRAM bytes per DP cell, in units of the element size, of each timed C-ABI call:
+#   forward  : read D + write R                      = 2
+#   backward : read R + write E                      = 2
+#   pairwise : write D (X, Y reads are O((N+M)d/NM)) = 1
+#   grad     : read E + read D (clamp mask)          = 2
+ALGO_BYTES = {"sdtw_forward": 2, "sdtw_backward": 2, "sdtw_pairwise_l2": 1, "sdtw_grad_l2": 2}
+
+
+def kernel_times(T, X, Y, lx, ly, w, dev, flush, reps: int = 20):
+    """Average device time (ms) of each C-ABI call of one step, CUDA events on the launching stream,
+    L2 flushed before each launch."""
+    import ctypes
+
+    from torchsoftdtw_b200 import _ext
+
+    lib = _ext.capi()
+    B, N, d = X.shape
+    M = Y.shape[1]
+    code = 1 if X.dtype == torch.float64 else 0
+    D = torch.empty(B, N, M, device=dev, dtype=X.dtype)
+    R = torch.empty(B, N + 2, M + 2, device=dev, dtype=X.dtype)
+    E = torch.empty(B, N, M, device=dev, dtype=X.dtype)
+    costs = torch.empty(B, device=dev, dtype=X.dtype)
+    g = torch.ones(B, device=dev, dtype=X.dtype)
+    gX = torch.empty_like(X)
+    err = torch.zeros(1, device=dev, dtype=torch.int32)
+    wsf = lib.sdtw_forward_workspace_bytes(B, N, M, code)
+    wsb = lib.sdtw_backward_workspace_bytes(B, N, M, code)
+    ws = torch.empty(max(wsf, wsb), device=dev, dtype=torch.uint8)
+    stream = torch.cuda.current_stream()
+    sp = ctypes.c_void_p(stream.cuda_stream)
+    p = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+    is32 = 1 if lx.dtype == torch.int32 else 0
+    calls = {
+        "sdtw_pairwise_l2": lambda: lib.sdtw_pairwise_l2(code, p(X), p(Y), B, N, M, d, p(D), sp),
+        "sdtw_forward": lambda: lib.sdtw_forward(code, p(D), B, N, M, p(lx), p(ly), is32, w.gamma, w.bandwidth,
+                                                 p(R), p(costs), p(ws), wsf, p(err), sp),
+        "sdtw_backward": lambda: lib.sdtw_backward(code, p(D), p(R), B, N, M, p(lx), p(ly), is32, w.gamma,
+                                                   w.bandwidth, p(E), p(ws), wsb, p(err), sp),
+        "sdtw_grad_l2": lambda: lib.sdtw_grad_l2(code, p(X), p(Y), p(D), p(E), p(g), B, N, M, d, p(gX), None, sp),
+    }
+    out = {}
+    for name, fn in calls.items():
+        st = fn()
+        assert st == 0, (name, lib.sdtw_status_string(st))
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(reps)]
+        for a, b in ev:
+            flush.fill_(1.0)
+            a.record(stream)
+            fn()
+            b.record(stream)
+        torch.cuda.synchronize()
+        out[name] = sum(a.elapsed_time(b) for a, b in ev) / reps
+    assert lib.sdtw_read_error_word(p(err), sp) == 0
+    return out
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,114 @@
+/*
+ * torchsoftdtw_b200 — C ABI of the sm_100a Soft-DTW kernel library (libsdtw_b200.so).
+ *
+ * Plain pointers and sizes only: no torch types. Every pointer argument named a "device pointer" is
+ * CUDA global memory on the current device; `stream` is a cudaStream_t (0 = legacy default stream).
+ * Calls only enqueue work on `stream`: none synchronises, none reads device data on the host, none
+ * allocates device memory. Scratch memory is passed in by the caller as `workspace` (size from the
+ * matching *_workspace_bytes function), so every call can be captured in a CUDA graph.
+ *
+ * Layouts (row-major, contiguous):
+ *   D  (B, N, M)      pairwise cost matrix                        [reference: softdtw.cpp:342-345 schemas]
+ *   R  (B, N+2, M+2)  forward DP table, +inf border, R[:,0,0] = 0  [reference: softdtw.cu:485-492]
+ *   E  (B, N, M)      d costs / d D                                [reference: softdtw.cu:636-641]
+ *   X  (B, N, d), Y (B, M, d) sequences for the fused distance path
+ *   lengths_x, lengths_y: (B,) int64, or int32 when lengths_int32 != 0
+ *
+ * Errors: a negative status is an invalid argument (nothing was launched); a positive status is a
+ * cudaError_t from a launch. Device-side failures (a strip wait that ran out, a length outside
+ * [0, N]/[0, M]) are OR-ed into the caller's sticky `err_word` (device pointer to one uint32, see
+ * SDTW_ERR_*); read it with sdtw_read_error_word (which synchronises the stream). Pairs with an
+ * invalid length get a NaN cost.
+ */
+#ifndef SDTW_B200_H
+#define SDTW_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef int sdtw_status;
+
+#define SDTW_OK 0
+#define SDTW_EINVAL (-1)     /* a size, pointer or parameter is invalid */
+#define SDTW_EDTYPE (-2)     /* unsupported dtype code */
+#define SDTW_EWORKSPACE (-3) /* workspace missing or too small */
+#define SDTW_EDEVICE (-4)    /* no usable sm_100 device / kernel image */
+
+#define SDTW_ERR_TIMEOUT 1u    /* a wait on a neighbouring strip's progress ran out (kernel returned early) */
+#define SDTW_ERR_BAD_LENGTH 2u /* some lengths value was outside [0, N] or [0, M] */
+
+typedef enum { SDTW_F32 = 0, SDTW_F64 = 1 } sdtw_dtype;
+
+/* Human-readable text of a status. */
+const char* sdtw_status_string(sdtw_status status);
+
+/* Columns [*lo, *hi] of row i that lie in the Sakoe-Chiba band of an (nx, ny) pair, intersected
+ * with [0, ny). Host function. Restates the per-cell predicate in_band of the reference
+ * (src/torchsoftdtw/csrc/band.h:23-38) as a per-row interval. */
+void sdtw_band_row_range(int64_t i, int64_t nx, int64_t ny, int64_t bandwidth, int64_t* lo, int64_t* hi);
+
+/* Number of DP cells evaluated for one pair: in-band cells (i, j) with i < nx, j < ny. Host function. */
+int64_t sdtw_pair_cells(int64_t nx, int64_t ny, int64_t bandwidth);
+
+/* Reads (synchronising `stream`) and clears the sticky device error word. Returns the SDTW_ERR_* bits,
+ * or 0xffffffff if the copy failed. */
+uint32_t sdtw_read_error_word(uint32_t* err_word, void* stream);
+
+/* Upper bound (seconds) of every device-side wait on another strip; default 2.0. Process-wide. */
+void sdtw_set_wait_timeout(double seconds);
+
+/* ---------------------------------------------------------------------------------------------------
+ * Forward: costs[b] = soft-DTW of D[b] restricted to [0, nx) x [0, ny), and the DP table R.
+ * Replaces the reference CUDA launcher softdtw_cuda_forward (src/torchsoftdtw/csrc/cuda/softdtw.cu:464-540),
+ * reached through the op torchsoftdtw::forward (src/torchsoftdtw/csrc/softdtw.cpp:343, :361-367).
+ * D, R, costs are `dtype`; R must hold (B, N+2, M+2) elements; D may be any device pointer (no
+ * alignment requirement). bandwidth < 0 disables the band.
+ * ------------------------------------------------------------------------------------------------- */
+size_t sdtw_forward_workspace_bytes(int64_t B, int64_t N, int64_t M, sdtw_dtype dtype);
+sdtw_status sdtw_forward(sdtw_dtype dtype, const void* D, int64_t B, int64_t N, int64_t M,
+                         const void* lengths_x, const void* lengths_y, int lengths_int32, double gamma,
+                         int64_t bandwidth, void* R, void* costs, void* workspace, size_t workspace_bytes,
+                         uint32_t* err_word, void* stream);
+
+/* ---------------------------------------------------------------------------------------------------
+ * Backward: E = d costs / d D (unscaled; the caller multiplies by the upstream gradient).
+ * Replaces softdtw_cuda_backward (src/torchsoftdtw/csrc/cuda/softdtw.cu:543-642), reached through the op
+ * torchsoftdtw::backward (src/torchsoftdtw/csrc/softdtw.cpp:344, :368-373). R must be the forward's
+ * output for the same D, lengths, gamma and bandwidth: the successor weights are recomputed from R
+ * alone (softmin weights of each cell's three predecessors), which equals the reference's
+ * exp((R[s] - R[p] - D[s]) / gamma) whenever R[s] = D[s] + softmin(predecessors of s).
+ * ------------------------------------------------------------------------------------------------- */
+size_t sdtw_backward_workspace_bytes(int64_t B, int64_t N, int64_t M, sdtw_dtype dtype);
+sdtw_status sdtw_backward(sdtw_dtype dtype, const void* D, const void* R, int64_t B, int64_t N, int64_t M,
+                          const void* lengths_x, const void* lengths_y, int lengths_int32, double gamma,
+                          int64_t bandwidth, void* E, void* workspace, size_t workspace_bytes,
+                          uint32_t* err_word, void* stream);
+
+/* ---------------------------------------------------------------------------------------------------
+ * Pairwise squared Euclidean cost: D[b,i,j] = (|x_i|^2 + |y_j|^2) - 2 x_i.y_j, clamped at 0.
+ * Replaces the reference's pairwise_l2_squared (src/torchsoftdtw/distances.py:4-18) on the module path.
+ * Cells where the unclamped value is negative are stored as -0.0 (sign bit set), so that the
+ * gradient kernel can reproduce the clamp's zero gradient there; -0.0 compares and adds as 0.
+ * ------------------------------------------------------------------------------------------------- */
+sdtw_status sdtw_pairwise_l2(sdtw_dtype dtype, const void* X, const void* Y, int64_t B, int64_t N, int64_t M,
+                             int64_t d, void* D, void* stream);
+
+/* ---------------------------------------------------------------------------------------------------
+ * Gradient of sum_b g[b] * costs[b] through the squared-L2 cost (the autograd of distances.py:14-18):
+ *   G = g[b] * E * [D >= 0 before the clamp]  (read from the sign bit written by sdtw_pairwise_l2)
+ *   grad_X = 2 * (rowsum(G) * X - G @ Y),   grad_Y = 2 * (colsum(G) * Y - G^T @ X)
+ * g is (B,) `dtype` on the device; grad_X / grad_Y may be NULL to skip them.
+ * ------------------------------------------------------------------------------------------------- */
+sdtw_status sdtw_grad_l2(sdtw_dtype dtype, const void* X, const void* Y, const void* D, const void* E,
+                         const void* g, int64_t B, int64_t N, int64_t M, int64_t d, void* grad_X, void* grad_Y,
+                         void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SDTW_B200_H */

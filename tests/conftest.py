@@ -1,0 +1,36 @@
+import glob
+import os
+import sys
+
+import numpy as np
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+GOLDEN = os.path.join(ROOT, "tests", "golden")
+
+
+def pytest_configure(config):
+    config.addinivalue_line("markers", "gpu: needs a CUDA sm_100 device (B200); run with -m gpu")
+
+
+def golden(name: str) -> dict:
+    with np.load(os.path.join(GOLDEN, name + ".npz")) as z:
+        return {k: z[k] for k in z.files}
+
+
+def golden_names(prefix: str) -> list[str]:
+    return sorted(os.path.basename(p)[:-4] for p in glob.glob(os.path.join(GOLDEN, prefix + "*.npz")))
+
+
+@pytest.fixture(scope="session")
+def cuda():
+    """The CUDA device for GPU tests. A GPU test on a machine without CUDA fails (it is never skipped)."""
+    import torch
+
+    assert torch.cuda.is_available(), "GPU test selected (-m gpu) but no CUDA device is available"
+    import torchsoftdtw_b200  # noqa: F401  (loads the native libraries)
+
+    return torch.device("cuda", 0)

@@ -1,0 +1,154 @@
+"""GPU parity of the SoftDTW module: the fused squared-L2 path (torchsoftdtw_b200::l2_forward /
+l2_backward: cost matrix, wavefront and gradient contraction in native kernels) against the reference's
+module (golden fixtures) and the oracle's module restatement; the l1 / cosine paths; module options.
+
+Tolerances: fp64 costs rtol 1e-10, fp64 gradients rtol 1e-8 (D is summed in a different order than
+torch's bmm); fp32 costs rtol 1e-5 / atol 1e-6; fp32 gradients vs the oracle in fp64 within the literal
+tolerance or no worse than the reference's own fp32 error."""
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import golden, golden_names
+from oracle import oracle as O
+import torchsoftdtw_b200 as T
+from torchsoftdtw_b200 import workloads
+
+pytestmark = pytest.mark.gpu
+
+
+def run_module(X, Y, lx, ly, gamma, bw, normalize, dev, need=(True, True), distance="l2_squared"):
+    Xd = torch.as_tensor(X).to(dev).requires_grad_(need[0])
+    Yd = torch.as_tensor(Y).to(dev).requires_grad_(need[1])
+    lxd = torch.as_tensor(lx).to(dev)
+    lyd = torch.as_tensor(ly).to(dev)
+    costs = T.SoftDTW(gamma=gamma, bandwidth=bw, normalize=normalize, distance=distance)(Xd, Yd, lxd, lyd)
+    costs.sum().backward()
+    torch.cuda.synchronize()
+    T.check_errors(dev)
+    gx = Xd.grad.cpu().numpy() if need[0] else None
+    gy = Yd.grad.cpu().numpy() if need[1] else None
+    return costs.detach().cpu().numpy(), gx, gy
+
+
+def grad_contract(ours, X, Y, lx, ly, gamma, bw, normalize, which):
+    """fp32 gradient vs fp64 oracle: literal tolerance or no worse than the reference's fp32 error."""
+    _, gx64, gy64 = O.module_forward_backward(X.astype(np.float64), Y.astype(np.float64), lx, ly, gamma, bw,
+                                              normalize)
+    _, gx32, gy32 = O.module_forward_backward(X.astype(np.float32), Y.astype(np.float32), lx, ly, gamma, bw,
+                                              normalize)
+    exact = gx64 if which == "x" else gy64
+    refe = gx32 if which == "x" else gy32
+    err = float(np.max(np.abs(ours.astype(np.float64) - exact)))
+    with np.errstate(invalid="ignore"):
+        err_ref = float(np.nanmax(np.abs(refe.astype(np.float64) - exact)))
+    literal = 1e-6 + 1e-5 * float(np.max(np.abs(exact)))
+    assert err <= max(literal, err_ref), (which, err, err_ref, literal)
+
+
+@pytest.mark.parametrize("name", golden_names("mod_"))
+def test_module_fixture(cuda, name):
+    g = golden(name)
+    X, Y = g["X"], g["Y"]
+    gamma, bw, norm = float(g["gamma"]), int(g["bw"]), bool(g["normalize"])
+    c, gx, gy = run_module(X, Y, g["lx"], g["ly"], gamma, bw, norm, cuda)
+    if X.dtype == np.float64:
+        np.testing.assert_allclose(c, g["costs"], rtol=1e-10, atol=1e-10)
+        np.testing.assert_allclose(gx, g["grad_X"], rtol=1e-8, atol=1e-8)
+        np.testing.assert_allclose(gy, g["grad_Y"], rtol=1e-8, atol=1e-8)
+    else:
+        np.testing.assert_allclose(c, g["costs"], rtol=1e-5, atol=1e-6)
+        grad_contract(gx, X, Y, g["lx"], g["ly"], gamma, bw, norm, "x")
+        grad_contract(gy, X, Y, g["lx"], g["ly"], gamma, bw, norm, "y")
+
+
+@pytest.mark.parametrize("name,batch", [("readme", 8), ("medium", 16), ("ragged", 128), ("long", 1),
+                                        ("largebatch", 2048)])
+def test_module_workloads_vs_oracle(cuda, name, batch):
+    X, Y, lx, ly, w = workloads.make_inputs(name, batch=batch)
+    Xn, Yn = X.numpy(), Y.numpy()
+    c, gx, _ = run_module(Xn, Yn, lx.numpy(), ly.numpy(), w.gamma, w.bandwidth, w.normalize, cuda,
+                          need=(True, False))
+    c64, gx64, _ = O.module_forward_backward(Xn.astype(np.float64), Yn.astype(np.float64), lx.numpy(), ly.numpy(),
+                                             w.gamma, w.bandwidth, w.normalize)
+    if w.dtype == torch.float64:
+        np.testing.assert_allclose(c, c64, rtol=1e-10, atol=1e-10)
+        np.testing.assert_allclose(gx, gx64, rtol=1e-8, atol=1e-8)
+    else:
+        np.testing.assert_allclose(c, c64, rtol=1e-5, atol=1e-6)
+        grad_contract(gx, Xn, Yn, lx.numpy(), ly.numpy(), w.gamma, w.bandwidth, w.normalize, "x")
+    # no gradient reaches the padded frames of X
+    pad = np.arange(X.shape[1])[None, :] >= lx.numpy()[:, None]
+    assert np.all(gx[pad] == 0.0)
+
+
+def test_module_grad_selection_and_unbatched(cuda):
+    torch.manual_seed(8)
+    X = torch.randn(2, 5, 4, dtype=torch.float64)
+    Y = torch.randn(2, 7, 4, dtype=torch.float64)
+    lx, ly = torch.tensor([5, 5]), torch.tensor([7, 7])
+    c1, gx1, gy1 = run_module(X, Y, lx, ly, 1.0, -1, False, cuda, need=(True, True))
+    c2, gx2, _ = run_module(X, Y, lx, ly, 1.0, -1, False, cuda, need=(True, False))
+    c3, _, gy3 = run_module(X, Y, lx, ly, 1.0, -1, False, cuda, need=(False, True))
+    np.testing.assert_array_equal(gx1, gx2)
+    np.testing.assert_array_equal(gy1, gy3)
+    cost = T.SoftDTW(gamma=1.0)(X[0].to(cuda), Y[0].to(cuda))
+    assert cost.shape == (1,)
+    torch.testing.assert_close(cost.cpu(), torch.from_numpy(c1[:1]), rtol=1e-12, atol=1e-12)
+
+
+def test_module_normalize_divisor(cuda):
+    torch.manual_seed(9)
+    X = torch.randn(2, 6, 4, dtype=torch.float64, device=cuda)
+    Y = torch.randn(2, 6, 4, dtype=torch.float64, device=cuda)
+    lx, ly = torch.tensor([4, 6], device=cuda), torch.tensor([5, 3], device=cuda)
+    raw = T.SoftDTW(gamma=1.0, normalize=False)(X, Y, lx, ly)
+    norm = T.SoftDTW(gamma=1.0, normalize=True)(X, Y, lx, ly)
+    assert torch.allclose(norm, raw / (lx + ly - 1).to(raw.dtype))
+
+
+@pytest.mark.parametrize("gamma,bw,normalize", [(1.0, -1, False), (0.5, 2, False), (1.0, -1, True), (0.5, 2, True)])
+def test_module_gradcheck_fused_path(cuda, gamma, bw, normalize):
+    torch.manual_seed(600)
+    X = torch.randn(2, 6, 4, dtype=torch.float64, device=cuda, requires_grad=True)
+    Y = torch.randn(2, 5, 4, dtype=torch.float64, device=cuda, requires_grad=True)
+    m = T.SoftDTW(gamma=gamma, bandwidth=bw, normalize=normalize)
+    torch.autograd.gradcheck(lambda x, y: m(x, y), (X, Y), eps=1e-6, atol=1e-4, rtol=1e-3)
+
+
+def test_fused_path_equals_unfused_composition(cuda):
+    torch.manual_seed(202)
+    X = torch.randn(3, 40, 8, dtype=torch.float64, device=cuda, requires_grad=True)
+    Y = torch.randn(3, 33, 8, dtype=torch.float64, device=cuda, requires_grad=True)
+    lx, ly = torch.tensor([40, 31, 17], device=cuda), torch.tensor([33, 20, 33], device=cuda)
+    fused = T.SoftDTW(gamma=0.3, bandwidth=6)(X, Y, lx, ly)
+    gX, gY = torch.autograd.grad(fused.sum(), (X, Y))
+    unfused = T.soft_dtw(T.pairwise_l2_squared(X, Y), lx, ly, 0.3, 6)
+    uX, uY = torch.autograd.grad(unfused.sum(), (X, Y))
+    torch.testing.assert_close(fused, unfused, rtol=1e-10, atol=1e-10)
+    torch.testing.assert_close(gX, uX, rtol=1e-8, atol=1e-8)
+    torch.testing.assert_close(gY, uY, rtol=1e-8, atol=1e-8)
+
+
+@pytest.mark.parametrize("distance", ["l1", "cosine"])
+def test_other_distances(cuda, distance):
+    torch.manual_seed(31)
+    X = torch.randn(3, 12, 5, dtype=torch.float64)
+    Y = torch.randn(3, 9, 5, dtype=torch.float64)
+    c, gx, gy = run_module(X, Y, torch.tensor([12, 10, 7]), torch.tensor([9, 9, 4]), 0.7, 3, True, cuda,
+                           distance=distance)
+    D = T.pairwise_l1(X, Y) if distance == "l1" else T.pairwise_cosine(X, Y)
+    cr, _ = O.forward(D.numpy(), [12, 10, 7], [9, 9, 4], 0.7, 3)
+    np.testing.assert_allclose(c, cr / (np.array([12, 10, 7]) + np.array([9, 9, 4]) - 1), rtol=1e-10, atol=1e-10)
+    assert np.isfinite(gx).all() and np.isfinite(gy).all()
+
+
+def test_identical_sequences_clamp(cuda):
+    # X == Y makes |x|^2 + |y|^2 - 2x.y round below 0 on the diagonal: the clamp must hold and gradients
+    # stay finite.
+    torch.manual_seed(12)
+    X = torch.randn(2, 16, 8, dtype=torch.float32, device=cuda, requires_grad=True)
+    c = T.SoftDTW(gamma=0.1)(X, X.detach())
+    c.sum().backward()
+    assert torch.isfinite(c).all() and torch.isfinite(X.grad).all()

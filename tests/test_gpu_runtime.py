@@ -1,0 +1,152 @@
+"""GPU: the runtime properties of the ops — torch.compile, CUDA-graph capture/replay, determinism,
+concurrent streams, the C ABI called directly, and failure detection without a GPU fault:
+
+* a wait that runs out: the failure-path hook makes one strip finish without publishing its progress;
+  the next strip's bounded wait expires, the launch aborts, the host reads SDTW_ERR_TIMEOUT, and the
+  context stays usable (a normal launch right after is correct);
+* lengths outside [0, N]: NaN cost and SDTW_ERR_BAD_LENGTH, no out-of-range access.
+"""
+
+import ctypes
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle as O
+import torchsoftdtw_b200 as T
+from torchsoftdtw_b200 import _ext
+
+pytestmark = pytest.mark.gpu
+
+
+def test_torch_compile_matches_eager(cuda):
+    torch.manual_seed(0)
+    X = torch.randn(4, 30, 8, device=cuda)
+    Y = torch.randn(4, 25, 8, device=cuda)
+    D = torch.rand(4, 30, 25, device=cuda)
+    m = T.SoftDTW(gamma=0.5, bandwidth=4, normalize=True)
+
+    def f(x, y, d):
+        return m(x, y).sum() + T.soft_dtw(d, gamma=0.3).sum()
+
+    eager = f(X, Y, D)
+    compiled = torch.compile(f)(X, Y, D)
+    torch.testing.assert_close(compiled, eager, rtol=1e-6, atol=1e-6)
+
+
+def test_cuda_graph_capture_and_replay(cuda):
+    torch.manual_seed(1)
+    D = torch.rand(8, 100, 90, device=cuda)
+    lx = torch.full((8,), 100, device=cuda, dtype=torch.long)
+    ly = torch.full((8,), 90, device=cuda, dtype=torch.long)
+    costs, R = torch.ops.torchsoftdtw.forward(D, lx, ly, 0.5, 7)  # warm-up outside capture
+    E = torch.ops.torchsoftdtw.backward(D, R, lx, ly, 0.5, 7)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        with torch.cuda.graph(g):
+            gc, gR = torch.ops.torchsoftdtw.forward(D, lx, ly, 0.5, 7)
+            gE = torch.ops.torchsoftdtw.backward(D, gR, lx, ly, 0.5, 7)
+    torch.cuda.current_stream().wait_stream(s)
+    for trial in range(3):
+        D.copy_(torch.rand(8, 100, 90, device=cuda))
+        g.replay()
+        torch.cuda.synchronize()
+        c_ref, R_ref = torch.ops.torchsoftdtw.forward(D, lx, ly, 0.5, 7)
+        E_ref = torch.ops.torchsoftdtw.backward(D, R_ref, lx, ly, 0.5, 7)
+        assert torch.equal(gc, c_ref) and torch.equal(gE, E_ref)
+    del g
+
+
+def test_deterministic(cuda):
+    torch.manual_seed(2)
+    X = torch.randn(16, 200, 16, device=cuda, requires_grad=True)
+    Y = torch.randn(16, 180, 16, device=cuda)
+    outs = []
+    for _ in range(2):
+        X.grad = None
+        c = T.SoftDTW(gamma=0.1)(X, Y)
+        c.sum().backward()
+        outs.append((c.detach().clone(), X.grad.clone()))
+    assert torch.equal(outs[0][0], outs[1][0]) and torch.equal(outs[0][1], outs[1][1])
+
+
+def test_concurrent_streams(cuda):
+    torch.manual_seed(3)
+    Ds = [torch.rand(4, 70 + 10 * k, 64, device=cuda, dtype=torch.float64) for k in range(4)]
+    streams = [torch.cuda.Stream() for _ in Ds]
+    outs = [None] * len(Ds)
+    torch.cuda.synchronize()
+    for k, (D, s) in enumerate(zip(Ds, streams)):
+        with torch.cuda.stream(s):
+            outs[k] = T.soft_dtw(D, gamma=0.2)
+    torch.cuda.synchronize()
+    for D, c in zip(Ds, outs):
+        ref, _ = O.forward(D.cpu().numpy(), None, None, 0.2, -1)
+        np.testing.assert_allclose(c.cpu().numpy(), ref, rtol=1e-10, atol=1e-12)
+
+
+def test_c_abi_direct_call(cuda):
+    """The C ABI used without torch's op layer: plain device pointers, a caller-owned workspace."""
+    lib = _ext.capi()
+    torch.manual_seed(4)
+    B, N, M = 3, 50, 41
+    D = torch.rand(B, N, M, device=cuda, dtype=torch.float64)
+    lx = torch.tensor([50, 44, 3], device=cuda, dtype=torch.int32)
+    ly = torch.tensor([41, 41, 40], device=cuda, dtype=torch.int32)
+    R = torch.empty(B, N + 2, M + 2, device=cuda, dtype=torch.float64)
+    costs = torch.empty(B, device=cuda, dtype=torch.float64)
+    E = torch.empty(B, N, M, device=cuda, dtype=torch.float64)
+    err = torch.zeros(1, device=cuda, dtype=torch.int32)
+    wsf = lib.sdtw_forward_workspace_bytes(B, N, M, 1)
+    wsb = lib.sdtw_backward_workspace_bytes(B, N, M, 1)
+    ws = torch.empty(max(wsf, wsb), device=cuda, dtype=torch.uint8)
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    p = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+    st = lib.sdtw_forward(1, p(D), B, N, M, p(lx), p(ly), 1, 0.4, 3, p(R), p(costs), p(ws), wsf, p(err), stream)
+    assert st == 0, lib.sdtw_status_string(st)
+    st = lib.sdtw_backward(1, p(D), p(R), B, N, M, p(lx), p(ly), 1, 0.4, 3, p(E), p(ws), wsb, p(err), stream)
+    assert st == 0, lib.sdtw_status_string(st)
+    assert lib.sdtw_read_error_word(p(err), stream) == 0
+    cr, Rr = O.forward(D.cpu().numpy(), [50, 44, 3], [41, 41, 40], 0.4, 3)
+    Er = O.backward(D.cpu().numpy(), Rr, [50, 44, 3], [41, 41, 40], 0.4, 3)
+    np.testing.assert_allclose(costs.cpu().numpy(), cr, rtol=1e-10)
+    np.testing.assert_allclose(E.cpu().numpy(), Er, rtol=1e-10, atol=1e-12)
+
+
+def test_wait_timeout_is_reported_and_context_survives(cuda):
+    lib = _ext.capi()
+    torch.manual_seed(5)
+    D = torch.rand(2, 64, 64, device=cuda)  # 2 strips per pair: strip 1 waits on strip 0
+    lx = torch.full((2,), 64, device=cuda, dtype=torch.long)
+    ly = torch.full((2,), 64, device=cuda, dtype=torch.long)
+    T.check_errors(cuda)
+    lib.sdtw_set_wait_timeout(0.2)
+    lib.sdtw_debug_inject_stall(0)  # ticket 0 = strip 0 of pair 0 never publishes
+    try:
+        torch.ops.torchsoftdtw.forward(D, lx, ly, 1.0, -1)
+        torch.cuda.synchronize()
+        with pytest.raises(RuntimeError, match="timed out"):
+            T.check_errors(cuda)
+    finally:
+        lib.sdtw_debug_inject_stall(-1)
+        lib.sdtw_set_wait_timeout(2.0)
+    costs = T.soft_dtw(D.double())
+    ref, _ = O.forward(D.double().cpu().numpy(), None, None, 1.0, -1)
+    np.testing.assert_allclose(costs.cpu().numpy(), ref, rtol=1e-10)
+    T.check_errors(cuda)
+
+
+def test_bad_lengths_give_nan_and_error_bit(cuda):
+    D = torch.rand(3, 10, 10, device=cuda, dtype=torch.float64)
+    lx = torch.tensor([10, 11, 5], device=cuda)
+    ly = torch.tensor([10, 10, -1], device=cuda)
+    costs, R = torch.ops.torchsoftdtw.forward(D, lx, ly, 1.0, -1)
+    c = costs.cpu().numpy()
+    assert np.isfinite(c[0]) and np.isnan(c[1]) and np.isnan(c[2])
+    with pytest.raises(RuntimeError, match="outside"):
+        T.check_errors(cuda)
+    T.check_errors(cuda)  # cleared

@@ -1,0 +1,112 @@
+"""In-tree build of the native parts of torchsoftdtw_b200.
+
+* ``lib/libsdtw_b200.so`` — the CUDA kernel library with the C ABI of ``include/sdtw_b200.h``,
+  compiled by nvcc for sm_100a only (``-gencode arch=compute_100a,code=sm_100a``), CUDA runtime linked
+  statically so the library carries the runtime its kernels were built with.
+* ``_C<ext>.so`` — the PyTorch operator layer (``csrc/torch_ops.cpp``), compiled by the host C++
+  compiler against libtorch and linked to ``lib/libsdtw_b200.so`` through ``$ORIGIN/lib``.
+
+Both are rebuilt only when a source is newer than the output. Run ``python -m torchsoftdtw_b200._build``.
+"""
+
+from __future__ import annotations
+
+import glob
+import os
+import shutil
+import subprocess
+import sys
+import sysconfig
+from concurrent.futures import ThreadPoolExecutor
+
+PKG = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(PKG)
+CSRC = os.path.join(PKG, "csrc")
+INCLUDE = os.path.join(ROOT, "include")
+LIBDIR = os.path.join(PKG, "lib")
+KERNEL_LIB = os.path.join(LIBDIR, "libsdtw_b200.so")
+OBJDIR = os.path.join(PKG, "_build")
+ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
+
+
+def _cuda_home() -> str:
+    home = os.environ.get("CUDA_HOME") or os.environ.get("CUDA_PATH")
+    if home and os.path.isdir(home):
+        return home
+    nvcc = shutil.which("nvcc")
+    if nvcc:
+        return os.path.dirname(os.path.dirname(os.path.realpath(nvcc)))
+    return "/usr/local/cuda"
+
+
+def ops_lib_path() -> str:
+    return os.path.join(PKG, "_C" + (sysconfig.get_config_var("EXT_SUFFIX") or ".so"))
+
+
+def _stale(out: str, deps: list[str]) -> bool:
+    if not os.path.exists(out):
+        return True
+    t = os.path.getmtime(out)
+    return any(os.path.getmtime(d) > t for d in deps)
+
+
+def _run(cmd: list[str]) -> None:
+    print("[torchsoftdtw_b200 build]", " ".join(cmd), flush=True)
+    subprocess.run(cmd, check=True)
+
+
+def build_kernels(force: bool = False) -> str:
+    """nvcc: csrc/*.cu -> lib/libsdtw_b200.so (sm_100a)."""
+    os.makedirs(LIBDIR, exist_ok=True)
+    os.makedirs(OBJDIR, exist_ok=True)
+    nvcc = os.path.join(_cuda_home(), "bin", "nvcc")
+    sources = sorted(glob.glob(os.path.join(CSRC, "*.cu")))
+    headers = sorted(glob.glob(os.path.join(CSRC, "*.cuh"))) + [os.path.join(INCLUDE, "sdtw_b200.h")]
+    objs = []
+    jobs = []
+    for src in sources:
+        obj = os.path.join(OBJDIR, os.path.basename(src) + ".o")
+        objs.append(obj)
+        if force or _stale(obj, [src] + headers):
+            jobs.append([nvcc, *ARCH_FLAGS, "-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC",
+                         "-I" + INCLUDE, "-I" + CSRC, "-c", src, "-o", obj])
+    if jobs:
+        with ThreadPoolExecutor(max_workers=len(jobs)) as ex:
+            list(ex.map(_run, jobs))
+    if force or _stale(KERNEL_LIB, objs):
+        _run([nvcc, *ARCH_FLAGS, "-shared", "-cudart", "static", "-o", KERNEL_LIB, *objs])
+    return KERNEL_LIB
+
+
+def build_ops(force: bool = False) -> str:
+    """g++: csrc/torch_ops.cpp -> _C.so, linked to lib/libsdtw_b200.so."""
+    import torch
+    from torch.utils import cpp_extension
+
+    out = ops_lib_path()
+    src = os.path.join(CSRC, "torch_ops.cpp")
+    deps = [src, os.path.join(INCLUDE, "sdtw_b200.h"), KERNEL_LIB]
+    if not (force or _stale(out, deps)):
+        return out
+    torch_dir = os.path.dirname(torch.__file__)
+    cuda_inc = os.path.join(_cuda_home(), "include")
+    abi = int(torch._C._GLIBCXX_USE_CXX11_ABI)
+    cxx = os.environ.get("CXX", "g++")
+    cmd = [cxx, "-O2", "-fPIC", "-shared", "-std=c++17", f"-D_GLIBCXX_USE_CXX11_ABI={abi}",
+           "-DTORCH_EXTENSION_NAME=_C", "-I" + INCLUDE, "-I" + cuda_inc]
+    for inc in cpp_extension.include_paths():
+        cmd.append("-I" + inc)
+    cmd += [src, "-o", out, "-L" + LIBDIR, "-lsdtw_b200", "-Wl,-rpath,$ORIGIN/lib",
+            "-L" + os.path.join(torch_dir, "lib"), "-lc10", "-lc10_cuda", "-ltorch", "-ltorch_cpu", "-ltorch_cuda",
+            "-Wl,-rpath," + os.path.join(torch_dir, "lib")]
+    _run(cmd)
+    return out
+
+
+def build(force: bool = False) -> None:
+    build_kernels(force)
+    build_ops(force)
+
+
+if __name__ == "__main__":
+    build(force="--force" in sys.argv)

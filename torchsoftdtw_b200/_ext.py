@@ -1,0 +1,80 @@
+"""Loader of the native libraries.
+
+* ``_C`` (the PyTorch operator layer) is loaded with ``torch.ops.load_library``; it registers
+  ``torch.ops.torchsoftdtw.forward/backward`` (the reference's schemas) and
+  ``torch.ops.torchsoftdtw_b200.*`` (the fused squared-L2 module path).
+* ``lib/libsdtw_b200.so`` (the CUDA kernels) is reachable directly through ctypes with :func:`capi`,
+  which declares every entry point of ``include/sdtw_b200.h``.
+
+There is no fallback: importing the package fails loudly when the libraries are not built.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+
+import torch
+
+from . import _build
+
+_loaded = False
+_capi = None
+
+
+def load() -> None:
+    global _loaded
+    if _loaded:
+        return
+    missing = [p for p in (_build.KERNEL_LIB, _build.ops_lib_path()) if not os.path.exists(p)]
+    if missing:
+        raise ImportError(
+            "torchsoftdtw_b200: native libraries are not built (missing: "
+            + ", ".join(missing)
+            + "). Build them with `python -m torchsoftdtw_b200._build` (needs nvcc for sm_100a)."
+        )
+    torch.ops.load_library(_build.ops_lib_path())
+    _loaded = True
+
+
+def library_paths() -> list[str]:
+    """The native libraries this package loads (kernel library first)."""
+    return [_build.KERNEL_LIB, _build.ops_lib_path()]
+
+
+# Exported C-ABI symbols and their ctypes signatures (include/sdtw_b200.h).
+_i64 = ctypes.c_int64
+_p = ctypes.c_void_p
+_i = ctypes.c_int
+_d = ctypes.c_double
+_sz = ctypes.c_size_t
+SIGNATURES: dict[str, tuple] = {
+    "sdtw_status_string": (ctypes.c_char_p, [_i]),
+    "sdtw_band_row_range": (None, [_i64, _i64, _i64, _i64, ctypes.POINTER(_i64), ctypes.POINTER(_i64)]),
+    "sdtw_pair_cells": (_i64, [_i64, _i64, _i64]),
+    "sdtw_read_error_word": (ctypes.c_uint32, [_p, _p]),
+    "sdtw_set_wait_timeout": (None, [_d]),
+    "sdtw_forward_workspace_bytes": (_sz, [_i64, _i64, _i64, _i]),
+    "sdtw_forward": (_i, [_i, _p, _i64, _i64, _i64, _p, _p, _i, _d, _i64, _p, _p, _p, _sz, _p, _p]),
+    "sdtw_backward_workspace_bytes": (_sz, [_i64, _i64, _i64, _i]),
+    "sdtw_backward": (_i, [_i, _p, _p, _i64, _i64, _i64, _p, _p, _i, _d, _i64, _p, _p, _sz, _p, _p]),
+    "sdtw_pairwise_l2": (_i, [_i, _p, _p, _i64, _i64, _i64, _i64, _p, _p]),
+    "sdtw_grad_l2": (_i, [_i, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _p, _p, _p]),
+}
+# Test hook of the failure path (declared in the .cu, not part of the public header).
+DEBUG_SIGNATURES: dict[str, tuple] = {"sdtw_debug_inject_stall": (None, [_i])}
+
+
+def capi() -> ctypes.CDLL:
+    """ctypes handle of lib/libsdtw_b200.so with every C-ABI signature declared."""
+    global _capi
+    if _capi is None:
+        if not os.path.exists(_build.KERNEL_LIB):
+            raise ImportError(f"torchsoftdtw_b200: {_build.KERNEL_LIB} is not built")
+        lib = ctypes.CDLL(_build.KERNEL_LIB)
+        for name, (res, args) in {**SIGNATURES, **DEBUG_SIGNATURES}.items():
+            fn = getattr(lib, name)
+            fn.restype = res
+            fn.argtypes = args
+        _capi = lib
+    return _capi

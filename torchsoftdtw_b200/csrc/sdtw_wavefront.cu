@@ -1,0 +1,812 @@
+// Soft-DTW forward / backward wavefront kernels for sm_100a, behind the C ABI of include/sdtw_b200.h.
+//
+// Work decomposition (both directions)
+//   * A pair's (nx, ny) DP grid is cut into strips of 32 rows. One warp owns one strip: lane l owns row
+//     r0 + l and processes column (tau - l) at step tau, so every warp step is one anti-diagonal and
+//     neighbouring rows exchange values with one warp shuffle per step; no block-wide barrier exists.
+//   * Strips are claimed from a global ticket counter in dependency order (forward: strip 0 of every
+//     pair, then strip 1, ...; backward: the last strip first). A strip only ever waits on the strip
+//     claimed just before it in the same pair, which was claimed earlier by a running warp, so the
+//     persistent grid cannot deadlock, whatever its size.
+//   * The boundary row between strips goes through global memory (L2): the forward reads the row
+//     above from R itself; the backward reads the contributions pushed up from the row below from a
+//     workspace buffer. Progress flags are published per 32-column block with release/acquire, and
+//     every wait is bounded in time (the launch aborts with SDTW_ERR_TIMEOUT instead of hanging).
+//   * Per warp, a shared-memory ring of 4 chunks x 32 columns holds the operands of the swept rows
+//     (forward: D, overwritten in place by R; backward: R, overwritten in place by E); chunks are
+//     prefetched two blocks ahead with cp.async and written back with coalesced row stores.
+//   * Only in-band columns of each strip are swept (the Sakoe-Chiba band and the lengths clip every
+//     row to an interval), so out-of-band cells cost nothing beyond the 32-step skew of a strip.
+//
+// Arithmetic
+//   Forward:  R[i,j] = D[i,j] + m - gamma*ln(1 + e^{-(x-m)/gamma} + e^{-(y-m)/gamma}),
+//             m <= x <= y the three predecessors sorted: two exp2 + one log2 per cell.
+//   Backward: scatter form. When E[s] is final, cell s pushes E[s] * w_p to each predecessor p, where
+//             w_p = e^{-(R_p - m_s)/gamma} / sum_q e^{-(R_q - m_s)/gamma} is the softmin weight of p in
+//             the forward of s. These are the reference's exp((R[s]-R[p]-D[s])/gamma) weights
+//             (softdtw.cpp:249-257) written without the cancellation R[s]-D[s]: three exp2 and one
+//             reciprocal per cell, and no read of D.
+#include <algorithm>
+#include <cmath>
+#include <mutex>
+
+#include "sdtw_common.cuh"
+#include "sdtw_b200.h"
+
+namespace sdtw {
+
+// Lengths arrive as int64 or int32 device arrays (the reference converts int32 to int64 on the host,
+// softdtw.cpp:67-70; here the kernel reads either directly).
+struct Lengths {
+    const void* px;
+    const void* py;
+    int is32;
+    __device__ __forceinline__ int64_t x(int64_t b) const
+    {
+        return is32 ? static_cast<int64_t>(static_cast<const int*>(px)[b]) : static_cast<const int64_t*>(px)[b];
+    }
+    __device__ __forceinline__ int64_t y(int64_t b) const
+    {
+        return is32 ? static_cast<int64_t>(static_cast<const int*>(py)[b]) : static_cast<const int64_t*>(py)[b];
+    }
+};
+
+// Per-lane geometry of one strip.
+struct Strip {
+    int64_t nx, ny;
+    int r0, rows;          // first row, number of valid rows (<= 32)
+    int lo, hi;            // this lane's in-band columns [lo, hi] (empty for lanes >= rows)
+    int c_begin, c_end;    // union over the strip's rows
+    int A, Z;              // this lane is valid at step tau iff A <= tau <= Z
+    int Amax, Zmin;        // every lane is valid for tau in [Amax, Zmin]
+    bool bad;
+};
+
+__device__ __forceinline__ int warp_max(int v)
+{
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = max(v, __shfl_xor_sync(kFull, v, o));
+    return v;
+}
+__device__ __forceinline__ int warp_min(int v)
+{
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = min(v, __shfl_xor_sync(kFull, v, o));
+    return v;
+}
+
+// Returns false if the strip has no cells (empty pair, or r0 beyond the pair's length).
+__device__ __forceinline__ bool make_strip(Strip& st, const Lengths& len, int64_t b, int s, int64_t N, int64_t M,
+                                           int64_t bw, int lane)
+{
+    st.nx = len.x(b);
+    st.ny = len.y(b);
+    st.bad = st.nx < 0 || st.nx > N || st.ny < 0 || st.ny > M;
+    if (st.bad) st.nx = st.ny = 0;
+    st.r0 = 32 * s;
+    if (st.nx == 0 || st.ny == 0 || st.r0 >= st.nx) return false;
+    st.rows = static_cast<int>(st.nx - st.r0 < 32 ? st.nx - st.r0 : 32);
+    int64_t lo = 1, hi = 0;
+    if (lane < st.rows) band_row_range(st.r0 + lane, st.nx, st.ny, bw, lo, hi);
+    st.lo = static_cast<int>(lo);
+    st.hi = static_cast<int>(hi);
+    st.c_begin = __shfl_sync(kFull, st.lo, 0);
+    st.c_end = __shfl_sync(kFull, st.hi, st.rows - 1);
+    st.A = lane < st.rows ? st.lo + lane : (1 << 30);
+    st.Z = lane < st.rows ? st.hi + lane : -(1 << 30);
+    st.Amax = warp_max(st.A);
+    st.Zmin = warp_min(st.Z);
+    return true;
+}
+
+// ==================================================================================================
+// Forward
+// ==================================================================================================
+template <typename T>
+struct FwdArgs {
+    const T* D;
+    T* R;
+    T* costs;
+    Lengths len;
+    int* flags;   // (B, S) progress of each strip: columns < value of its last row are final
+    int* ticket;  // strip ticket counter
+    int64_t B, N, M, bw;
+    int S;
+    T k;   // log2(e) / gamma
+    T gl;  // gamma * ln(2)
+    Sync sy;
+    int inject_skip;  // ticket whose strip never publishes progress (failure-detection test); -1 = none
+    int vec;          // D rows are 16-byte aligned: 16-byte cp.async
+};
+
+template <typename T>
+__device__ __forceinline__ T fwd_cell(T d, T diag, T up, T left, T k, T gl)
+{
+    const T a = Num<T>::mn(up, left);
+    const T y = Num<T>::mx(up, left);
+    const T m = Num<T>::mn(a, diag);
+    const T x = Num<T>::mx(a, diag);
+    // m is +inf only when all three predecessors are: the exponents then stay -inf and R = D + inf.
+    const T mc = Num<T>::mn(m, Num<T>::big());
+    const T e1 = Num<T>::exp2_((mc - x) * k);
+    const T e2 = Num<T>::exp2_((mc - y) * k);
+    const T sum = (T(1) + e1) + e2;
+    return fma(-gl, Num<T>::log2_(sum), m) + d;
+}
+
+// 32 forward steps tau = tau0 .. tau0+31 of one warp.
+template <typename T, bool MASKED>
+__device__ __forceinline__ void fwd_block(T* myrow, const T* top, int tau0, int lane, int A, int Z, T k, T gl,
+                                          T& outp, T& upp)
+{
+    const T INF = Num<T>::inf();
+    const int src = (lane + 31) & 31;
+    const bool lane0 = lane == 0;
+    const int base = tau0 - lane;
+    const T* topb = top + (tau0 & kSideMask);
+#pragma unroll
+    for (int u = 0; u < 32; ++u) {
+        T* cell = myrow + ((base + u) & kRingMask);
+        const T d = *cell;
+        const T upw = __shfl_sync(kFull, outp, src);
+        const T tv = topb[u];
+        const T up = lane0 ? tv : upw;
+        T r = fwd_cell<T>(d, upp, up, outp, k, gl);
+        if (MASKED) {
+            const int tau = tau0 + u;
+            r = (tau >= A && tau <= Z) ? r : INF;
+        }
+        *cell = r;
+        upp = up;
+        outp = r;
+    }
+}
+
+// D chunk kk (columns [32kk, 32kk+32) of the strip's rows) -> ring, asynchronously.
+template <typename T>
+__device__ __forceinline__ void fwd_load_chunk(const FwdArgs<T>& a, const T* Db, T* ring, int kk, int rows, int lane)
+{
+    const int64_t M = a.M;
+    const int col0 = 32 * kk;
+    if (a.vec) {
+        constexpr int EPP = 16 / sizeof(T);  // elements per 16-byte piece
+        constexpr int PPR = 32 / EPP;        // pieces per row of a chunk
+#pragma unroll 4
+        for (int p = lane; p < 32 * PPR; p += 32) {
+            const int r = p / PPR;
+            if (r >= rows) break;
+            const int col = col0 + (p % PPR) * EPP;
+            const int64_t left = (M - col) * static_cast<int64_t>(sizeof(T));
+            const int bytes = left >= 16 ? 16 : (left > 0 ? static_cast<int>(left) : 0);
+            const T* src = Db + static_cast<int64_t>(r) * M + (bytes > 0 ? col : 0);
+            cp_async_16(ring + r * kRing + (col & kRingMask), src, bytes);
+        }
+    } else {
+        const int col = col0 + lane;
+        const bool in = col < M;
+        for (int r = 0; r < rows; ++r) {
+            const T* src = Db + static_cast<int64_t>(r) * M + (in ? col : 0);
+            cp_async_scalar<sizeof(T)>(ring + r * kRing + (col & kRingMask), src, in ? static_cast<int>(sizeof(T)) : 0);
+        }
+    }
+}
+
+// Completed R chunk kk -> global R (padded layout), columns clipped to the swept range.
+template <typename T>
+__device__ __forceinline__ void fwd_store_chunk(const FwdArgs<T>& a, T* Rb, const T* ring, int kk, const Strip& st,
+                                                int lane)
+{
+    const int col = 32 * kk + lane;
+    if (col < st.c_begin || col > st.c_end) return;
+    const int64_t pitch = a.M + 2;
+    T* dst = Rb + static_cast<int64_t>(st.r0 + 1) * pitch + col + 1;
+    const T* srcp = ring + (col & kRingMask);
+    for (int r = 0; r < st.rows; ++r) dst[r * pitch] = srcp[r * kRing];
+}
+
+template <typename T>
+__device__ void fwd_strip(const FwdArgs<T>& a, T* ring, T* top, int64_t b, int s, int lane, bool skip_publish)
+{
+    const T INF = Num<T>::inf();
+    int* my_flag = a.flags + b * a.S + s;
+    Strip st;
+    if (!make_strip(st, a.len, b, s, a.N, a.M, a.bw, lane)) {
+        if (s == 0 && lane == 0) {
+            if (st.bad) {
+                atomicOr(a.sy.err, kErrBadLength);
+                a.costs[b] = Num<T>::nan();
+            } else {
+                a.costs[b] = (st.nx == 0 && st.ny == 0) ? T(0) : INF;
+            }
+        }
+        if (!skip_publish) publish(my_flag, kDone, lane);
+        return;
+    }
+    const int64_t pitch = a.M + 2;
+    const T* Db = a.D + (b * a.N + st.r0) * a.M;
+    T* Rb = a.R + b * (a.N + 2) * pitch;
+    const int k0 = st.c_begin >> 5;
+    const int k1 = (st.c_end + 31) >> 5;
+    const int kc = st.c_end >> 5;
+    const bool has_consumer = st.rows == 32 && st.r0 + 32 < st.nx;
+    int plo = 0, phi = -1;  // in-band columns of the row above (row r0-1)
+    if (s > 0) {
+        int64_t l64, h64;
+        band_row_range(st.r0 - 1, st.nx, st.ny, a.bw, l64, h64);
+        plo = static_cast<int>(l64);
+        phi = static_cast<int>(h64);
+    }
+    const T* above = Rb + static_cast<int64_t>(st.r0) * pitch + 1;  // padded row r0 == row r0-1, column 0
+
+#pragma unroll 1
+    for (int q = 0; q < 3; ++q) {
+        if (k0 + q <= kc) fwd_load_chunk<T>(a, Db, ring, k0 + q, st.rows, lane);
+        cp_async_commit();
+    }
+
+    T outp = INF;
+    T upp = (s == 0 && lane == 0) ? T(0) : INF;
+    T* myrow = ring + lane * kRing;
+
+#pragma unroll 1
+    for (int blk = k0; blk <= k1; ++blk) {
+        const int tau0 = 32 * blk;
+        // Row above, columns [tau0, tau0+31], for lane 0.
+        if (s > 0) {
+            if (!wait_progress(my_flag - 1, tau0 + 32, a.sy, lane)) return;
+            const int c = tau0 + lane;
+            T v = INF;
+            if (c >= plo && c <= phi) v = __ldcg(above + c);
+            top[c & kSideMask] = v;
+            if (blk == k0) {
+                T vd = INF;
+                if (tau0 - 1 >= plo && tau0 - 1 <= phi) vd = __ldcg(above + tau0 - 1);
+                if (lane == 0) upp = vd;
+            }
+        } else {
+            top[(tau0 + lane) & kSideMask] = INF;
+        }
+        cp_async_wait<2>();
+        __syncwarp();
+        if (tau0 >= st.Amax && tau0 + 31 <= st.Zmin)
+            fwd_block<T, false>(myrow, top, tau0, lane, st.A, st.Z, a.k, a.gl, outp, upp);
+        else
+            fwd_block<T, true>(myrow, top, tau0, lane, st.A, st.Z, a.k, a.gl, outp, upp);
+        __syncwarp();
+        if (has_consumer) {
+            // Bottom row (lane 31) finished columns [tau0-31, tau0] in this block.
+            const int c = tau0 - 31 + lane;
+            if (c >= st.c_begin && c <= st.c_end)
+                Rb[static_cast<int64_t>(st.r0 + 32) * pitch + c + 1] = ring[31 * kRing + (c & kRingMask)];
+            if (!skip_publish) publish(my_flag, tau0 + 1, lane);
+        }
+        if (blk - 1 >= k0) fwd_store_chunk<T>(a, Rb, ring, blk - 1, st, lane);
+        __syncwarp();
+        if (blk + 3 <= kc) fwd_load_chunk<T>(a, Db, ring, blk + 3, st.rows, lane);
+        cp_async_commit();
+    }
+    cp_async_wait<0>();
+    __syncwarp();
+    if (kc == k1) fwd_store_chunk<T>(a, Rb, ring, kc, st, lane);
+    if (st.nx - 1 - st.r0 == lane) a.costs[b] = ring[lane * kRing + ((st.ny - 1) & kRingMask)];
+    __syncwarp();
+    if (!skip_publish) publish(my_flag, kDone, lane);
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kWarpsPerCta * 32) sdtw_fwd_kernel(FwdArgs<T> a)
+{
+    extern __shared__ __align__(16) unsigned char smem[];
+    const int lane = threadIdx.x & 31;
+    const int warp = threadIdx.x >> 5;
+    T* ring = reinterpret_cast<T*>(smem) + static_cast<size_t>(warp) * (32 * kRing + kSide);
+    T* top = ring + 32 * kRing;
+    for (int e = lane; e < 32 * kRing + kSide; e += 32) ring[e] = T(0);
+    __syncwarp();
+    const int64_t total = a.B * a.S;
+    while (true) {
+        int tk = 0;
+        if (lane == 0) tk = aborted(a.sy) ? static_cast<int>(total) : atomicAdd(a.ticket, 1);
+        tk = __shfl_sync(kFull, tk, 0);
+        if (tk >= total) break;
+        const int s = static_cast<int>(tk / a.B);
+        const int64_t b = tk % a.B;
+        fwd_strip<T>(a, ring, top, b, s, lane, tk == a.inject_skip);
+    }
+}
+
+// R <- +inf everywhere, R[:, 0, 0] <- 0 (softdtw.cpp:114-121).
+template <typename T>
+__global__ void sdtw_fill_r_kernel(T* R, int64_t total, int64_t slab)
+{
+    const T INF = Num<T>::inf();
+    for (int64_t e = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; e < total;
+         e += static_cast<int64_t>(gridDim.x) * blockDim.x)
+        R[e] = (e % slab == 0) ? T(0) : INF;
+}
+
+// ==================================================================================================
+// Backward
+// ==================================================================================================
+template <typename T>
+struct BwdArgs {
+    const T* R;
+    T* E;
+    T* bnd;  // (B, S, M): contributions pushed from the first row of strip s+1 into the last row of strip s
+    Lengths len;
+    int* flags;
+    int* ticket;
+    int64_t B, N, M, bw;
+    int S;
+    int Mpad;  // progress = Mpad - (lowest final boundary column)
+    T k;
+    Sync sy;
+    int inject_skip;
+};
+
+template <typename T, bool MASKED>
+__device__ __forceinline__ void bwd_block(T* rowA, T* rowB, const T* bndring, T* sendring, int tau0, int lane, int A,
+                                          int Z, T k, T seed, T& upc, T& sendv, T& pend, T& acc)
+{
+    const T big = Num<T>::big();
+    const int src = (lane + 1) & 31;
+    const bool lane31 = lane == 31;
+    const bool lane0 = lane == 0;
+    const int base = tau0 - lane;
+    // Boundary values of lane 31's column c live at (c + 31) & 63, so a block reads them without wrapping.
+    const T* bndb = bndring + (tau0 & kSideMask);
+#pragma unroll
+    for (int u = 31; u >= 0; --u) {
+        const int c = base + u;
+        const int cm = (c - 1) & kRingMask;
+        const T rd = rowA[cm];  // R[i-1][c-1]
+        const T rl = rowB[cm];  // R[i][c-1]
+        const T ru = upc;       // R[i-1][c]
+        const T recvw = __shfl_sync(kFull, sendv, src);
+        const T bv = bndb[u];  // column tau0 + u - 31
+        const T recv = lane31 ? bv : recvw;
+        const T Es = acc + recv;
+        const T m = Num<T>::mn(Num<T>::mn(rd, ru), rl);
+        const T mc = Num<T>::mn(m, big);
+        const T ed = Num<T>::exp2_((mc - rd) * k);
+        const T eu = Num<T>::exp2_((mc - ru) * k);
+        const T el = Num<T>::exp2_((mc - rl) * k);
+        T q = Es * Num<T>::rcp_((ed + eu) + el);
+        T Eo = Es;
+        if (MASKED) {
+            const int tau = tau0 + u;
+            const bool valid = tau >= A && tau <= Z;
+            q = valid ? q : T(0);
+            acc = valid ? q * el : seed;
+            Eo = valid ? Es : T(0);
+        } else {
+            acc = q * el;
+        }
+        sendv = fma(q, eu, pend);
+        pend = q * ed;
+        rowB[c & kRingMask] = Eo;
+        if (lane0) sendring[c & kSideMask] = sendv;
+        upc = rd;
+    }
+}
+
+// R chunk kk (padded rows r0 .. r0+rows, D-columns [32kk, 32kk+32)) -> ring rows 0..rows.
+template <typename T>
+__device__ __forceinline__ void bwd_load_chunk(const BwdArgs<T>& a, const T* Rb, T* ring, int kk, int r0, int rows,
+                                               int lane)
+{
+    const int64_t pitch = a.M + 2;
+    const int c = 32 * kk + lane;  // D-column; padded column c+1 exists for -1 <= c <= M
+    const bool in = c >= -1 && c <= a.M;
+    const T* src = Rb + static_cast<int64_t>(r0) * pitch + (in ? c + 1 : 0);
+    T* dst = ring + (c & kRingMask);
+    for (int q = 0; q <= rows; ++q)
+        cp_async_scalar<sizeof(T)>(dst + q * kRing, src + q * pitch, in ? static_cast<int>(sizeof(T)) : 0);
+}
+
+template <typename T>
+__device__ __forceinline__ void bwd_store_chunk(const BwdArgs<T>& a, T* Eb, const T* ring, int kk, const Strip& st,
+                                                int lane)
+{
+    const int col = 32 * kk + lane;
+    if (col < st.c_begin || col > st.c_end) return;
+    T* dst = Eb + static_cast<int64_t>(st.r0) * a.M + col;
+    const T* srcp = ring + kRing + (col & kRingMask);
+    for (int r = 0; r < st.rows; ++r) dst[r * a.M] = srcp[r * kRing];
+}
+
+template <typename T>
+__device__ void bwd_strip(const BwdArgs<T>& a, T* ring, T* bndring, T* sendring, int64_t b, int s, int lane,
+                          bool skip_publish)
+{
+    int* my_flag = a.flags + b * a.S + s;
+    Strip st;
+    if (!make_strip(st, a.len, b, s, a.N, a.M, a.bw, lane)) {
+        if (st.bad && s == 0 && lane == 0) atomicOr(a.sy.err, kErrBadLength);
+        if (!skip_publish) publish(my_flag, kDone, lane);
+        return;
+    }
+    const int64_t pitch = a.M + 2;
+    const T* Rb = a.R + b * (a.N + 2) * pitch;
+    T* Eb = a.E + b * a.N * a.M;
+    const int k0 = st.c_begin >> 5;
+    const int k1 = (st.c_end + 31) >> 5;
+    const int kmin = (st.c_begin - 1) >> 5;  // arithmetic shift: -1 when c_begin == 0
+    const bool has_producer = st.r0 + 32 < st.nx;
+    const bool has_consumer = s > 0;
+    int plo = 0, phi = -1;  // in-band columns of the producer's first row (row r0+32)
+    if (has_producer) {
+        int64_t l64, h64;
+        band_row_range(st.r0 + 32, st.nx, st.ny, a.bw, l64, h64);
+        plo = static_cast<int>(l64);
+        phi = static_cast<int>(h64);
+    }
+    const T* bnd_in = a.bnd + (b * a.S + s) * a.M;
+    T* bnd_out = a.bnd + (b * a.S + (s - 1)) * a.M;
+    // Terminal cell (nx-1, ny-1): E = 1 (the reference's sentinel, softdtw.cpp:225-227). Masked steps of
+    // the terminal row leave `acc` = seed, so its first valid cell (column ny-1) starts from 1.
+    const T seed = (st.r0 + lane == st.nx - 1) ? T(1) : T(0);
+    const int hi0 = __shfl_sync(kFull, st.hi, 0);
+
+#pragma unroll 1
+    for (int q = 0; q < 4; ++q) {
+        if (k1 - q >= kmin) bwd_load_chunk<T>(a, Rb, ring, k1 - q, st.r0, st.rows, lane);
+        cp_async_commit();
+    }
+
+    T* rowA = ring + lane * kRing;
+    T* rowB = rowA + kRing;
+    T upc = T(0), sendv = T(0), pend = T(0), acc = seed;
+
+#pragma unroll 1
+    for (int blk = k1; blk >= k0; --blk) {
+        const int tau0 = 32 * blk;
+        // Contributions from the row below into lane 31's columns [tau0-31, tau0].
+        {
+            const int c = tau0 - 31 + lane;
+            T v = T(0);
+            if (has_producer) {
+                if (!wait_progress(my_flag + 1, a.Mpad - 32 * (blk - 1), a.sy, lane)) return;
+                if (c >= 0 && c >= plo - 1 && c <= phi) v = __ldcg(bnd_in + c);
+            }
+            bndring[(c + 31) & kSideMask] = v;
+        }
+        cp_async_wait<2>();
+        __syncwarp();
+        if (blk == k1) upc = rowA[(tau0 + 31 - lane) & kRingMask];
+        if (tau0 >= st.Amax && tau0 + 31 <= st.Zmin)
+            bwd_block<T, false>(rowA, rowB, bndring, sendring, tau0, lane, st.A, st.Z, a.k, seed, upc, sendv, pend,
+                                acc);
+        else
+            bwd_block<T, true>(rowA, rowB, bndring, sendring, tau0, lane, st.A, st.Z, a.k, seed, upc, sendv, pend,
+                               acc);
+        __syncwarp();
+        if (has_consumer) {
+            // Lane 0 finished its pushes into row r0-1 for columns [tau0, tau0+31].
+            const int c = tau0 + lane;
+            if (c >= 0 && c >= st.c_begin - 1 && c <= hi0) bnd_out[c] = sendring[c & kSideMask];
+            if (!skip_publish) publish(my_flag, a.Mpad - tau0, lane);
+        }
+        bwd_store_chunk<T>(a, Eb, ring, blk, st, lane);
+        __syncwarp();
+        if (blk - 4 >= kmin) bwd_load_chunk<T>(a, Rb, ring, blk - 4, st.r0, st.rows, lane);
+        cp_async_commit();
+    }
+    cp_async_wait<0>();
+    // When the sweep starts exactly at a chunk boundary, lane 0's last diagonal push (into column
+    // c_begin-1 of the row above) was never followed by another step: write it out now.
+    if (has_consumer && lane == 0 && st.c_begin == 32 * k0 && st.c_begin >= 1) bnd_out[st.c_begin - 1] = pend;
+    __syncwarp();
+    if (!skip_publish) publish(my_flag, kDone, lane);
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kWarpsPerCta * 32) sdtw_bwd_kernel(BwdArgs<T> a)
+{
+    extern __shared__ __align__(16) unsigned char smem[];
+    const int lane = threadIdx.x & 31;
+    const int warp = threadIdx.x >> 5;
+    constexpr int per_warp = 33 * kRing + 2 * kSide;
+    T* ring = reinterpret_cast<T*>(smem) + static_cast<size_t>(warp) * per_warp;
+    T* bndring = ring + 33 * kRing;
+    T* sendring = bndring + kSide;
+    for (int e = lane; e < per_warp; e += 32) ring[e] = T(0);
+    __syncwarp();
+    const int64_t total = a.B * a.S;
+    while (true) {
+        int tk = 0;
+        if (lane == 0) tk = aborted(a.sy) ? static_cast<int>(total) : atomicAdd(a.ticket, 1);
+        tk = __shfl_sync(kFull, tk, 0);
+        if (tk >= total) break;
+        const int s = a.S - 1 - static_cast<int>(tk / a.B);
+        const int64_t b = tk % a.B;
+        bwd_strip<T>(a, ring, bndring, sendring, b, s, lane, tk == a.inject_skip);
+    }
+}
+
+// ==================================================================================================
+// Host side
+// ==================================================================================================
+namespace {
+
+double g_timeout_s = 2.0;
+int g_inject_skip = -1;  // set only through sdtw_debug_inject_stall (tests of the failure path)
+
+struct DeviceInfo {
+    bool ready = false;
+    int sms = 0;
+    int occ_fwd[2] = {0, 0};
+    int occ_bwd[2] = {0, 0};
+};
+std::mutex g_mu;
+DeviceInfo g_dev[128];
+
+template <typename T>
+constexpr size_t fwd_smem_bytes()
+{
+    return static_cast<size_t>(kWarpsPerCta) * (32 * kRing + kSide) * sizeof(T);
+}
+template <typename T>
+constexpr size_t bwd_smem_bytes()
+{
+    return static_cast<size_t>(kWarpsPerCta) * (33 * kRing + 2 * kSide) * sizeof(T);
+}
+
+template <typename T>
+cudaError_t init_kernel_attrs(int& occ_f, int& occ_b)
+{
+    cudaError_t e = cudaFuncSetAttribute(sdtw_fwd_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(fwd_smem_bytes<T>()));
+    if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(sdtw_bwd_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(bwd_smem_bytes<T>()));
+    if (e != cudaSuccess) return e;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ_f, sdtw_fwd_kernel<T>, kWarpsPerCta * 32,
+                                                      fwd_smem_bytes<T>());
+    if (e != cudaSuccess) return e;
+    return cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ_b, sdtw_bwd_kernel<T>, kWarpsPerCta * 32,
+                                                         bwd_smem_bytes<T>());
+}
+
+cudaError_t device_info(const DeviceInfo*& out)
+{
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= 128) return cudaErrorInvalidDevice;
+    std::lock_guard<std::mutex> lock(g_mu);
+    DeviceInfo& di = g_dev[dev];
+    if (!di.ready) {
+        e = cudaDeviceGetAttribute(&di.sms, cudaDevAttrMultiProcessorCount, dev);
+        if (e != cudaSuccess) return e;
+        e = init_kernel_attrs<float>(di.occ_fwd[0], di.occ_bwd[0]);
+        if (e != cudaSuccess) return e;
+        e = init_kernel_attrs<double>(di.occ_fwd[1], di.occ_bwd[1]);
+        if (e != cudaSuccess) return e;
+        di.ready = true;
+    }
+    out = &di;
+    return cudaSuccess;
+}
+
+constexpr size_t kHeader = 256;  // ticket, abort word
+inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+inline int64_t strips_of(int64_t N) { return N > 0 ? (N + 31) / 32 : 1; }
+inline size_t flags_bytes(int64_t B, int64_t N) { return align_up(static_cast<size_t>(B * strips_of(N)) * 4, 256); }
+inline size_t elem_size(sdtw_dtype t) { return t == SDTW_F64 ? 8 : 4; }
+
+inline sdtw_status from_cuda(cudaError_t e) { return e == cudaSuccess ? SDTW_OK : static_cast<sdtw_status>(e); }
+
+// A bandwidth beyond N+M admits every cell, exactly like an unconstrained band; clamping keeps the
+// integer band arithmetic far from overflow.
+inline int64_t clamp_bw(int64_t bw, int64_t N, int64_t M) { return bw > N + M ? N + M : bw; }
+
+bool common_args_ok(int64_t B, int64_t N, int64_t M, double gamma)
+{
+    if (B < 0 || N < 0 || M < 0) return false;
+    if (!(gamma > 0.0) || !std::isfinite(gamma)) return false;
+    if (N > (1 << 29) || M > (1 << 29)) return false;
+    if (B * strips_of(N) >= (int64_t(1) << 31)) return false;
+    return true;
+}
+
+Sync make_sync(void* workspace, uint32_t* err_word)
+{
+    Sync sy;
+    sy.err = err_word;
+    sy.abort = reinterpret_cast<int*>(static_cast<char*>(workspace) + 4);
+    sy.timeout_ns = static_cast<uint64_t>(g_timeout_s * 1e9);
+    return sy;
+}
+
+template <typename T>
+sdtw_status launch_forward(const void* D, int64_t B, int64_t N, int64_t M, const void* lx, const void* ly, int is32,
+                           double gamma, int64_t bw, void* R, void* costs, void* ws, uint32_t* err,
+                           cudaStream_t stream)
+{
+    const DeviceInfo* di = nullptr;
+    cudaError_t e = device_info(di);
+    if (e != cudaSuccess) return from_cuda(e);
+    const int64_t S = strips_of(N);
+    e = cudaMemsetAsync(ws, 0, kHeader + flags_bytes(B, N), stream);
+    if (e != cudaSuccess) return from_cuda(e);
+    const int64_t slab = (N + 2) * (M + 2);
+    {
+        const int64_t total = B * slab;
+        const int threads = 256;
+        const int64_t want = (total + threads - 1) / threads;
+        const int blocks = static_cast<int>(std::min<int64_t>(want, int64_t(di->sms) * 16));
+        sdtw_fill_r_kernel<T><<<std::max(blocks, 1), threads, 0, stream>>>(static_cast<T*>(R), total, slab);
+    }
+    FwdArgs<T> a;
+    a.D = static_cast<const T*>(D);
+    a.R = static_cast<T*>(R);
+    a.costs = static_cast<T*>(costs);
+    a.len = Lengths{lx, ly, is32};
+    a.ticket = reinterpret_cast<int*>(ws);
+    a.flags = reinterpret_cast<int*>(static_cast<char*>(ws) + kHeader);
+    a.B = B;
+    a.N = N;
+    a.M = M;
+    a.bw = clamp_bw(bw, N, M);
+    a.S = static_cast<int>(S);
+    a.k = static_cast<T>(1.4426950408889634 / gamma);
+    a.gl = static_cast<T>(gamma * 0.6931471805599453);
+    a.sy = make_sync(ws, err);
+    a.inject_skip = g_inject_skip;
+    a.vec = (M % (16 / sizeof(T)) == 0) && (reinterpret_cast<uintptr_t>(D) % 16 == 0);
+    const int occ = di->occ_fwd[sizeof(T) == 8 ? 1 : 0];
+    const int64_t ctas_needed = (B * S + kWarpsPerCta - 1) / kWarpsPerCta;
+    const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(ctas_needed, int64_t(di->sms) * std::max(occ, 1))));
+    sdtw_fwd_kernel<T><<<grid, kWarpsPerCta * 32, fwd_smem_bytes<T>(), stream>>>(a);
+    return from_cuda(cudaGetLastError());
+}
+
+template <typename T>
+sdtw_status launch_backward(const void* R, int64_t B, int64_t N, int64_t M, const void* lx, const void* ly, int is32,
+                            double gamma, int64_t bw, void* E, void* ws, uint32_t* err, cudaStream_t stream)
+{
+    const DeviceInfo* di = nullptr;
+    cudaError_t e = device_info(di);
+    if (e != cudaSuccess) return from_cuda(e);
+    const int64_t S = strips_of(N);
+    e = cudaMemsetAsync(ws, 0, kHeader + flags_bytes(B, N), stream);
+    if (e != cudaSuccess) return from_cuda(e);
+    e = cudaMemsetAsync(E, 0, static_cast<size_t>(B * N * M) * sizeof(T), stream);
+    if (e != cudaSuccess) return from_cuda(e);
+    BwdArgs<T> a;
+    a.R = static_cast<const T*>(R);
+    a.E = static_cast<T*>(E);
+    a.bnd = reinterpret_cast<T*>(static_cast<char*>(ws) + kHeader + flags_bytes(B, N));
+    a.len = Lengths{lx, ly, is32};
+    a.ticket = reinterpret_cast<int*>(ws);
+    a.flags = reinterpret_cast<int*>(static_cast<char*>(ws) + kHeader);
+    a.B = B;
+    a.N = N;
+    a.M = M;
+    a.bw = clamp_bw(bw, N, M);
+    a.S = static_cast<int>(S);
+    a.Mpad = static_cast<int>(M + 64);
+    a.k = static_cast<T>(1.4426950408889634 / gamma);
+    a.sy = make_sync(ws, err);
+    a.inject_skip = g_inject_skip;
+    const int occ = di->occ_bwd[sizeof(T) == 8 ? 1 : 0];
+    const int64_t ctas_needed = (B * S + kWarpsPerCta - 1) / kWarpsPerCta;
+    const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(ctas_needed, int64_t(di->sms) * std::max(occ, 1))));
+    sdtw_bwd_kernel<T><<<grid, kWarpsPerCta * 32, bwd_smem_bytes<T>(), stream>>>(a);
+    return from_cuda(cudaGetLastError());
+}
+
+}  // namespace
+}  // namespace sdtw
+
+using namespace sdtw;
+
+extern "C" {
+
+const char* sdtw_status_string(sdtw_status status)
+{
+    switch (status) {
+        case SDTW_OK: return "ok";
+        case SDTW_EINVAL: return "invalid argument (size, pointer, gamma or bandwidth)";
+        case SDTW_EDTYPE: return "unsupported dtype (expected SDTW_F32 or SDTW_F64)";
+        case SDTW_EWORKSPACE: return "workspace missing or smaller than the *_workspace_bytes size";
+        case SDTW_EDEVICE: return "no usable sm_100 device";
+        default: break;
+    }
+    if (status > 0) return cudaGetErrorString(static_cast<cudaError_t>(status));
+    return "unknown status";
+}
+
+void sdtw_band_row_range(int64_t i, int64_t nx, int64_t ny, int64_t bandwidth, int64_t* lo, int64_t* hi)
+{
+    int64_t l, h;
+    band_row_range(i, nx, ny, clamp_bw(bandwidth, nx, ny), l, h);
+    *lo = l;
+    *hi = h;
+}
+
+int64_t sdtw_pair_cells(int64_t nx, int64_t ny, int64_t bandwidth)
+{
+    if (nx <= 0 || ny <= 0) return 0;
+    int64_t total = 0;
+    for (int64_t i = 0; i < nx; ++i) {
+        int64_t l, h;
+        band_row_range(i, nx, ny, clamp_bw(bandwidth, nx, ny), l, h);
+        if (h >= l) total += h - l + 1;
+    }
+    return total;
+}
+
+uint32_t sdtw_read_error_word(uint32_t* err_word, void* stream)
+{
+    uint32_t v = 0;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (cudaMemcpyAsync(&v, err_word, 4, cudaMemcpyDeviceToHost, s) != cudaSuccess) return 0xffffffffu;
+    if (cudaStreamSynchronize(s) != cudaSuccess) return 0xffffffffu;
+    if (v != 0 && cudaMemsetAsync(err_word, 0, 4, s) != cudaSuccess) return 0xffffffffu;
+    if (cudaStreamSynchronize(s) != cudaSuccess) return 0xffffffffu;
+    return v;
+}
+
+void sdtw_set_wait_timeout(double seconds)
+{
+    if (seconds > 0 && std::isfinite(seconds)) g_timeout_s = seconds;
+}
+
+/* Failure-path test hook (not in the public header's main API): the strip holding ticket `ticket` of
+ * every following launch completes its cells but never publishes its progress, so the strip after it
+ * runs into the bounded wait. -1 switches it off. */
+void sdtw_debug_inject_stall(int ticket) { g_inject_skip = ticket; }
+
+size_t sdtw_forward_workspace_bytes(int64_t B, int64_t N, int64_t M, sdtw_dtype dtype)
+{
+    (void)M;
+    (void)dtype;
+    if (B < 0 || N < 0) return 0;
+    return kHeader + flags_bytes(B, N);
+}
+
+size_t sdtw_backward_workspace_bytes(int64_t B, int64_t N, int64_t M, sdtw_dtype dtype)
+{
+    if (B < 0 || N < 0 || M < 0) return 0;
+    return kHeader + flags_bytes(B, N) + align_up(static_cast<size_t>(B * strips_of(N) * M) * elem_size(dtype), 256);
+}
+
+sdtw_status sdtw_forward(sdtw_dtype dtype, const void* D, int64_t B, int64_t N, int64_t M, const void* lengths_x,
+                         const void* lengths_y, int lengths_int32, double gamma, int64_t bandwidth, void* R,
+                         void* costs, void* workspace, size_t workspace_bytes, uint32_t* err_word, void* stream)
+{
+    if (dtype != SDTW_F32 && dtype != SDTW_F64) return SDTW_EDTYPE;
+    if (!common_args_ok(B, N, M, gamma)) return SDTW_EINVAL;
+    if (B == 0) return SDTW_OK;
+    if (!lengths_x || !lengths_y || !R || !costs || !err_word || (N * M > 0 && !D)) return SDTW_EINVAL;
+    if (!workspace || workspace_bytes < sdtw_forward_workspace_bytes(B, N, M, dtype)) return SDTW_EWORKSPACE;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (dtype == SDTW_F32)
+        return launch_forward<float>(D, B, N, M, lengths_x, lengths_y, lengths_int32, gamma, bandwidth, R, costs,
+                                     workspace, err_word, s);
+    return launch_forward<double>(D, B, N, M, lengths_x, lengths_y, lengths_int32, gamma, bandwidth, R, costs,
+                                  workspace, err_word, s);
+}
+
+sdtw_status sdtw_backward(sdtw_dtype dtype, const void* D, const void* R, int64_t B, int64_t N, int64_t M,
+                          const void* lengths_x, const void* lengths_y, int lengths_int32, double gamma,
+                          int64_t bandwidth, void* E, void* workspace, size_t workspace_bytes, uint32_t* err_word,
+                          void* stream)
+{
+    (void)D;
+    if (dtype != SDTW_F32 && dtype != SDTW_F64) return SDTW_EDTYPE;
+    if (!common_args_ok(B, N, M, gamma)) return SDTW_EINVAL;
+    if (B == 0 || N == 0 || M == 0) return SDTW_OK;
+    if (!lengths_x || !lengths_y || !R || !E || !err_word) return SDTW_EINVAL;
+    if (!workspace || workspace_bytes < sdtw_backward_workspace_bytes(B, N, M, dtype)) return SDTW_EWORKSPACE;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (dtype == SDTW_F32)
+        return launch_backward<float>(R, B, N, M, lengths_x, lengths_y, lengths_int32, gamma, bandwidth, E, workspace,
+                                      err_word, s);
+    return launch_backward<double>(R, B, N, M, lengths_x, lengths_y, lengths_int32, gamma, bandwidth, E, workspace,
+                                   err_word, s);
+}
+
+}  // extern "C"
