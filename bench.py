@@ -218,12 +218,20 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", default="medium", choices=sorted(WORKLOADS))
-    ap.add_argument("--cpu-sample", type=int, default=16, help="pairs per CPU-baseline step")
+    ap.add_argument("--cpu-sample", type=int, default=None,
+                    help="pairs per CPU-baseline step (default: one per host thread, at least 16)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--profile", action="store_true", help="small run for profilers: no extras, few steps")
+    ap.add_argument("--profile", action="store_true", help="run for profilers: no e2e, roofline or baseline")
+    ap.add_argument("--batch", type=int, default=None, help="pairs per GPU (default: the workload's B)")
     args = ap.parse_args()
     rank, world, local = dist_env()
     w = WORKLOADS[args.workload]
+    if args.cpu_sample is None:
+        args.cpu_sample = max(16, os.cpu_count() or 1)
+    if args.batch is not None:
+        import dataclasses
+
+        w = dataclasses.replace(w, B=args.batch)
 
     if args.impl == "reference":
         run_reference_arm(args, w, rank)
@@ -240,7 +248,7 @@ def main():
     import torchsoftdtw_b200 as T
     from torchsoftdtw_b200.workloads import count_cells
 
-    X, Y, lx, ly, _ = make_inputs(w.name, seed=rank)
+    X, Y, lx, ly, _ = make_inputs(w.name, seed=rank, batch=w.B)
     cells_rank = count_cells(lx, ly, w.bandwidth)
     Xd, Yd, lxd, lyd = X.to(dev), Y.to(dev), lx.to(dev), ly.to(dev)
     Xd.requires_grad_(True)
@@ -359,8 +367,8 @@ def main():
 #   forward  : read D + write R                      = 2
 #   backward : read R + write E                      = 2
 #   pairwise : write D (X, Y reads are O((N+M)d/NM)) = 1
-#   grad     : read E + read D (clamp mask)          = 2
-ALGO_BYTES = {"sdtw_forward": 2, "sdtw_backward": 2, "sdtw_pairwise_l2": 1, "sdtw_grad_l2": 2}
+#   grad     : read E (D only for pairs with a clamped cell) = 1
+ALGO_BYTES = {"sdtw_forward": 2, "sdtw_backward": 2, "sdtw_pairwise_l2": 1, "sdtw_grad_l2": 1}
 
 
 def kernel_times(T, X, Y, lx, ly, w, dev, flush, reps: int = 20):
@@ -379,6 +387,7 @@ def kernel_times(T, X, Y, lx, ly, w, dev, flush, reps: int = 20):
     E = torch.empty(B, N, M, device=dev, dtype=X.dtype)
     costs = torch.empty(B, device=dev, dtype=X.dtype)
     g = torch.ones(B, device=dev, dtype=X.dtype)
+    flags = torch.zeros(B, device=dev, dtype=torch.int32)
     gX = torch.empty_like(X)
     err = torch.zeros(1, device=dev, dtype=torch.int32)
     wsf = lib.sdtw_forward_workspace_bytes(B, N, M, code)
@@ -389,12 +398,13 @@ def kernel_times(T, X, Y, lx, ly, w, dev, flush, reps: int = 20):
     p = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
     is32 = 1 if lx.dtype == torch.int32 else 0
     calls = {
-        "sdtw_pairwise_l2": lambda: lib.sdtw_pairwise_l2(code, p(X), p(Y), B, N, M, d, p(D), sp),
+        "sdtw_pairwise_l2": lambda: lib.sdtw_pairwise_l2(code, p(X), p(Y), B, N, M, d, p(D), p(flags), sp),
         "sdtw_forward": lambda: lib.sdtw_forward(code, p(D), B, N, M, p(lx), p(ly), is32, w.gamma, w.bandwidth,
                                                  p(R), p(costs), p(ws), wsf, p(err), sp),
         "sdtw_backward": lambda: lib.sdtw_backward(code, p(D), p(R), B, N, M, p(lx), p(ly), is32, w.gamma,
                                                    w.bandwidth, p(E), p(ws), wsb, p(err), sp),
-        "sdtw_grad_l2": lambda: lib.sdtw_grad_l2(code, p(X), p(Y), p(D), p(E), p(g), B, N, M, d, p(gX), None, sp),
+        "sdtw_grad_l2": lambda: lib.sdtw_grad_l2(code, p(X), p(Y), p(D), p(E), p(g), p(flags), B, N, M, d, p(gX),
+                                                 None, sp),
     }
     out = {}
     for name, fn in calls.items():

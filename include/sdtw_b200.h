@@ -93,19 +93,22 @@ sdtw_status sdtw_backward(sdtw_dtype dtype, const void* D, const void* R, int64_
  * Replaces the reference's pairwise_l2_squared (src/torchsoftdtw/distances.py:4-18) on the module path.
  * Cells where the unclamped value is negative are stored as -0.0 (sign bit set), so that the
  * gradient kernel can reproduce the clamp's zero gradient there; -0.0 compares and adds as 0.
+ * clamp_flags (optional, (B,) int32 device array): set non-zero for every pair that has such a cell.
+ * fp32 with d % 4 == 0 and 16-byte aligned X, Y runs on the tensor cores (3xTF32, fp32 accuracy).
  * ------------------------------------------------------------------------------------------------- */
 sdtw_status sdtw_pairwise_l2(sdtw_dtype dtype, const void* X, const void* Y, int64_t B, int64_t N, int64_t M,
-                             int64_t d, void* D, void* stream);
+                             int64_t d, void* D, int* clamp_flags, void* stream);
 
 /* ---------------------------------------------------------------------------------------------------
  * Gradient of sum_b g[b] * costs[b] through the squared-L2 cost (the autograd of distances.py:14-18):
  *   G = g[b] * E * [D >= 0 before the clamp]  (read from the sign bit written by sdtw_pairwise_l2)
  *   grad_X = 2 * (rowsum(G) * X - G @ Y),   grad_Y = 2 * (colsum(G) * Y - G^T @ X)
- * g is (B,) `dtype` on the device; grad_X / grad_Y may be NULL to skip them.
+ * g is (B,) `dtype` on the device; grad_X / grad_Y may be NULL to skip them. clamp_flags (optional)
+ * is sdtw_pairwise_l2's output: pairs whose flag is 0 skip reading D.
  * ------------------------------------------------------------------------------------------------- */
 sdtw_status sdtw_grad_l2(sdtw_dtype dtype, const void* X, const void* Y, const void* D, const void* E,
-                         const void* g, int64_t B, int64_t N, int64_t M, int64_t d, void* grad_X, void* grad_Y,
-                         void* stream);
+                         const void* g, const int* clamp_flags, int64_t B, int64_t N, int64_t M, int64_t d,
+                         void* grad_X, void* grad_Y, void* stream);
 
 #ifdef __cplusplus
 }

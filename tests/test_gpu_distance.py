@@ -1,0 +1,114 @@
+"""GPU: the cost-matrix and gradient kernels called through the C ABI, against fp64 numpy.
+
+* fp32 tensor-core kernels (3xTF32): D within 2e-6 of the fp64 value relative to |x|^2 + |y|^2, the
+  clamp recorded as -0.0, per-pair clamp flags consistent with the sign bits;
+* grad_X / grad_Y: against 2*g*(rowsum(G) X - G Y) in fp64 with G = E * mask, for masked and unmasked
+  pairs, and for shapes that take the CUDA-core kernels.
+"""
+
+import ctypes
+
+import numpy as np
+import pytest
+import torch
+
+from torchsoftdtw_b200 import _ext
+
+pytestmark = pytest.mark.gpu
+
+p = lambda t: ctypes.c_void_p(t.data_ptr()) if t is not None else None  # noqa: E731
+
+
+def stream():
+    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+def pairwise(X, Y, flags=True):
+    lib = _ext.capi()
+    B, N, d = X.shape
+    M = Y.shape[1]
+    D = torch.empty(B, N, M, device=X.device, dtype=X.dtype)
+    fl = torch.full((B,), 7, device=X.device, dtype=torch.int32) if flags else None
+    st = lib.sdtw_pairwise_l2(1 if X.dtype == torch.float64 else 0, p(X), p(Y), B, N, M, d, p(D), p(fl), stream())
+    assert st == 0, lib.sdtw_status_string(st)
+    torch.cuda.synchronize()
+    return D, fl
+
+
+def grad(X, Y, D, E, g, flags, need_x=True, need_y=True):
+    lib = _ext.capi()
+    B, N, d = X.shape
+    M = Y.shape[1]
+    gX = torch.empty_like(X) if need_x else None
+    gY = torch.empty_like(Y) if need_y else None
+    st = lib.sdtw_grad_l2(1 if X.dtype == torch.float64 else 0, p(X), p(Y), p(D), p(E), p(g), p(flags), B, N, M, d,
+                          p(gX), p(gY), stream())
+    assert st == 0, lib.sdtw_status_string(st)
+    torch.cuda.synchronize()
+    return gX, gY
+
+
+SHAPES = [(3, 130, 70, 64), (2, 64, 64, 4), (2, 33, 257, 16), (1, 300, 200, 128), (2, 5, 7, 8), (2, 128, 128, 12),
+          (1, 17, 19, 3)]
+
+
+@pytest.mark.parametrize("B,N,M,d", SHAPES)
+def test_pairwise_fp32_accuracy_and_clamp_sign(cuda, B, N, M, d):
+    g = torch.Generator().manual_seed(N * M + d)
+    X = torch.randn(B, N, d, generator=g)
+    Y = torch.randn(B, M, d, generator=g)
+    Y[0, : min(N, M) // 2] = X[0, : min(N, M) // 2]  # identical frames: values near 0, some clamped
+    D, fl = pairwise(X.to(cuda), Y.to(cuda))
+    Dn = D.cpu().numpy()
+    Xd, Yd = X.double().numpy(), Y.double().numpy()
+    x2, y2 = (Xd * Xd).sum(-1), (Yd * Yd).sum(-1)
+    exact = x2[:, :, None] + y2[:, None, :] - 2 * np.matmul(Xd, np.swapaxes(Yd, 1, 2))
+    scale = x2[:, :, None] + y2[:, None, :] + 1e-30
+    assert np.max(np.abs(Dn - np.maximum(exact, 0)) / scale) < 2e-6
+    neg = np.signbit(Dn)
+    assert np.all(Dn[neg] == 0.0) and np.all(Dn >= 0)
+    assert np.array_equal(fl.cpu().numpy() != 0, neg.reshape(B, -1).any(1))
+
+
+def test_pairwise_fp64_matches_numpy(cuda):
+    g = torch.Generator().manual_seed(3)
+    X = torch.rand(4, 40, 4, generator=g, dtype=torch.float64) * 2 - 1
+    Y = torch.rand(4, 33, 4, generator=g, dtype=torch.float64) * 2 - 1
+    D, _ = pairwise(X.to(cuda), Y.to(cuda))
+    Xd, Yd = X.numpy(), Y.numpy()
+    exact = (Xd * Xd).sum(-1)[:, :, None] + (Yd * Yd).sum(-1)[:, None, :] - 2 * np.matmul(Xd, np.swapaxes(Yd, 1, 2))
+    np.testing.assert_allclose(D.cpu().numpy(), np.maximum(exact, 0), rtol=1e-13, atol=1e-13)
+
+
+def reference_grads(X, Y, D, E, g):
+    Xd, Yd = X.double().cpu().numpy(), Y.double().cpu().numpy()
+    mask = ~np.signbit(D.cpu().numpy())
+    G = g.double().cpu().numpy()[:, None, None] * E.double().cpu().numpy() * mask
+    gx = 2 * (G.sum(2)[:, :, None] * Xd - np.matmul(G, Yd))
+    gy = 2 * (G.sum(1)[:, :, None] * Yd - np.matmul(np.swapaxes(G, 1, 2), Xd))
+    return gx, gy
+
+
+@pytest.mark.parametrize("B,N,M,d", [(2, 130, 72, 64), (3, 64, 64, 4), (1, 257, 100, 128), (2, 40, 36, 12),
+                                     (2, 9, 10, 3), (2, 128, 130, 16)])
+@pytest.mark.parametrize("force_mask", [False, True])
+def test_grad_matches_fp64(cuda, B, N, M, d, force_mask):
+    gen = torch.Generator().manual_seed(B + N + M + d)
+    X = torch.randn(B, N, d, generator=gen)
+    Y = torch.randn(B, M, d, generator=gen)
+    E = torch.rand(B, N, M, generator=gen)
+    D = torch.rand(B, N, M, generator=gen) + 0.1
+    if force_mask:
+        D[torch.rand(B, N, M, generator=gen) < 0.1] = -0.0
+    gvec = torch.rand(B, generator=gen) + 0.5
+    flags = torch.tensor([1 if force_mask else 0] * B, dtype=torch.int32)
+    Xc, Yc, Dc, Ec, gc, fc = (t.to(cuda) for t in (X, Y, D, E, gvec, flags))
+    gX, gY = grad(Xc, Yc, Dc, Ec, gc, fc)
+    ex, ey = reference_grads(X, Y, D, E, gvec)
+    scale_x = np.max(np.abs(ex)) + 1e-30
+    scale_y = np.max(np.abs(ey)) + 1e-30
+    assert np.max(np.abs(gX.cpu().numpy() - ex)) / scale_x < 2e-6
+    assert np.max(np.abs(gY.cpu().numpy() - ey)) / scale_y < 2e-6
+    # no flags at all: every pair is treated as possibly clamped
+    gX2, _ = grad(Xc, Yc, Dc, Ec, gc, None, need_y=False)
+    assert np.max(np.abs(gX2.cpu().numpy() - ex)) / scale_x < 2e-6

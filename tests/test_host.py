@@ -99,8 +99,8 @@ def test_c_abi_rejects_bad_arguments_before_launching(lib):
     assert lib.sdtw_forward(0, p, 1, 4, 4, p, p, 0, 1.0, -1, p, p, null, 0, p, null) == -3
     assert lib.sdtw_backward(0, null, p, 1, 4, 4, p, p, 0, 1.0, -1, p, p, 1, p, null) == -3
     assert lib.sdtw_backward(1, null, null, 2, 4, 4, null, null, 0, -1.0, -1, null, null, 0, null, null) == -1
-    assert lib.sdtw_pairwise_l2(3, null, null, 1, 1, 1, 1, null, null) == -2
-    assert lib.sdtw_grad_l2(0, null, null, null, null, null, -2, 1, 1, 1, null, null, null) == -1
+    assert lib.sdtw_pairwise_l2(3, null, null, 1, 1, 1, 1, null, null, null) == -2
+    assert lib.sdtw_grad_l2(0, null, null, null, null, null, null, -2, 1, 1, 1, null, null, null) == -1
     # empty batch: nothing to do
     assert lib.sdtw_forward(0, null, 0, 4, 4, null, null, 0, 1.0, -1, null, null, null, 0, null, null) == 0
 
@@ -108,8 +108,7 @@ def test_c_abi_rejects_bad_arguments_before_launching(lib):
 def test_workspace_sizes(lib):
     f = lib.sdtw_forward_workspace_bytes(256, 512, 512, 0)
     b = lib.sdtw_backward_workspace_bytes(256, 512, 512, 0)
-    assert 0 < f < b
-    assert b >= 256 * 16 * 512 * 4  # boundary rows of every strip
+    assert f >= 256 * 16 * 512 * 4 and b >= 256 * 16 * 512 * 4  # one boundary row per strip
     assert lib.sdtw_backward_workspace_bytes(256, 512, 512, 1) > b
 
 
@@ -181,8 +180,8 @@ def test_fake_tensor_shapes():
         assert torch.ops.torchsoftdtw.backward(Dh, R16, lx, ly, 1.0, -1).dtype == torch.float16
         X = mode.from_tensor(torch.rand(2, 5, 3))
         Y = mode.from_tensor(torch.rand(2, 7, 3))
-        c, R, Dm = torch.ops.torchsoftdtw_b200.l2_forward(X, Y, lx, ly, 1.0, -1)
-        assert c.shape == (2,) and R.shape == (2, 7, 9) and Dm.shape == (2, 5, 7)
+        c, R, Dm, fl = torch.ops.torchsoftdtw_b200.l2_forward(X, Y, lx, ly, 1.0, -1)
+        assert c.shape == (2,) and R.shape == (2, 7, 9) and Dm.shape == (2, 5, 7) and fl.dtype == torch.int32
 
 
 def test_drop_in_import_name():

@@ -58,8 +58,8 @@ SIGNATURES: dict[str, tuple] = {
     "sdtw_forward": (_i, [_i, _p, _i64, _i64, _i64, _p, _p, _i, _d, _i64, _p, _p, _p, _sz, _p, _p]),
     "sdtw_backward_workspace_bytes": (_sz, [_i64, _i64, _i64, _i]),
     "sdtw_backward": (_i, [_i, _p, _p, _i64, _i64, _i64, _p, _p, _i, _d, _i64, _p, _p, _sz, _p, _p]),
-    "sdtw_pairwise_l2": (_i, [_i, _p, _p, _i64, _i64, _i64, _i64, _p, _p]),
-    "sdtw_grad_l2": (_i, [_i, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _p, _p, _p]),
+    "sdtw_pairwise_l2": (_i, [_i, _p, _p, _i64, _i64, _i64, _i64, _p, _p, _p]),
+    "sdtw_grad_l2": (_i, [_i, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _p, _p, _p]),
 }
 # Test hook of the failure path (declared in the .cu, not part of the public header).
 DEBUG_SIGNATURES: dict[str, tuple] = {"sdtw_debug_inject_stall": (None, [_i])}

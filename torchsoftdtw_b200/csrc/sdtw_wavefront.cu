@@ -8,10 +8,12 @@
 //     pair, then strip 1, ...; backward: the last strip first). A strip only ever waits on the strip
 //     claimed just before it in the same pair, which was claimed earlier by a running warp, so the
 //     persistent grid cannot deadlock, whatever its size.
-//   * The boundary row between strips goes through global memory (L2): the forward reads the row
-//     above from R itself; the backward reads the contributions pushed up from the row below from a
-//     workspace buffer. Progress flags are published per 32-column block with release/acquire, and
-//     every wait is bounded in time (the launch aborts with SDTW_ERR_TIMEOUT instead of hanging).
+//   * The boundary row between strips goes through a workspace buffer in global memory (L2): the
+//     forward passes each strip's last row of R down, the backward passes the contributions pushed
+//     from a strip's first row up. The buffer starts as an all-ones NaN pattern and every value is
+//     written once with st.relaxed, so a consumer knows a value has arrived when it is no longer the
+//     pattern: no flags, no fences. Consumers prefetch the next block's boundary values one block
+//     ahead; every wait is bounded in time (the launch aborts with SDTW_ERR_TIMEOUT, never hangs).
 //   * Per warp, a shared-memory ring of 4 chunks x 32 columns holds the operands of the swept rows
 //     (forward: D, overwritten in place by R; backward: R, overwritten in place by E); chunks are
 //     prefetched two blocks ahead with cp.async and written back with coalesced row stores.
@@ -108,14 +110,14 @@ struct FwdArgs {
     T* R;
     T* costs;
     Lengths len;
-    int* flags;   // (B, S) progress of each strip: columns < value of its last row are final
+    T* bnd;       // (B, S, M): last row of R of each strip, read by the strip below
     int* ticket;  // strip ticket counter
     int64_t B, N, M, bw;
     int S;
     T k;   // log2(e) / gamma
     T gl;  // gamma * ln(2)
     Sync sy;
-    int inject_skip;  // ticket whose strip never publishes progress (failure-detection test); -1 = none
+    int inject_skip;  // ticket whose strip never writes its boundary row (failure-detection test); -1 = none
     int vec;          // D rows are 16-byte aligned: 16-byte cp.async
 };
 
@@ -208,7 +210,6 @@ template <typename T>
 __device__ void fwd_strip(const FwdArgs<T>& a, T* ring, T* top, int64_t b, int s, int lane, bool skip_publish)
 {
     const T INF = Num<T>::inf();
-    int* my_flag = a.flags + b * a.S + s;
     Strip st;
     if (!make_strip(st, a.len, b, s, a.N, a.M, a.bw, lane)) {
         if (s == 0 && lane == 0) {
@@ -219,7 +220,6 @@ __device__ void fwd_strip(const FwdArgs<T>& a, T* ring, T* top, int64_t b, int s
                 a.costs[b] = (st.nx == 0 && st.ny == 0) ? T(0) : INF;
             }
         }
-        if (!skip_publish) publish(my_flag, kDone, lane);
         return;
     }
     const int64_t pitch = a.M + 2;
@@ -228,15 +228,16 @@ __device__ void fwd_strip(const FwdArgs<T>& a, T* ring, T* top, int64_t b, int s
     const int k0 = st.c_begin >> 5;
     const int k1 = (st.c_end + 31) >> 5;
     const int kc = st.c_end >> 5;
-    const bool has_consumer = st.rows == 32 && st.r0 + 32 < st.nx;
-    int plo = 0, phi = -1;  // in-band columns of the row above (row r0-1)
+    const bool has_consumer = st.rows == 32 && st.r0 + 32 < st.nx && !skip_publish;
+    T* bnd_out = a.bnd + (b * a.S + s) * a.M;
+    const T* bnd_in = a.bnd + (b * a.S + s - 1) * a.M;
+    int plo = 0, phi = -1;  // in-band columns of the row above (row r0-1), the ones the strip above wrote
     if (s > 0) {
         int64_t l64, h64;
         band_row_range(st.r0 - 1, st.nx, st.ny, a.bw, l64, h64);
         plo = static_cast<int>(l64);
         phi = static_cast<int>(h64);
     }
-    const T* above = Rb + static_cast<int64_t>(st.r0) * pitch + 1;  // padded row r0 == row r0-1, column 0
 
 #pragma unroll 1
     for (int q = 0; q < 3; ++q) {
@@ -248,21 +249,29 @@ __device__ void fwd_strip(const FwdArgs<T>& a, T* ring, T* top, int64_t b, int s
     T upp = (s == 0 && lane == 0) ? T(0) : INF;
     T* myrow = ring + lane * kRing;
 
+    // Row above, lane `lane`'s column of the next block (prefetched one block ahead).
+    T nv = INF;
+    if (s > 0) {
+        // lane 0's diagonal predecessor of column 32*k0 (column 32*k0 - 1 of the row above)
+        const int cd = 32 * k0 - 1;
+        const bool need_d = lane == 0 && cd >= plo && cd <= phi;
+        T vd = need_d ? ld_relaxed(bnd_in + cd) : INF;
+        if (!await_boundary(vd, bnd_in + cd, need_d, a.sy, lane)) return;
+        if (lane == 0) upp = vd;
+        const int c = 32 * k0 + lane;
+        if (c >= plo && c <= phi) nv = ld_relaxed(bnd_in + c);
+    }
+
 #pragma unroll 1
     for (int blk = k0; blk <= k1; ++blk) {
         const int tau0 = 32 * blk;
-        // Row above, columns [tau0, tau0+31], for lane 0.
         if (s > 0) {
-            if (!wait_progress(my_flag - 1, tau0 + 32, a.sy, lane)) return;
             const int c = tau0 + lane;
-            T v = INF;
-            if (c >= plo && c <= phi) v = __ldcg(above + c);
-            top[c & kSideMask] = v;
-            if (blk == k0) {
-                T vd = INF;
-                if (tau0 - 1 >= plo && tau0 - 1 <= phi) vd = __ldcg(above + tau0 - 1);
-                if (lane == 0) upp = vd;
-            }
+            const bool need = c >= plo && c <= phi;
+            if (!await_boundary(nv, bnd_in + c, need, a.sy, lane)) return;
+            top[c & kSideMask] = need ? nv : INF;
+            const int cn = c + 32;
+            nv = (cn >= plo && cn <= phi) ? ld_relaxed(bnd_in + cn) : INF;
         } else {
             top[(tau0 + lane) & kSideMask] = INF;
         }
@@ -274,11 +283,9 @@ __device__ void fwd_strip(const FwdArgs<T>& a, T* ring, T* top, int64_t b, int s
             fwd_block<T, true>(myrow, top, tau0, lane, st.A, st.Z, a.k, a.gl, outp, upp);
         __syncwarp();
         if (has_consumer) {
-            // Bottom row (lane 31) finished columns [tau0-31, tau0] in this block.
+            // Last row (lane 31) finished columns [tau0-31, tau0] in this block.
             const int c = tau0 - 31 + lane;
-            if (c >= st.c_begin && c <= st.c_end)
-                Rb[static_cast<int64_t>(st.r0 + 32) * pitch + c + 1] = ring[31 * kRing + (c & kRingMask)];
-            if (!skip_publish) publish(my_flag, tau0 + 1, lane);
+            if (c >= st.c_begin && c <= st.c_end) st_relaxed(bnd_out + c, ring[31 * kRing + (c & kRingMask)]);
         }
         if (blk - 1 >= k0) fwd_store_chunk<T>(a, Rb, ring, blk - 1, st, lane);
         __syncwarp();
@@ -290,7 +297,6 @@ __device__ void fwd_strip(const FwdArgs<T>& a, T* ring, T* top, int64_t b, int s
     if (kc == k1) fwd_store_chunk<T>(a, Rb, ring, kc, st, lane);
     if (st.nx - 1 - st.r0 == lane) a.costs[b] = ring[lane * kRing + ((st.ny - 1) & kRingMask)];
     __syncwarp();
-    if (!skip_publish) publish(my_flag, kDone, lane);
 }
 
 template <typename T>
@@ -334,11 +340,9 @@ struct BwdArgs {
     T* E;
     T* bnd;  // (B, S, M): contributions pushed from the first row of strip s+1 into the last row of strip s
     Lengths len;
-    int* flags;
     int* ticket;
     int64_t B, N, M, bw;
     int S;
-    int Mpad;  // progress = Mpad - (lowest final boundary column)
     T k;
     Sync sy;
     int inject_skip;
@@ -419,11 +423,9 @@ template <typename T>
 __device__ void bwd_strip(const BwdArgs<T>& a, T* ring, T* bndring, T* sendring, int64_t b, int s, int lane,
                           bool skip_publish)
 {
-    int* my_flag = a.flags + b * a.S + s;
     Strip st;
     if (!make_strip(st, a.len, b, s, a.N, a.M, a.bw, lane)) {
         if (st.bad && s == 0 && lane == 0) atomicOr(a.sy.err, kErrBadLength);
-        if (!skip_publish) publish(my_flag, kDone, lane);
         return;
     }
     const int64_t pitch = a.M + 2;
@@ -433,8 +435,8 @@ __device__ void bwd_strip(const BwdArgs<T>& a, T* ring, T* bndring, T* sendring,
     const int k1 = (st.c_end + 31) >> 5;
     const int kmin = (st.c_begin - 1) >> 5;  // arithmetic shift: -1 when c_begin == 0
     const bool has_producer = st.r0 + 32 < st.nx;
-    const bool has_consumer = s > 0;
-    int plo = 0, phi = -1;  // in-band columns of the producer's first row (row r0+32)
+    const bool has_consumer = s > 0 && !skip_publish;
+    int plo = 0, phi = -1;  // the producer's first row (row r0+32) pushes into columns [plo-1, phi]
     if (has_producer) {
         int64_t l64, h64;
         band_row_range(st.r0 + 32, st.nx, st.ny, a.bw, l64, h64);
@@ -458,18 +460,24 @@ __device__ void bwd_strip(const BwdArgs<T>& a, T* ring, T* bndring, T* sendring,
     T* rowB = rowA + kRing;
     T upc = T(0), sendv = T(0), pend = T(0), acc = seed;
 
+    // Contributions from the row below into lane 31's columns of the next block, prefetched.
+    auto needed = [&](int c) { return has_producer && c >= 0 && c >= plo - 1 && c <= phi; };
+    T nv = T(0);
+    {
+        const int c = 32 * k1 - 31 + lane;
+        if (needed(c)) nv = ld_relaxed(bnd_in + c);
+    }
+
 #pragma unroll 1
     for (int blk = k1; blk >= k0; --blk) {
         const int tau0 = 32 * blk;
-        // Contributions from the row below into lane 31's columns [tau0-31, tau0].
         {
             const int c = tau0 - 31 + lane;
-            T v = T(0);
-            if (has_producer) {
-                if (!wait_progress(my_flag + 1, a.Mpad - 32 * (blk - 1), a.sy, lane)) return;
-                if (c >= 0 && c >= plo - 1 && c <= phi) v = __ldcg(bnd_in + c);
-            }
-            bndring[(c + 31) & kSideMask] = v;
+            const bool need = needed(c);
+            if (!await_boundary(nv, bnd_in + c, need, a.sy, lane)) return;
+            bndring[(c + 31) & kSideMask] = need ? nv : T(0);
+            const int cn = c - 32;
+            nv = needed(cn) ? ld_relaxed(bnd_in + cn) : T(0);
         }
         cp_async_wait<2>();
         __syncwarp();
@@ -484,8 +492,7 @@ __device__ void bwd_strip(const BwdArgs<T>& a, T* ring, T* bndring, T* sendring,
         if (has_consumer) {
             // Lane 0 finished its pushes into row r0-1 for columns [tau0, tau0+31].
             const int c = tau0 + lane;
-            if (c >= 0 && c >= st.c_begin - 1 && c <= hi0) bnd_out[c] = sendring[c & kSideMask];
-            if (!skip_publish) publish(my_flag, a.Mpad - tau0, lane);
+            if (c >= 0 && c >= st.c_begin - 1 && c <= hi0) st_relaxed(bnd_out + c, sendring[c & kSideMask]);
         }
         bwd_store_chunk<T>(a, Eb, ring, blk, st, lane);
         __syncwarp();
@@ -495,9 +502,8 @@ __device__ void bwd_strip(const BwdArgs<T>& a, T* ring, T* bndring, T* sendring,
     cp_async_wait<0>();
     // When the sweep starts exactly at a chunk boundary, lane 0's last diagonal push (into column
     // c_begin-1 of the row above) was never followed by another step: write it out now.
-    if (has_consumer && lane == 0 && st.c_begin == 32 * k0 && st.c_begin >= 1) bnd_out[st.c_begin - 1] = pend;
+    if (has_consumer && lane == 0 && st.c_begin == 32 * k0 && st.c_begin >= 1) st_relaxed(bnd_out + st.c_begin - 1, pend);
     __syncwarp();
-    if (!skip_publish) publish(my_flag, kDone, lane);
 }
 
 template <typename T>
@@ -592,7 +598,11 @@ cudaError_t device_info(const DeviceInfo*& out)
 constexpr size_t kHeader = 256;  // ticket, abort word
 inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 inline int64_t strips_of(int64_t N) { return N > 0 ? (N + 31) / 32 : 1; }
-inline size_t flags_bytes(int64_t B, int64_t N) { return align_up(static_cast<size_t>(B * strips_of(N)) * 4, 256); }
+// Boundary buffer: one row of M values per strip.
+inline size_t bnd_bytes(int64_t B, int64_t N, int64_t M, size_t es)
+{
+    return align_up(static_cast<size_t>(B * strips_of(N) * M) * es, 256);
+}
 inline size_t elem_size(sdtw_dtype t) { return t == SDTW_F64 ? 8 : 4; }
 
 inline sdtw_status from_cuda(cudaError_t e) { return e == cudaSuccess ? SDTW_OK : static_cast<sdtw_status>(e); }
@@ -628,7 +638,9 @@ sdtw_status launch_forward(const void* D, int64_t B, int64_t N, int64_t M, const
     cudaError_t e = device_info(di);
     if (e != cudaSuccess) return from_cuda(e);
     const int64_t S = strips_of(N);
-    e = cudaMemsetAsync(ws, 0, kHeader + flags_bytes(B, N), stream);
+    e = cudaMemsetAsync(ws, 0, kHeader, stream);
+    if (e != cudaSuccess) return from_cuda(e);
+    e = cudaMemsetAsync(static_cast<char*>(ws) + kHeader, 0xff, bnd_bytes(B, N, M, sizeof(T)), stream);
     if (e != cudaSuccess) return from_cuda(e);
     const int64_t slab = (N + 2) * (M + 2);
     {
@@ -644,7 +656,7 @@ sdtw_status launch_forward(const void* D, int64_t B, int64_t N, int64_t M, const
     a.costs = static_cast<T*>(costs);
     a.len = Lengths{lx, ly, is32};
     a.ticket = reinterpret_cast<int*>(ws);
-    a.flags = reinterpret_cast<int*>(static_cast<char*>(ws) + kHeader);
+    a.bnd = reinterpret_cast<T*>(static_cast<char*>(ws) + kHeader);
     a.B = B;
     a.N = N;
     a.M = M;
@@ -670,23 +682,23 @@ sdtw_status launch_backward(const void* R, int64_t B, int64_t N, int64_t M, cons
     cudaError_t e = device_info(di);
     if (e != cudaSuccess) return from_cuda(e);
     const int64_t S = strips_of(N);
-    e = cudaMemsetAsync(ws, 0, kHeader + flags_bytes(B, N), stream);
+    e = cudaMemsetAsync(ws, 0, kHeader, stream);
+    if (e != cudaSuccess) return from_cuda(e);
+    e = cudaMemsetAsync(static_cast<char*>(ws) + kHeader, 0xff, bnd_bytes(B, N, M, sizeof(T)), stream);
     if (e != cudaSuccess) return from_cuda(e);
     e = cudaMemsetAsync(E, 0, static_cast<size_t>(B * N * M) * sizeof(T), stream);
     if (e != cudaSuccess) return from_cuda(e);
     BwdArgs<T> a;
     a.R = static_cast<const T*>(R);
     a.E = static_cast<T*>(E);
-    a.bnd = reinterpret_cast<T*>(static_cast<char*>(ws) + kHeader + flags_bytes(B, N));
+    a.bnd = reinterpret_cast<T*>(static_cast<char*>(ws) + kHeader);
     a.len = Lengths{lx, ly, is32};
     a.ticket = reinterpret_cast<int*>(ws);
-    a.flags = reinterpret_cast<int*>(static_cast<char*>(ws) + kHeader);
     a.B = B;
     a.N = N;
     a.M = M;
     a.bw = clamp_bw(bw, N, M);
     a.S = static_cast<int>(S);
-    a.Mpad = static_cast<int>(M + 64);
     a.k = static_cast<T>(1.4426950408889634 / gamma);
     a.sy = make_sync(ws, err);
     a.inject_skip = g_inject_skip;
@@ -755,22 +767,20 @@ void sdtw_set_wait_timeout(double seconds)
 }
 
 /* Failure-path test hook (not in the public header's main API): the strip holding ticket `ticket` of
- * every following launch completes its cells but never publishes its progress, so the strip after it
+ * every following launch completes its cells but never writes its boundary row, so the strip after it
  * runs into the bounded wait. -1 switches it off. */
 void sdtw_debug_inject_stall(int ticket) { g_inject_skip = ticket; }
 
 size_t sdtw_forward_workspace_bytes(int64_t B, int64_t N, int64_t M, sdtw_dtype dtype)
 {
-    (void)M;
-    (void)dtype;
-    if (B < 0 || N < 0) return 0;
-    return kHeader + flags_bytes(B, N);
+    if (B < 0 || N < 0 || M < 0) return 0;
+    return kHeader + bnd_bytes(B, N, M, elem_size(dtype));
 }
 
 size_t sdtw_backward_workspace_bytes(int64_t B, int64_t N, int64_t M, sdtw_dtype dtype)
 {
     if (B < 0 || N < 0 || M < 0) return 0;
-    return kHeader + flags_bytes(B, N) + align_up(static_cast<size_t>(B * strips_of(N) * M) * elem_size(dtype), 256);
+    return kHeader + bnd_bytes(B, N, M, elem_size(dtype));
 }
 
 sdtw_status sdtw_forward(sdtw_dtype dtype, const void* D, int64_t B, int64_t N, int64_t M, const void* lengths_x,

@@ -209,9 +209,11 @@ void xy_checks(const Tensor& X, const Tensor& Y, const Tensor& lengths_x, const 
     same_device(X, lengths_y, "lengths_y");
 }
 
-// Returns (costs, R, D): D is the clamped cost matrix with the clamp recorded in its sign bit.
-std::tuple<Tensor, Tensor, Tensor> l2_forward_cuda(const Tensor& X, const Tensor& Y, const Tensor& lengths_x,
-                                                   const Tensor& lengths_y, double gamma, int64_t bandwidth)
+// Returns (costs, R, D, clamp_flags): D is the clamped cost matrix with the clamp recorded in its sign
+// bit; clamp_flags (B,) int32 marks the pairs that have a clamped cell.
+std::tuple<Tensor, Tensor, Tensor, Tensor> l2_forward_cuda(const Tensor& X, const Tensor& Y,
+                                                           const Tensor& lengths_x, const Tensor& lengths_y,
+                                                           double gamma, int64_t bandwidth)
 {
     xy_checks(X, Y, lengths_x, lengths_y, gamma);
     const c10::cuda::CUDAGuard guard(X.device());
@@ -219,18 +221,20 @@ std::tuple<Tensor, Tensor, Tensor> l2_forward_cuda(const Tensor& X, const Tensor
     const Tensor Xc = X.to(acc).contiguous(), Yc = Y.to(acc).contiguous();
     const int64_t B = Xc.size(0), N = Xc.size(1), M = Yc.size(1), d = Xc.size(2);
     Tensor D = at::empty({B, N, M}, Xc.options());
+    Tensor flags = at::empty({B}, Xc.options().dtype(at::kInt));
     cudaStream_t stream = at::cuda::getCurrentCUDAStream(X.get_device()).stream();
-    check_status(sdtw_pairwise_l2(code_of(acc), Xc.data_ptr(), Yc.data_ptr(), B, N, M, d, D.data_ptr(), stream),
+    check_status(sdtw_pairwise_l2(code_of(acc), Xc.data_ptr(), Yc.data_ptr(), B, N, M, d, D.data_ptr(),
+                                  flags.data_ptr<int>(), stream),
                  "pairwise_l2");
     auto [costs, R] = run_forward(D, prep_lengths(lengths_x), prep_lengths(lengths_y), gamma, bandwidth);
-    return {costs, R, D};
+    return {costs, R, D, flags};
 }
 
 // Gradients of sum_b grad_costs[b] * costs[b] w.r.t. X and Y (each skipped when not requested).
 std::tuple<Tensor, Tensor> l2_backward_cuda(const Tensor& X, const Tensor& Y, const Tensor& D, const Tensor& R,
-                                            const Tensor& lengths_x, const Tensor& lengths_y,
-                                            const Tensor& grad_costs, double gamma, int64_t bandwidth, bool need_x,
-                                            bool need_y)
+                                            const Tensor& clamp_flags, const Tensor& lengths_x,
+                                            const Tensor& lengths_y, const Tensor& grad_costs, double gamma,
+                                            int64_t bandwidth, bool need_x, bool need_y)
 {
     xy_checks(X, Y, lengths_x, lengths_y, gamma);
     const c10::cuda::CUDAGuard guard(X.device());
@@ -246,8 +250,10 @@ std::tuple<Tensor, Tensor> l2_backward_cuda(const Tensor& X, const Tensor& Y, co
     Tensor gX = need_x ? at::empty({B, N, d}, Xc.options()) : at::empty({0}, X.options());
     Tensor gY = need_y ? at::empty({B, M, d}, Xc.options()) : at::empty({0}, Y.options());
     cudaStream_t stream = at::cuda::getCurrentCUDAStream(X.get_device()).stream();
+    TORCH_CHECK(clamp_flags.numel() == B && clamp_flags.scalar_type() == at::kInt, "clamp_flags must be (B,) int32");
     check_status(sdtw_grad_l2(code_of(acc), Xc.data_ptr(), Yc.data_ptr(), D.contiguous().data_ptr(), E.data_ptr(),
-                              g.data_ptr(), B, N, M, d, need_x ? gX.data_ptr() : nullptr,
+                              g.data_ptr(), clamp_flags.contiguous().data_ptr<int>(), B, N, M, d,
+                              need_x ? gX.data_ptr() : nullptr,
                               need_y ? gY.data_ptr() : nullptr, stream),
                  "grad_l2");
     if (need_x && gX.scalar_type() != X.scalar_type()) gX = gX.to(X.scalar_type());
@@ -288,9 +294,10 @@ TORCH_LIBRARY_IMPL(torchsoftdtw, CPU, m)
 TORCH_LIBRARY(torchsoftdtw_b200, m)
 {
     m.def("l2_forward(Tensor X, Tensor Y, Tensor lengths_x, Tensor lengths_y, float gamma, int bandwidth) "
-          "-> (Tensor, Tensor, Tensor)");
-    m.def("l2_backward(Tensor X, Tensor Y, Tensor D, Tensor R, Tensor lengths_x, Tensor lengths_y, "
-          "Tensor grad_costs, float gamma, int bandwidth, bool need_x, bool need_y) -> (Tensor, Tensor)");
+          "-> (Tensor, Tensor, Tensor, Tensor)");
+    m.def("l2_backward(Tensor X, Tensor Y, Tensor D, Tensor R, Tensor clamp_flags, Tensor lengths_x, "
+          "Tensor lengths_y, Tensor grad_costs, float gamma, int bandwidth, bool need_x, bool need_y) "
+          "-> (Tensor, Tensor)");
     m.def("error_bits(Tensor like) -> Tensor");
 }
 

@@ -53,11 +53,11 @@ def _l2_forward_fake(X, Y, lengths_x, lengths_y, gamma, bandwidth):
     M = Y.shape[1]
     acc_dt = _acc_dtype(X.dtype)
     return (X.new_empty((B,), dtype=acc_dt), X.new_empty((B, N + 2, M + 2), dtype=acc_dt),
-            X.new_empty((B, N, M), dtype=acc_dt))
+            X.new_empty((B, N, M), dtype=acc_dt), X.new_empty((B,), dtype=torch.int32))
 
 
 @torch.library.register_fake("torchsoftdtw_b200::l2_backward")
-def _l2_backward_fake(X, Y, D, R, lengths_x, lengths_y, grad_costs, gamma, bandwidth, need_x, need_y):
+def _l2_backward_fake(X, Y, D, R, clamp_flags, lengths_x, lengths_y, grad_costs, gamma, bandwidth, need_x, need_y):
     gX = X.new_empty(X.shape) if need_x else X.new_empty((0,))
     gY = Y.new_empty(Y.shape) if need_y else Y.new_empty((0,))
     return gX, gY
@@ -92,8 +92,8 @@ class _SoftDTWL2(Function):
     @staticmethod
     @torch.amp.custom_fwd(device_type="cuda")
     def forward(ctx, X, Y, lengths_x, lengths_y, gamma, bandwidth):
-        costs, R, D = torch.ops.torchsoftdtw_b200.l2_forward(X, Y, lengths_x, lengths_y, gamma, bandwidth)
-        ctx.save_for_backward(X, Y, D, R, lengths_x, lengths_y)
+        costs, R, D, flags = torch.ops.torchsoftdtw_b200.l2_forward(X, Y, lengths_x, lengths_y, gamma, bandwidth)
+        ctx.save_for_backward(X, Y, D, R, flags, lengths_x, lengths_y)
         ctx.gamma = gamma
         ctx.bandwidth = bandwidth
         return costs
@@ -101,10 +101,10 @@ class _SoftDTWL2(Function):
     @staticmethod
     @torch.amp.custom_bwd(device_type="cuda")
     def backward(ctx, grad_costs):
-        X, Y, D, R, lengths_x, lengths_y = ctx.saved_tensors
+        X, Y, D, R, flags, lengths_x, lengths_y = ctx.saved_tensors
         need_x, need_y = bool(ctx.needs_input_grad[0]), bool(ctx.needs_input_grad[1])
         gX, gY = torch.ops.torchsoftdtw_b200.l2_backward(
-            X, Y, D, R, lengths_x, lengths_y, grad_costs.contiguous(), ctx.gamma, ctx.bandwidth, need_x, need_y
+            X, Y, D, R, flags, lengths_x, lengths_y, grad_costs.contiguous(), ctx.gamma, ctx.bandwidth, need_x, need_y
         )
         return (gX if need_x else None), (gY if need_y else None), None, None, None, None
 
