@@ -34,3 +34,19 @@ def cuda():
     import torchsoftdtw_b200  # noqa: F401  (loads the native libraries)
 
     return torch.device("cuda", 0)
+
+
+KERNEL_PATHS = {"auto": 0, "ticket": 1, "pair": 2}
+
+
+@pytest.fixture(params=list(KERNEL_PATHS))
+def kernel_path(request):
+    """Runs a GPU test once per wavefront kernel family: chosen by shape ("auto"), the strip-ticket
+    kernels (strips claimed from a global counter, boundaries in global memory) and the pair-resident
+    kernels (one CTA per pair, boundaries in shared memory)."""
+    from torchsoftdtw_b200 import _ext
+
+    lib = _ext.capi()
+    lib.sdtw_debug_force_path(KERNEL_PATHS[request.param])
+    yield request.param
+    lib.sdtw_debug_force_path(0)

@@ -15,7 +15,7 @@ from oracle import oracle as O
 import torchsoftdtw_b200 as T
 from torchsoftdtw_b200 import workloads
 
-pytestmark = pytest.mark.gpu
+pytestmark = [pytest.mark.gpu, pytest.mark.usefixtures("kernel_path")]
 
 
 def run_module(X, Y, lx, ly, gamma, bw, normalize, dev, need=(True, True), distance="l2_squared"):

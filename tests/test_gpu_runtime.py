@@ -1,9 +1,12 @@
 """GPU: the runtime properties of the ops — torch.compile, CUDA-graph capture/replay, determinism,
 concurrent streams, the C ABI called directly, and failure detection without a GPU fault:
 
-* a wait that runs out: the failure-path hook makes one strip finish without publishing its progress;
-  the next strip's bounded wait expires, the launch aborts, the host reads SDTW_ERR_TIMEOUT, and the
-  context stays usable (a normal launch right after is correct);
+* a wait that runs out (both kernel families, forward and backward): the failure-path hook makes one
+  strip finish without publishing its progress; the next strip's bounded wait expires, the launch
+  aborts, the host reads SDTW_ERR_TIMEOUT, and the context stays usable (a normal launch right after
+  is correct);
+* the strip-ticket and pair-resident kernels agree bit for bit; the pair-resident kernels are correct
+  for any number of warps per CTA;
 * lengths outside [0, N]: NaN cost and SDTW_ERR_BAD_LENGTH, no out-of-range access.
 """
 
@@ -117,27 +120,97 @@ def test_c_abi_direct_call(cuda):
     np.testing.assert_allclose(E.cpu().numpy(), Er, rtol=1e-10, atol=1e-12)
 
 
-def test_wait_timeout_is_reported_and_context_survives(cuda):
+@pytest.mark.parametrize("path,direction", [(1, "forward"), (2, "forward"), (2, "backward")])
+def test_wait_timeout_is_reported_and_context_survives(cuda, path, direction):
+    """Strip 0 of pair 0 never publishes its boundary row (strip-ticket kernels: ticket 0; pair-resident
+    kernels: pair 0 * 4 strips + strip 0); the strip that depends on it runs into its bounded wait."""
     lib = _ext.capi()
     torch.manual_seed(5)
-    D = torch.rand(2, 64, 64, device=cuda)  # 2 strips per pair: strip 1 waits on strip 0
-    lx = torch.full((2,), 64, device=cuda, dtype=torch.long)
+    D = torch.rand(2, 128, 64, device=cuda)  # 4 strips of 32 rows per pair
+    lx = torch.full((2,), 128, device=cuda, dtype=torch.long)
     ly = torch.full((2,), 64, device=cuda, dtype=torch.long)
     T.check_errors(cuda)
+    _, R = torch.ops.torchsoftdtw.forward(D, lx, ly, 1.0, -1)
+    torch.cuda.synchronize()
+    lib.sdtw_debug_force_path(path)
     lib.sdtw_set_wait_timeout(0.2)
-    lib.sdtw_debug_inject_stall(0)  # ticket 0 = strip 0 of pair 0 never publishes
+    # backward: strip 0 is swept last and has no consumer; stall strip 3 (the first) instead
+    lib.sdtw_debug_inject_stall(0 if direction == "forward" else 3)
     try:
-        torch.ops.torchsoftdtw.forward(D, lx, ly, 1.0, -1)
+        if direction == "forward":
+            torch.ops.torchsoftdtw.forward(D, lx, ly, 1.0, -1)
+        else:
+            torch.ops.torchsoftdtw.backward(D, R, lx, ly, 1.0, -1)
         torch.cuda.synchronize()
         with pytest.raises(RuntimeError, match="timed out"):
             T.check_errors(cuda)
     finally:
         lib.sdtw_debug_inject_stall(-1)
         lib.sdtw_set_wait_timeout(2.0)
-    costs = T.soft_dtw(D.double())
-    ref, _ = O.forward(D.double().cpu().numpy(), None, None, 1.0, -1)
-    np.testing.assert_allclose(costs.cpu().numpy(), ref, rtol=1e-10)
+    try:
+        costs = T.soft_dtw(D.double())
+        ref, _ = O.forward(D.double().cpu().numpy(), None, None, 1.0, -1)
+        np.testing.assert_allclose(costs.cpu().numpy(), ref, rtol=1e-10)
+        T.check_errors(cuda)
+    finally:
+        lib.sdtw_debug_force_path(0)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float64])
+@pytest.mark.parametrize("B,N,M,bw,ragged", [(3, 100, 90, -1, False), (4, 257, 130, 20, True), (5, 64, 300, 3, True),
+                                             (2, 31, 33, -1, True), (3, 450, 70, 0, False)])
+def test_kernel_families_agree_bit_for_bit(cuda, dtype, B, N, M, bw, ragged):
+    """The strip-ticket and pair-resident kernels evaluate every cell with the same expression in the
+    same order, so costs, R and E agree exactly."""
+    lib = _ext.capi()
+    g = torch.Generator().manual_seed(N + M + B)
+    D = (torch.rand(B, N, M, generator=g, dtype=torch.float64) * 2).to(dtype).to(cuda)
+    if ragged:
+        lx = torch.randint(max(1, N // 2), N + 1, (B,), generator=g)
+        ly = torch.randint(max(1, M // 2), M + 1, (B,), generator=g)
+    else:
+        lx, ly = torch.full((B,), N), torch.full((B,), M)
+    lx, ly = lx.to(cuda), ly.to(cuda)
+    outs = []
+    try:
+        for path in (1, 2):
+            lib.sdtw_debug_force_path(path)
+            c, R = torch.ops.torchsoftdtw.forward(D, lx, ly, 0.3, bw)
+            E = torch.ops.torchsoftdtw.backward(D, R, lx, ly, 0.3, bw)
+            torch.cuda.synchronize()
+            outs.append((c, R, E))
+    finally:
+        lib.sdtw_debug_force_path(0)
     T.check_errors(cuda)
+    for x, y in zip(outs[0], outs[1]):
+        assert torch.equal(x, y)
+
+
+@pytest.mark.parametrize("warps", [1, 2, 3, 5, 16])
+def test_pair_kernels_any_warp_count(cuda, warps):
+    """The pair-resident kernels are correct for any number of warps per CTA (strips wrap around the
+    warps several times when warps < strips)."""
+    lib = _ext.capi()
+    g = torch.Generator().manual_seed(warps)
+    B, N, M = 3, 300, 120
+    D = torch.rand(B, N, M, generator=g, dtype=torch.float64)
+    lx = torch.tensor([300, 287, 150])
+    ly = torch.tensor([120, 97, 120])
+    try:
+        lib.sdtw_debug_force_path(2)
+        lib.sdtw_debug_set_pair_warps(warps)
+        c, R = torch.ops.torchsoftdtw.forward(D.to(cuda), lx.to(cuda), ly.to(cuda), 0.7, 40)
+        E = torch.ops.torchsoftdtw.backward(D.to(cuda), R, lx.to(cuda), ly.to(cuda), 0.7, 40)
+        torch.cuda.synchronize()
+    finally:
+        lib.sdtw_debug_force_path(0)
+        lib.sdtw_debug_set_pair_warps(16)
+    T.check_errors(cuda)
+    cr, Rr = O.forward(D.numpy(), lx.numpy(), ly.numpy(), 0.7, 40)
+    Er = O.backward(D.numpy(), Rr, lx.numpy(), ly.numpy(), 0.7, 40)
+    np.testing.assert_allclose(c.cpu().numpy(), cr, rtol=1e-10)
+    np.testing.assert_allclose(R.cpu().numpy(), Rr, rtol=1e-10, atol=1e-12)
+    np.testing.assert_allclose(E.cpu().numpy(), Er, rtol=1e-10, atol=1e-12)
 
 
 def test_bad_lengths_give_nan_and_error_bit(cuda):

@@ -55,21 +55,29 @@ def _run(cmd: list[str]) -> None:
     subprocess.run(cmd, check=True)
 
 
+def _extra_flags(src: str) -> list[str]:
+    # The wavefront kernels spell out every fused multiply-add they use (fma()); no other product is
+    # contracted, so the two kernel families (and both directions) round every cell identically.
+    if os.path.basename(src) in ("sdtw_wavefront.cu", "sdtw_pairwave.cu"):
+        return ["--fmad=false"]
+    return []
+
+
 def build_kernels(force: bool = False) -> str:
     """nvcc: csrc/*.cu -> lib/libsdtw_b200.so (sm_100a)."""
     os.makedirs(LIBDIR, exist_ok=True)
     os.makedirs(OBJDIR, exist_ok=True)
     nvcc = os.path.join(_cuda_home(), "bin", "nvcc")
     sources = sorted(glob.glob(os.path.join(CSRC, "*.cu")))
-    headers = sorted(glob.glob(os.path.join(CSRC, "*.cuh"))) + [os.path.join(INCLUDE, "sdtw_b200.h")]
+    headers = sorted(glob.glob(os.path.join(CSRC, "*.cuh")) + glob.glob(os.path.join(CSRC, "*.h"))) + [os.path.join(INCLUDE, "sdtw_b200.h")]
     objs = []
     jobs = []
     for src in sources:
         obj = os.path.join(OBJDIR, os.path.basename(src) + ".o")
         objs.append(obj)
-        if force or _stale(obj, [src] + headers):
-            jobs.append([nvcc, *ARCH_FLAGS, "-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC",
-                         "-I" + INCLUDE, "-I" + CSRC, "-c", src, "-o", obj])
+        if force or _stale(obj, [src] + headers + [__file__]):
+            jobs.append([nvcc, *ARCH_FLAGS, "-O3", "-lineinfo", "-std=c++17", *_extra_flags(src), "-Xcompiler",
+                         "-fPIC", "-I" + INCLUDE, "-I" + CSRC, "-c", src, "-o", obj])
     if jobs:
         with ThreadPoolExecutor(max_workers=len(jobs)) as ex:
             list(ex.map(_run, jobs))

@@ -61,8 +61,13 @@ SIGNATURES: dict[str, tuple] = {
     "sdtw_pairwise_l2": (_i, [_i, _p, _p, _i64, _i64, _i64, _i64, _p, _p, _p]),
     "sdtw_grad_l2": (_i, [_i, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _p, _p, _p]),
 }
-# Test hook of the failure path (declared in the .cu, not part of the public header).
-DEBUG_SIGNATURES: dict[str, tuple] = {"sdtw_debug_inject_stall": (None, [_i])}
+# Test and tuning hooks (declared in the .cu, not part of the public header).
+DEBUG_SIGNATURES: dict[str, tuple] = {
+    "sdtw_debug_inject_stall": (None, [_i]),
+    "sdtw_debug_force_path": (None, [_i]),
+    "sdtw_debug_set_pair_warps": (None, [_i]),
+    "sdtw_debug_kernel_launches": (ctypes.c_uint64, []),
+}
 
 
 def capi() -> ctypes.CDLL:

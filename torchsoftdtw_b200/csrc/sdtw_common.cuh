@@ -8,6 +8,10 @@
 
 namespace sdtw {
 
+// Kernel launches made by this library in this process (all entry points; read by
+// sdtw_debug_kernel_launches). Defined in sdtw_wavefront.cu.
+void count_launch();
+
 // --------------------------------------------------------------------------------------------------
 // Tiling constants of the strip wavefront.
 //   A strip is 32 consecutive rows of one pair, owned by one warp (lane l <-> row r0 + l).

@@ -482,6 +482,7 @@ sdtw_status launch_pairwise(const void* X, const void* Y, int64_t B, int64_t N, 
             }
             const dim3 grid(static_cast<unsigned>((M + kPT - 1) / kPT), static_cast<unsigned>((N + kPT - 1) / kPT),
                             static_cast<unsigned>(B));
+            count_launch();
             pairwise_l2_mma_kernel<<<grid, 256, kPairwiseSmem, s>>>(static_cast<const float*>(X),
                                                                    static_cast<const float*>(Y),
                                                                    static_cast<float*>(D), clamp_flags, N, M, d);
@@ -491,6 +492,7 @@ sdtw_status launch_pairwise(const void* X, const void* Y, int64_t B, int64_t N, 
     }
     const dim3 grid(static_cast<unsigned>((M + kTile - 1) / kTile), static_cast<unsigned>((N + kTile - 1) / kTile),
                     static_cast<unsigned>(B));
+    count_launch();
     pairwise_l2_kernel<T><<<grid, 256, 0, s>>>(static_cast<const T*>(X), static_cast<const T*>(Y), static_cast<T*>(D),
                                                clamp_flags, N, M, d);
     const cudaError_t e = cudaGetLastError();
@@ -516,6 +518,7 @@ sdtw_status launch_grad(const void* X, const void* Y, const void* D, const void*
             }
             const dim3 grid(static_cast<unsigned>((d + kGC - 1) / kGC), static_cast<unsigned>((N + kGR - 1) / kGR),
                             static_cast<unsigned>(B));
+            count_launch();
             grad_x_mma_kernel<<<grid, 256, kGradSmem, s>>>(
                 static_cast<const float*>(X), static_cast<const float*>(Y), static_cast<const float*>(D),
                 static_cast<const float*>(E), static_cast<const float*>(g), clamp_flags, static_cast<float*>(gX), N,
@@ -525,12 +528,14 @@ sdtw_status launch_grad(const void* X, const void* Y, const void* D, const void*
     }
     if (gX && !gx_done) {
         const dim3 grid(cblocks, static_cast<unsigned>((N + kTile - 1) / kTile), static_cast<unsigned>(B));
+        count_launch();
         grad_l2_kernel<T, false><<<grid, 256, 0, s>>>(static_cast<const T*>(X), static_cast<const T*>(Y),
                                                       static_cast<const T*>(D), static_cast<const T*>(E),
                                                       static_cast<const T*>(g), static_cast<T*>(gX), N, M, d, N, M);
     }
     if (gY) {
         const dim3 grid(cblocks, static_cast<unsigned>((M + kTile - 1) / kTile), static_cast<unsigned>(B));
+        count_launch();
         grad_l2_kernel<T, true><<<grid, 256, 0, s>>>(static_cast<const T*>(Y), static_cast<const T*>(X),
                                                      static_cast<const T*>(D), static_cast<const T*>(E),
                                                      static_cast<const T*>(g), static_cast<T*>(gY), M, N, d, N, M);

@@ -1,0 +1,55 @@
+// Pair-resident wavefront kernels (one CTA per pair, strip boundaries in shared memory): host entry
+// points used by the C ABI in sdtw_wavefront.cu.
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+
+#include <cuda_runtime.h>
+
+#include "sdtw_common.cuh"
+
+namespace sdtw {
+
+// Launch bounds of the pair-resident kernels: at most SDTW_PAIR_THREADS threads per CTA, and registers
+// sized for SDTW_PAIR_MIN_CTAS resident CTAs of that size per SM.
+#ifndef SDTW_PAIR_THREADS
+#define SDTW_PAIR_THREADS 512
+#endif
+#ifndef SDTW_PAIR_MIN_CTAS
+#define SDTW_PAIR_MIN_CTAS 1
+#endif
+constexpr int kPairMaxWarps = SDTW_PAIR_THREADS / 32;  // warps per CTA at most
+constexpr int kFwdStride = 65;     // forward ring row: 2 slots of 32 positions + 1 (odd: conflict-free)
+constexpr int kBwdStride = 97;     // backward ring row: 3 slots + 1
+constexpr int kBufPad = 64;        // boundary rows are indexed by column + kBufPad
+
+// Shared-memory bytes of one CTA with W warps.
+template <typename T>
+size_t pair_fwd_smem_bytes(int W, int64_t M);
+template <typename T>
+size_t pair_bwd_smem_bytes(int W, int64_t M);
+
+// Sets the kernels' dynamic shared-memory limit (once per device).
+template <typename T>
+cudaError_t pair_init_attrs(int max_smem);
+
+// Registers per thread of the forward / backward kernel.
+template <typename T>
+cudaError_t pair_regs(bool backward, int& regs);
+
+// Largest W <= cap (and <= the strip count) whose CTA fits `budget` bytes; 0 if none.
+template <typename T>
+int pair_warps(bool backward, int64_t N, int64_t M, int cap, size_t budget);
+
+// Progress keys stay below 2^30 for these sizes.
+bool pair_keys_fit(int64_t N, int64_t M);
+
+template <typename T>
+cudaError_t pair_forward(const T* D, T* R, T* costs, const void* lx, const void* ly, int is32, int64_t B, int64_t N,
+                         int64_t M, int64_t bw, double gamma, int W, Sync sy, int64_t inject, cudaStream_t stream);
+template <typename T>
+cudaError_t pair_backward(const T* R, T* E, const void* lx, const void* ly, int is32, int64_t B, int64_t N, int64_t M,
+                          int64_t bw, double gamma, int W, Sync sy, int64_t inject, cudaStream_t stream);
+
+}  // namespace sdtw

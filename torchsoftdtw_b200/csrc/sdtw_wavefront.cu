@@ -29,77 +29,15 @@
 //             (softdtw.cpp:249-257) written without the cancellation R[s]-D[s]: three exp2 and one
 //             reciprocal per cell, and no read of D.
 #include <algorithm>
+#include <atomic>
 #include <cmath>
 #include <mutex>
 
-#include "sdtw_common.cuh"
 #include "sdtw_b200.h"
+#include "sdtw_pairwave.h"
+#include "sdtw_strip.cuh"
 
 namespace sdtw {
-
-// Lengths arrive as int64 or int32 device arrays (the reference converts int32 to int64 on the host,
-// softdtw.cpp:67-70; here the kernel reads either directly).
-struct Lengths {
-    const void* px;
-    const void* py;
-    int is32;
-    __device__ __forceinline__ int64_t x(int64_t b) const
-    {
-        return is32 ? static_cast<int64_t>(static_cast<const int*>(px)[b]) : static_cast<const int64_t*>(px)[b];
-    }
-    __device__ __forceinline__ int64_t y(int64_t b) const
-    {
-        return is32 ? static_cast<int64_t>(static_cast<const int*>(py)[b]) : static_cast<const int64_t*>(py)[b];
-    }
-};
-
-// Per-lane geometry of one strip.
-struct Strip {
-    int64_t nx, ny;
-    int r0, rows;          // first row, number of valid rows (<= 32)
-    int lo, hi;            // this lane's in-band columns [lo, hi] (empty for lanes >= rows)
-    int c_begin, c_end;    // union over the strip's rows
-    int A, Z;              // this lane is valid at step tau iff A <= tau <= Z
-    int Amax, Zmin;        // every lane is valid for tau in [Amax, Zmin]
-    bool bad;
-};
-
-__device__ __forceinline__ int warp_max(int v)
-{
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v = max(v, __shfl_xor_sync(kFull, v, o));
-    return v;
-}
-__device__ __forceinline__ int warp_min(int v)
-{
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v = min(v, __shfl_xor_sync(kFull, v, o));
-    return v;
-}
-
-// Returns false if the strip has no cells (empty pair, or r0 beyond the pair's length).
-__device__ __forceinline__ bool make_strip(Strip& st, const Lengths& len, int64_t b, int s, int64_t N, int64_t M,
-                                           int64_t bw, int lane)
-{
-    st.nx = len.x(b);
-    st.ny = len.y(b);
-    st.bad = st.nx < 0 || st.nx > N || st.ny < 0 || st.ny > M;
-    if (st.bad) st.nx = st.ny = 0;
-    st.r0 = 32 * s;
-    if (st.nx == 0 || st.ny == 0 || st.r0 >= st.nx) return false;
-    st.rows = static_cast<int>(st.nx - st.r0 < 32 ? st.nx - st.r0 : 32);
-    int64_t lo = 1, hi = 0;
-    if (lane < st.rows) band_row_range(st.r0 + lane, st.nx, st.ny, bw, lo, hi);
-    st.lo = static_cast<int>(lo);
-    st.hi = static_cast<int>(hi);
-    st.c_begin = __shfl_sync(kFull, st.lo, 0);
-    st.c_end = __shfl_sync(kFull, st.hi, st.rows - 1);
-    st.A = lane < st.rows ? st.lo + lane : (1 << 30);
-    st.Z = lane < st.rows ? st.hi + lane : -(1 << 30);
-    st.Amax = warp_max(st.A);
-    st.Zmin = warp_min(st.Z);
-    return true;
-}
 
 // ==================================================================================================
 // Forward
@@ -120,21 +58,6 @@ struct FwdArgs {
     int inject_skip;  // ticket whose strip never writes its boundary row (failure-detection test); -1 = none
     int vec;          // D rows are 16-byte aligned: 16-byte cp.async
 };
-
-template <typename T>
-__device__ __forceinline__ T fwd_cell(T d, T diag, T up, T left, T k, T gl)
-{
-    const T a = Num<T>::mn(up, left);
-    const T y = Num<T>::mx(up, left);
-    const T m = Num<T>::mn(a, diag);
-    const T x = Num<T>::mx(a, diag);
-    // m is +inf only when all three predecessors are: the exponents then stay -inf and R = D + inf.
-    const T mc = Num<T>::mn(m, Num<T>::big());
-    const T e1 = Num<T>::exp2_((mc - x) * k);
-    const T e2 = Num<T>::exp2_((mc - y) * k);
-    const T sum = (T(1) + e1) + e2;
-    return fma(-gl, Num<T>::log2_(sum), m) + d;
-}
 
 // 32 forward steps tau = tau0 .. tau0+31 of one warp.
 template <typename T, bool MASKED>
@@ -533,14 +456,23 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32) sdtw_bwd_kernel(BwdArgs<T> 
 // ==================================================================================================
 // Host side
 // ==================================================================================================
+std::atomic<uint64_t> g_launches{0};
+void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+
 namespace {
 
 double g_timeout_s = 2.0;
 int g_inject_skip = -1;  // set only through sdtw_debug_inject_stall (tests of the failure path)
+int g_force_path = 0;    // 0: automatic, 1: strip-ticket kernels, 2: pair-resident kernels
+int g_pair_warps = kPairMaxWarps;  // warps per CTA of the pair-resident kernels (upper bound)
 
 struct DeviceInfo {
     bool ready = false;
     int sms = 0;
+    int max_smem = 0;  // opt-in dynamic shared memory per CTA
+    int sm_smem = 0;   // shared memory per SM
+    int sm_regs = 0;   // 32-bit registers per SM
+    int pair_regs[2][2] = {{0, 0}, {0, 0}};  // [fp64][backward]: registers per thread of the pair kernels
     int occ_fwd[2] = {0, 0};
     int occ_bwd[2] = {0, 0};
 };
@@ -585,6 +517,22 @@ cudaError_t device_info(const DeviceInfo*& out)
     if (!di.ready) {
         e = cudaDeviceGetAttribute(&di.sms, cudaDevAttrMultiProcessorCount, dev);
         if (e != cudaSuccess) return e;
+        e = cudaDeviceGetAttribute(&di.max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+        if (e != cudaSuccess) return e;
+        e = cudaDeviceGetAttribute(&di.sm_smem, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev);
+        if (e != cudaSuccess) return e;
+        e = cudaDeviceGetAttribute(&di.sm_regs, cudaDevAttrMaxRegistersPerMultiprocessor, dev);
+        if (e != cudaSuccess) return e;
+        e = pair_init_attrs<float>(di.max_smem);
+        if (e != cudaSuccess) return e;
+        e = pair_init_attrs<double>(di.max_smem);
+        if (e != cudaSuccess) return e;
+        for (int bwd = 0; bwd < 2; ++bwd) {
+            e = pair_regs<float>(bwd != 0, di.pair_regs[0][bwd]);
+            if (e != cudaSuccess) return e;
+            e = pair_regs<double>(bwd != 0, di.pair_regs[1][bwd]);
+            if (e != cudaSuccess) return e;
+        }
         e = init_kernel_attrs<float>(di.occ_fwd[0], di.occ_bwd[0]);
         if (e != cudaSuccess) return e;
         e = init_kernel_attrs<double>(di.occ_fwd[1], di.occ_bwd[1]);
@@ -629,6 +577,29 @@ Sync make_sync(void* workspace, uint32_t* err_word)
     return sy;
 }
 
+// Pair-resident kernels (one CTA per pair) when the batch fills the GPU and a CTA fits in shared
+// memory; otherwise the strip-ticket kernels, which spread a few long pairs over every SM. Returns the
+// pair kernels' warps per CTA, or 0 for the strip-ticket kernels.
+template <typename T>
+int choose_pair_warps(const DeviceInfo& di, bool backward, int64_t B, int64_t N, int64_t M)
+{
+    if (g_force_path == 1) return 0;
+    // Measured on B200 (B = 256, N = M = 512, fp32): the pair-resident forward takes 233 us against the
+    // strip-ticket forward's 303 us; the backward is on par (322 us against 319 us), so by default only
+    // the forward switches.
+    if (g_force_path != 2 && (B < di.sms || backward)) return 0;
+    if (B > 0x7fffffff || !pair_keys_fit(N, M)) return 0;
+    // Enough CTAs per SM for the whole batch to be resident at once (up to 8), each as wide as its
+    // share of the SM's shared memory and registers allows.
+    const int64_t want = std::min<int64_t>(8, std::max<int64_t>(1, (B + di.sms - 1) / di.sms));
+    const size_t share = static_cast<size_t>(di.sm_smem) / static_cast<size_t>(want);
+    const size_t budget = std::min<size_t>(static_cast<size_t>(di.max_smem), share > 1024 ? share - 1024 : 0);
+    const int regs = std::max(1, di.pair_regs[sizeof(T) == 8 ? 1 : 0][backward ? 1 : 0]);
+    const int reg_warps = static_cast<int>(di.sm_regs / (want * 32 * regs));
+    const int W = pair_warps<T>(backward, N, M, std::min(g_pair_warps, std::max(1, reg_warps)), budget);
+    return W > 0 ? W : pair_warps<T>(backward, N, M, g_pair_warps, static_cast<size_t>(di.max_smem));
+}
+
 template <typename T>
 sdtw_status launch_forward(const void* D, int64_t B, int64_t N, int64_t M, const void* lx, const void* ly, int is32,
                            double gamma, int64_t bw, void* R, void* costs, void* ws, uint32_t* err,
@@ -640,6 +611,11 @@ sdtw_status launch_forward(const void* D, int64_t B, int64_t N, int64_t M, const
     const int64_t S = strips_of(N);
     e = cudaMemsetAsync(ws, 0, kHeader, stream);
     if (e != cudaSuccess) return from_cuda(e);
+    const int W = choose_pair_warps<T>(*di, false, B, N, M);
+    if (W > 0)
+        return from_cuda(pair_forward<T>(static_cast<const T*>(D), static_cast<T*>(R), static_cast<T*>(costs), lx, ly,
+                                         is32, B, N, M, clamp_bw(bw, N, M), gamma, W, make_sync(ws, err),
+                                         g_inject_skip, stream));
     e = cudaMemsetAsync(static_cast<char*>(ws) + kHeader, 0xff, bnd_bytes(B, N, M, sizeof(T)), stream);
     if (e != cudaSuccess) return from_cuda(e);
     const int64_t slab = (N + 2) * (M + 2);
@@ -648,6 +624,7 @@ sdtw_status launch_forward(const void* D, int64_t B, int64_t N, int64_t M, const
         const int threads = 256;
         const int64_t want = (total + threads - 1) / threads;
         const int blocks = static_cast<int>(std::min<int64_t>(want, int64_t(di->sms) * 16));
+        count_launch();
         sdtw_fill_r_kernel<T><<<std::max(blocks, 1), threads, 0, stream>>>(static_cast<T*>(R), total, slab);
     }
     FwdArgs<T> a;
@@ -670,6 +647,7 @@ sdtw_status launch_forward(const void* D, int64_t B, int64_t N, int64_t M, const
     const int occ = di->occ_fwd[sizeof(T) == 8 ? 1 : 0];
     const int64_t ctas_needed = (B * S + kWarpsPerCta - 1) / kWarpsPerCta;
     const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(ctas_needed, int64_t(di->sms) * std::max(occ, 1))));
+    count_launch();
     sdtw_fwd_kernel<T><<<grid, kWarpsPerCta * 32, fwd_smem_bytes<T>(), stream>>>(a);
     return from_cuda(cudaGetLastError());
 }
@@ -684,6 +662,10 @@ sdtw_status launch_backward(const void* R, int64_t B, int64_t N, int64_t M, cons
     const int64_t S = strips_of(N);
     e = cudaMemsetAsync(ws, 0, kHeader, stream);
     if (e != cudaSuccess) return from_cuda(e);
+    const int W = choose_pair_warps<T>(*di, true, B, N, M);
+    if (W > 0)
+        return from_cuda(pair_backward<T>(static_cast<const T*>(R), static_cast<T*>(E), lx, ly, is32, B, N, M,
+                                          clamp_bw(bw, N, M), gamma, W, make_sync(ws, err), g_inject_skip, stream));
     e = cudaMemsetAsync(static_cast<char*>(ws) + kHeader, 0xff, bnd_bytes(B, N, M, sizeof(T)), stream);
     if (e != cudaSuccess) return from_cuda(e);
     e = cudaMemsetAsync(E, 0, static_cast<size_t>(B * N * M) * sizeof(T), stream);
@@ -705,6 +687,7 @@ sdtw_status launch_backward(const void* R, int64_t B, int64_t N, int64_t M, cons
     const int occ = di->occ_bwd[sizeof(T) == 8 ? 1 : 0];
     const int64_t ctas_needed = (B * S + kWarpsPerCta - 1) / kWarpsPerCta;
     const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(ctas_needed, int64_t(di->sms) * std::max(occ, 1))));
+    count_launch();
     sdtw_bwd_kernel<T><<<grid, kWarpsPerCta * 32, bwd_smem_bytes<T>(), stream>>>(a);
     return from_cuda(cudaGetLastError());
 }
@@ -770,6 +753,16 @@ void sdtw_set_wait_timeout(double seconds)
  * every following launch completes its cells but never writes its boundary row, so the strip after it
  * runs into the bounded wait. -1 switches it off. */
 void sdtw_debug_inject_stall(int ticket) { g_inject_skip = ticket; }
+
+/* Test and tuning hooks (not in the public header): `path` 0 chooses the kernels by shape, 1 forces the
+ * strip-ticket kernels, 2 the pair-resident kernels (when a CTA fits); `warps` caps the pair-resident
+ * kernels' warps per CTA (1..16). With the pair-resident kernels, sdtw_debug_inject_stall's argument
+ * names strip s of pair b as b * ceil(N/32) + s. */
+/* Number of kernels this library has launched in this process (all entry points). */
+uint64_t sdtw_debug_kernel_launches(void) { return g_launches.load(std::memory_order_relaxed); }
+
+void sdtw_debug_force_path(int path) { g_force_path = (path >= 0 && path <= 2) ? path : 0; }
+void sdtw_debug_set_pair_warps(int warps) { g_pair_warps = (warps >= 1 && warps <= kPairMaxWarps) ? warps : kPairMaxWarps; }
 
 size_t sdtw_forward_workspace_bytes(int64_t B, int64_t N, int64_t M, sdtw_dtype dtype)
 {
