@@ -354,8 +354,11 @@ def main():
         name, ms = max(kt.items(), key=lambda kv: kv[1])
         bytes_per_cell = ALGO_BYTES[name] * (8 if w.dtype == torch.float64 else 4)
         achieved = cells_rank * bytes_per_cell / (ms / 1e3) / 1e9
+        traffic = measured_traffic(w, name)
         result["roofline"] = {"bound": "hbm", "kernel": name, "achieved": achieved, "peak": hbm,
-                              "unit": "GB/s", "frac": achieved / hbm, "traffic": None,
+                              "unit": "GB/s", "frac": achieved / hbm,
+                              "traffic": traffic / (ms / 1e3) / 1e9 if traffic else None,
+                              "traffic_bytes_per_launch": traffic,
                               "peak_source": peak_kind,
                               "algorithmic_bytes_per_cell": bytes_per_cell, "launch_ms": ms,
                               "per_kernel_ms": kt}
@@ -366,6 +369,21 @@ def main():
         print(json.dumps(result), flush=True)
     if world > 1:
         dist.destroy_process_group()
+
+
+def measured_traffic(w, name: str):
+    """DRAM bytes (read + write) of one launch of the C-ABI call `name` on workload `w`, as recorded from
+    an ncu capture in profiles/dram_traffic_<workload>_b<B>.txt (lines: <call> <kernel> <bytes>), or
+    None when no capture of this workload exists."""
+    path = os.path.join(ROOT, "profiles", f"dram_traffic_{w.name}_b{w.B}.txt")
+    if not os.path.exists(path):
+        return None
+    with open(path) as f:
+        for line in f:
+            parts = line.split()
+            if len(parts) == 3 and not line.startswith("#") and parts[0] == name:
+                return int(parts[2])
+    return None
 
 
 # Algorithmic DRAM bytes per DP cell, in units of the element size, of each timed C-ABI call:

@@ -347,13 +347,25 @@ __device__ void bwd_strip(const BwdArgs<T>& a, T* ring, T* bndring, T* sendring,
                           bool skip_publish)
 {
     Strip st;
+    T* Eb = a.E + b * a.N * a.M;
+    const int nmat = static_cast<int>(a.N - 32 * s < 32 ? a.N - 32 * s : 32);  // rows of E this strip owns
     if (!make_strip(st, a.len, b, s, a.N, a.M, a.bw, lane)) {
         if (st.bad && s == 0 && lane == 0) atomicOr(a.sy.err, kErrBadLength);
+        T* row0 = Eb + static_cast<int64_t>(32 * s) * a.M;
+        for (int r = 0; r < nmat; ++r)
+            for (int c = lane; c < a.M; c += 32) row0[r * a.M + c] = T(0);
         return;
+    }
+    // E is written in full: zeros outside the swept columns [c_begin, c_end] and in rows past the length.
+    for (int r = 0; r < nmat; ++r) {
+        T* row = Eb + static_cast<int64_t>(st.r0 + r) * a.M;
+        const int lo = r < st.rows ? st.c_begin : static_cast<int>(a.M);
+        const int hi = r < st.rows ? st.c_end : static_cast<int>(a.M);
+        for (int c = lane; c < lo; c += 32) row[c] = T(0);
+        for (int c = hi + 1 + lane; c < a.M; c += 32) row[c] = T(0);
     }
     const int64_t pitch = a.M + 2;
     const T* Rb = a.R + b * (a.N + 2) * pitch;
-    T* Eb = a.E + b * a.N * a.M;
     const int k0 = st.c_begin >> 5;
     const int k1 = (st.c_end + 31) >> 5;
     const int kmin = (st.c_begin - 1) >> 5;  // arithmetic shift: -1 when c_begin == 0
@@ -667,8 +679,6 @@ sdtw_status launch_backward(const void* R, int64_t B, int64_t N, int64_t M, cons
         return from_cuda(pair_backward<T>(static_cast<const T*>(R), static_cast<T*>(E), lx, ly, is32, B, N, M,
                                           clamp_bw(bw, N, M), gamma, W, make_sync(ws, err), g_inject_skip, stream));
     e = cudaMemsetAsync(static_cast<char*>(ws) + kHeader, 0xff, bnd_bytes(B, N, M, sizeof(T)), stream);
-    if (e != cudaSuccess) return from_cuda(e);
-    e = cudaMemsetAsync(E, 0, static_cast<size_t>(B * N * M) * sizeof(T), stream);
     if (e != cudaSuccess) return from_cuda(e);
     BwdArgs<T> a;
     a.R = static_cast<const T*>(R);
