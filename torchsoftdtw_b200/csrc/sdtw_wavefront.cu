@@ -26,7 +26,7 @@
 //   Backward: scatter form. When E[s] is final, cell s pushes E[s] * w_p to each predecessor p, where
 //             w_p = e^{-(R_p - m_s)/gamma} / sum_q e^{-(R_q - m_s)/gamma} is the softmin weight of p in
 //             the forward of s. These are the reference's exp((R[s]-R[p]-D[s])/gamma) weights
-//             (softdtw.cpp:249-257) written without the cancellation R[s]-D[s]: three exp2 and one
+//             (softdtw.cpp:248-256) written without the cancellation R[s]-D[s]: three exp2 and one
 //             reciprocal per cell, and no read of D.
 #include <algorithm>
 #include <atomic>
