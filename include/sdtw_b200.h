@@ -37,6 +37,7 @@ typedef int sdtw_status;
 #define SDTW_EDTYPE (-2)     /* unsupported dtype code */
 #define SDTW_EWORKSPACE (-3) /* workspace missing or too small */
 #define SDTW_EDEVICE (-4)    /* no usable sm_100 device / kernel image */
+#define SDTW_ETOOLARGE (-5)  /* sdtw_forward_noalloc: the problem needs more than its static scratch */
 
 #define SDTW_ERR_TIMEOUT 1u    /* a wait on a neighbouring strip's progress ran out (kernel returned early) */
 #define SDTW_ERR_BAD_LENGTH 2u /* some lengths value was outside [0, N] or [0, M] */
@@ -73,6 +74,29 @@ sdtw_status sdtw_forward(sdtw_dtype dtype, const void* D, int64_t B, int64_t N, 
                          const void* lengths_x, const void* lengths_y, int lengths_int32, double gamma,
                          int64_t bandwidth, void* R, void* costs, void* workspace, size_t workspace_bytes,
                          uint32_t* err_word, void* stream);
+
+/* ---------------------------------------------------------------------------------------------------
+ * Forward that allocates nothing (no counterpart in the reference, which always allocates its outputs
+ * and temporaries through torch).
+ * For callers that cannot allocate device memory on their hot path: a host that reaches this library
+ * through its C ABI alone and owns no device allocator (a service in another language, with no torch
+ * in the process), or one that must not call cudaMalloc there because it can synchronise the device.
+ * Same arguments, work and results as sdtw_forward, minus the workspace: the call uses a file-scope
+ * static device array of SDTW_NOALLOC_SCRATCH_BYTES (16 MiB) inside this library instead. The caller
+ * still provides D, R, costs, lengths and err_word (err_word must start at zero, as for sdtw_forward);
+ * nothing else needs to start at zero (the call resets its scratch on the stream before use).
+ *   - Limit: problems whose sdtw_forward_workspace_bytes exceeds SDTW_NOALLOC_SCRATCH_BYTES are rejected
+ *     with SDTW_ETOOLARGE before anything is enqueued (e.g. B=256, N=M=512 fp32 fits; fp64 does not).
+ *   - The first call on each device looks the scratch's address up (cudaGetSymbolAddress); make it
+ *     before any stream capture. Later calls only enqueue work.
+ *   - The scratch is shared by every call in the process on that device: calls that can overlap in time
+ *     (different streams, or different host threads without ordering) race on it and give wrong results.
+ *     Serialise them, e.g. on one stream.
+ * ------------------------------------------------------------------------------------------------- */
+#define SDTW_NOALLOC_SCRATCH_BYTES (16u << 20)
+sdtw_status sdtw_forward_noalloc(sdtw_dtype dtype, const void* D, int64_t B, int64_t N, int64_t M,
+                                 const void* lengths_x, const void* lengths_y, int lengths_int32, double gamma,
+                                 int64_t bandwidth, void* R, void* costs, uint32_t* err_word, void* stream);
 
 /* ---------------------------------------------------------------------------------------------------
  * Backward: E = d costs / d D (unscaled; the caller multiplies by the upstream gradient).

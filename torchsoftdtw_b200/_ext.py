@@ -56,6 +56,7 @@ SIGNATURES: dict[str, tuple] = {
     "sdtw_set_wait_timeout": (None, [_d]),
     "sdtw_forward_workspace_bytes": (_sz, [_i64, _i64, _i64, _i]),
     "sdtw_forward": (_i, [_i, _p, _i64, _i64, _i64, _p, _p, _i, _d, _i64, _p, _p, _p, _sz, _p, _p]),
+    "sdtw_forward_noalloc": (_i, [_i, _p, _i64, _i64, _i64, _p, _p, _i, _d, _i64, _p, _p, _p, _p]),
     "sdtw_backward_workspace_bytes": (_sz, [_i64, _i64, _i64, _i]),
     "sdtw_backward": (_i, [_i, _p, _p, _i64, _i64, _i64, _p, _p, _i, _d, _i64, _p, _p, _sz, _p, _p]),
     "sdtw_pairwise_l2": (_i, [_i, _p, _p, _i64, _i64, _i64, _i64, _p, _p, _p]),

@@ -471,6 +471,11 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32) sdtw_bwd_kernel(BwdArgs<T> 
 std::atomic<uint64_t> g_launches{0};
 void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 
+// Scratch of sdtw_forward_noalloc: one forward's workspace (launch header + strip boundary rows) as a
+// file-scope device array, so that the call allocates nothing. Its device address is looked up once per
+// device (cudaGetSymbolAddress) on the first call.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[SDTW_NOALLOC_SCRATCH_BYTES];
+
 namespace {
 
 double g_timeout_s = 2.0;
@@ -717,6 +722,9 @@ const char* sdtw_status_string(sdtw_status status)
         case SDTW_EDTYPE: return "unsupported dtype (expected SDTW_F32 or SDTW_F64)";
         case SDTW_EWORKSPACE: return "workspace missing or smaller than the *_workspace_bytes size";
         case SDTW_EDEVICE: return "no usable sm_100 device";
+        case SDTW_ETOOLARGE:
+            return "problem needs more scratch than sdtw_forward_noalloc's static scratch "
+                   "(SDTW_NOALLOC_SCRATCH_BYTES); use sdtw_forward with a workspace";
         default: break;
     }
     if (status > 0) return cudaGetErrorString(static_cast<cudaError_t>(status));
@@ -784,6 +792,44 @@ size_t sdtw_backward_workspace_bytes(int64_t B, int64_t N, int64_t M, sdtw_dtype
 {
     if (B < 0 || N < 0 || M < 0) return 0;
     return kHeader + bnd_bytes(B, N, M, elem_size(dtype));
+}
+
+/* Forward for callers that cannot allocate device memory (see the header): the workspace is the static
+ * device array g_noalloc_scratch. The first call on a device looks its address up; later calls only
+ * enqueue work. The launch resets the scratch itself (cudaMemsetAsync of the header to 0 and of the
+ * boundary rows to 0xFF), so its content between calls does not matter. */
+sdtw_status sdtw_forward_noalloc(sdtw_dtype dtype, const void* D, int64_t B, int64_t N, int64_t M,
+                                 const void* lengths_x, const void* lengths_y, int lengths_int32, double gamma,
+                                 int64_t bandwidth, void* R, void* costs, uint32_t* err_word, void* stream)
+{
+    static std::mutex mu;
+    static void* scratch[128] = {};
+    if (dtype != SDTW_F32 && dtype != SDTW_F64) return SDTW_EDTYPE;
+    if (!common_args_ok(B, N, M, gamma)) return SDTW_EINVAL;
+    if (B == 0) return SDTW_OK;
+    if (!lengths_x || !lengths_y || !R || !costs || !err_word || (N * M > 0 && !D)) return SDTW_EINVAL;
+    if (sdtw_forward_workspace_bytes(B, N, M, dtype) > SDTW_NOALLOC_SCRATCH_BYTES) return SDTW_ETOOLARGE;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return from_cuda(e);
+    if (dev < 0 || dev >= 128) return SDTW_EDEVICE;
+    void* ws = nullptr;
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        if (!scratch[dev]) {
+            void* p = nullptr;
+            e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+            if (e != cudaSuccess) return from_cuda(e);
+            scratch[dev] = p;
+        }
+        ws = scratch[dev];
+    }
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (dtype == SDTW_F32)
+        return launch_forward<float>(D, B, N, M, lengths_x, lengths_y, lengths_int32, gamma, bandwidth, R, costs, ws,
+                                     err_word, s);
+    return launch_forward<double>(D, B, N, M, lengths_x, lengths_y, lengths_int32, gamma, bandwidth, R, costs, ws,
+                                  err_word, s);
 }
 
 sdtw_status sdtw_forward(sdtw_dtype dtype, const void* D, int64_t B, int64_t N, int64_t M, const void* lengths_x,
