@@ -1,7 +1,8 @@
 """GPU: the cost-matrix and gradient kernels called through the C ABI, against fp64 numpy.
 
-* fp32 tensor-core kernels (3xTF32): D within 2e-6 of the fp64 value relative to |x|^2 + |y|^2, the
-  clamp recorded as -0.0, per-pair clamp flags consistent with the sign bits;
+* fp32 cost matrix on every path (tcgen05 tensor cores, mma.sync, CUDA cores; both tensor-core paths in
+  3xTF32): D within 2e-6 of the fp64 value relative to |x|^2 + |y|^2, the clamp recorded as -0.0,
+  per-pair clamp flags consistent with the sign bits, tiles and feature chunks cut at any size;
 * grad_X / grad_Y: against 2*g*(rowsum(G) X - G Y) in fp64 with G = E * mask, for masked and unmasked
   pairs, and for shapes that take the CUDA-core kernels.
 """
@@ -49,11 +50,22 @@ def grad(X, Y, D, E, g, flags, need_x=True, need_y=True):
 
 
 SHAPES = [(3, 130, 70, 64), (2, 64, 64, 4), (2, 33, 257, 16), (1, 300, 200, 128), (2, 5, 7, 8), (2, 128, 128, 12),
-          (1, 17, 19, 3)]
+          (1, 17, 19, 3), (2, 130, 132, 64), (3, 64, 64, 36), (2, 257, 260, 8), (1, 129, 4, 4), (1, 40, 384, 100)]
+
+# 0: chosen by shape (tcgen05 where d % 4 == 0 and M % 4 == 0), 1: mma.sync kernels, 2: CUDA-core kernels
+DISTANCE_PATHS = [0, 1, 2]
+
+
+@pytest.fixture(params=DISTANCE_PATHS)
+def distance_path(request):
+    lib = _ext.capi()
+    lib.sdtw_debug_force_distance_path(request.param)
+    yield request.param
+    lib.sdtw_debug_force_distance_path(0)
 
 
 @pytest.mark.parametrize("B,N,M,d", SHAPES)
-def test_pairwise_fp32_accuracy_and_clamp_sign(cuda, B, N, M, d):
+def test_pairwise_fp32_accuracy_and_clamp_sign(cuda, distance_path, B, N, M, d):
     g = torch.Generator().manual_seed(N * M + d)
     X = torch.randn(B, N, d, generator=g)
     Y = torch.randn(B, M, d, generator=g)
@@ -92,7 +104,7 @@ def reference_grads(X, Y, D, E, g):
 @pytest.mark.parametrize("B,N,M,d", [(2, 130, 72, 64), (3, 64, 64, 4), (1, 257, 100, 128), (2, 40, 36, 12),
                                      (2, 9, 10, 3), (2, 128, 130, 16)])
 @pytest.mark.parametrize("force_mask", [False, True])
-def test_grad_matches_fp64(cuda, B, N, M, d, force_mask):
+def test_grad_matches_fp64(cuda, distance_path, B, N, M, d, force_mask):
     gen = torch.Generator().manual_seed(B + N + M + d)
     X = torch.randn(B, N, d, generator=gen)
     Y = torch.randn(B, M, d, generator=gen)
@@ -112,3 +124,20 @@ def test_grad_matches_fp64(cuda, B, N, M, d, force_mask):
     # no flags at all: every pair is treated as possibly clamped
     gX2, _ = grad(Xc, Yc, Dc, Ec, gc, None, need_y=False)
     assert np.max(np.abs(gX2.cpu().numpy() - ex)) / scale_x < 2e-6
+
+
+def test_tensor_core_paths_agree(cuda):
+    """tcgen05 and mma.sync cost matrices of the headline shape agree to fp32 rounding."""
+    lib = _ext.capi()
+    g = torch.Generator().manual_seed(11)
+    X = torch.randn(4, 512, 64, generator=g).to(cuda)
+    Y = torch.randn(4, 512, 64, generator=g).to(cuda)
+    try:
+        D_tc, f_tc = pairwise(X, Y)
+        lib.sdtw_debug_force_distance_path(1)
+        D_mma, f_mma = pairwise(X, Y)
+    finally:
+        lib.sdtw_debug_force_distance_path(0)
+    scale = (X * X).sum(-1)[:, :, None] + (Y * Y).sum(-1)[:, None, :]
+    assert float(((D_tc - D_mma).abs() / scale).max()) < 2e-6
+    assert torch.equal(f_tc, f_mma)

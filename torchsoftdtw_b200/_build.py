@@ -6,7 +6,8 @@
 * ``_C<ext>.so`` — the PyTorch operator layer (``csrc/torch_ops.cpp``), compiled by the host C++
   compiler against libtorch and linked to ``lib/libsdtw_b200.so`` through ``$ORIGIN/lib``.
 
-Both are rebuilt only when a source is newer than the output. Run ``python -m torchsoftdtw_b200._build``.
+Both are rebuilt only when a source is newer than the output. Run ``python torchsoftdtw_b200/_build.py`` (as a
+file: importing the package would load the libraries it builds).
 """
 
 from __future__ import annotations

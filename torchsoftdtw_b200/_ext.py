@@ -31,7 +31,7 @@ def load() -> None:
         raise ImportError(
             "torchsoftdtw_b200: native libraries are not built (missing: "
             + ", ".join(missing)
-            + "). Build them with `python -m torchsoftdtw_b200._build` (needs nvcc for sm_100a)."
+            + "). Build them with `python torchsoftdtw_b200/_build.py` (needs nvcc for sm_100a)."
         )
     torch.ops.load_library(_build.ops_lib_path())
     _loaded = True
@@ -68,6 +68,7 @@ DEBUG_SIGNATURES: dict[str, tuple] = {
     "sdtw_debug_force_path": (None, [_i]),
     "sdtw_debug_set_pair_warps": (None, [_i]),
     "sdtw_debug_kernel_launches": (ctypes.c_uint64, []),
+    "sdtw_debug_force_distance_path": (None, [_i]),
 }
 
 

@@ -11,6 +11,8 @@ namespace sdtw {
 // Kernel launches made by this library in this process (all entry points; read by
 // sdtw_debug_kernel_launches). Defined in sdtw_wavefront.cu.
 void count_launch();
+// Upper bound (seconds) of every device-side wait (sdtw_set_wait_timeout). Defined in sdtw_wavefront.cu.
+double wait_timeout_s();
 
 // --------------------------------------------------------------------------------------------------
 // Tiling constants of the strip wavefront.

@@ -12,6 +12,7 @@
 
 #include "sdtw_common.cuh"
 #include "sdtw_b200.h"
+#include "sdtw_tcgen05.h"
 
 namespace sdtw {
 
@@ -466,12 +467,22 @@ __global__ void __launch_bounds__(256, 2) grad_x_mma_kernel(const float* __restr
 namespace {
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
+int g_distance_path = 0;  // 0: automatic, 1: mma.sync kernels (no tcgen05), 2: CUDA-core kernels only
+
 template <typename T>
 sdtw_status launch_pairwise(const void* X, const void* Y, int64_t B, int64_t N, int64_t M, int64_t d, void* D,
                             int* clamp_flags, cudaStream_t s)
 {
     if constexpr (sizeof(T) == 4) {
-        if (d % 4 == 0 && aligned16(X) && aligned16(Y)) {
+        if (g_distance_path == 0 && pairwise_tc_supported(X, Y, D, B, N, M, d)) {
+            const cudaError_t e = pairwise_tc_launch(static_cast<const float*>(X), static_cast<const float*>(Y),
+                                                     static_cast<float*>(D), clamp_flags, B, N, M, d,
+                                                     wait_timeout_s(), s);
+            return e == cudaSuccess ? SDTW_OK : static_cast<sdtw_status>(e);
+        }
+    }
+    if constexpr (sizeof(T) == 4) {
+        if (g_distance_path != 2 && d % 4 == 0 && aligned16(X) && aligned16(Y)) {
             static bool attr_set = false;
             if (!attr_set) {
                 const cudaError_t e = cudaFuncSetAttribute(pairwise_l2_mma_kernel,
@@ -507,7 +518,8 @@ sdtw_status launch_grad(const void* X, const void* Y, const void* D, const void*
     const unsigned cblocks = static_cast<unsigned>((d + kTile - 1) / kTile);
     bool gx_done = false;
     if constexpr (sizeof(T) == 4) {
-        if (gX && d % 4 == 0 && M % 4 == 0 && aligned16(X) && aligned16(Y) && aligned16(E) && aligned16(gX)) {
+        if (g_distance_path != 2 && gX && d % 4 == 0 && M % 4 == 0 && aligned16(X) && aligned16(Y) && aligned16(E) &&
+            aligned16(gX)) {
             static bool attr_set = false;
             if (!attr_set) {
                 const cudaError_t e = cudaFuncSetAttribute(grad_x_mma_kernel,
@@ -555,6 +567,10 @@ bool sizes_ok(int64_t B, int64_t N, int64_t M, int64_t d)
 using namespace sdtw;
 
 extern "C" {
+
+/* Test hook (not in the public header): 0 chooses the cost-matrix kernel by shape (tcgen05 where
+ * supported), 1 forces the mma.sync kernels, 2 the CUDA-core kernels. */
+void sdtw_debug_force_distance_path(int path) { g_distance_path = (path >= 0 && path <= 2) ? path : 0; }
 
 sdtw_status sdtw_pairwise_l2(sdtw_dtype dtype, const void* X, const void* Y, int64_t B, int64_t N, int64_t M,
                              int64_t d, void* D, int* clamp_flags, void* stream)

@@ -1,0 +1,22 @@
+// Tensor-core (tcgen05) kernels: host entry points used by the C ABI in sdtw_distance.cu.
+#pragma once
+
+#include <cstdint>
+
+#include <cuda_runtime.h>
+
+namespace sdtw {
+
+// Whether the tcgen05 cost-matrix kernel handles these fp32 arguments (TMA needs 16-byte aligned bases
+// and rows, hence d % 4 == 0 and M % 4 == 0).
+bool pairwise_tc_supported(const void* X, const void* Y, const void* D, int64_t B, int64_t N, int64_t M, int64_t d);
+
+// D = clamp(|x|^2 + |y|^2 - 2 X Y^T) for fp32 X (B,N,d), Y (B,M,d); clamp_flags (optional) as for
+// sdtw_pairwise_l2. Every wait in the kernel is bounded by timeout_s.
+cudaError_t pairwise_tc_launch(const float* X, const float* Y, float* D, int* clamp_flags, int64_t B, int64_t N,
+                               int64_t M, int64_t d, double timeout_s, cudaStream_t s);
+
+// Reads and clears the tensor-core kernels' error bits (1: a wait ran out and a tile was written as NaN).
+cudaError_t read_distance_errors(uint32_t& bits);
+
+}  // namespace sdtw

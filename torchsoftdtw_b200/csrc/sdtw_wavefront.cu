@@ -35,6 +35,7 @@
 
 #include "sdtw_b200.h"
 #include "sdtw_pairwave.h"
+#include "sdtw_tcgen05.h"
 #include "sdtw_strip.cuh"
 
 namespace sdtw {
@@ -477,8 +478,12 @@ void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 static __device__ __align__(256) unsigned char g_noalloc_scratch[SDTW_NOALLOC_SCRATCH_BYTES];
 
 namespace {
-
 double g_timeout_s = 2.0;
+}  // namespace
+double wait_timeout_s() { return g_timeout_s; }
+
+namespace {
+
 int g_inject_skip = -1;  // set only through sdtw_debug_inject_stall (tests of the failure path)
 int g_force_path = 0;    // 0: automatic, 1: strip-ticket kernels, 2: pair-resident kernels
 int g_pair_warps = kPairMaxWarps;  // warps per CTA of the pair-resident kernels (upper bound)
@@ -759,7 +764,11 @@ uint32_t sdtw_read_error_word(uint32_t* err_word, void* stream)
     if (cudaStreamSynchronize(s) != cudaSuccess) return 0xffffffffu;
     if (v != 0 && cudaMemsetAsync(err_word, 0, 4, s) != cudaSuccess) return 0xffffffffu;
     if (cudaStreamSynchronize(s) != cudaSuccess) return 0xffffffffu;
-    return v;
+    // The tensor-core cost kernel has no caller error word: its timeouts live in the library's own device
+    // word and are reported here as SDTW_ERR_TIMEOUT.
+    uint32_t tc = 0;
+    if (read_distance_errors(tc) != cudaSuccess) return 0xffffffffu;
+    return v | (tc ? SDTW_ERR_TIMEOUT : 0u);
 }
 
 void sdtw_set_wait_timeout(double seconds)
