@@ -518,7 +518,17 @@ sdtw_status launch_grad(const void* X, const void* Y, const void* D, const void*
     const unsigned cblocks = static_cast<unsigned>((d + kTile - 1) / kTile);
     bool gx_done = false;
     if constexpr (sizeof(T) == 4) {
-        if (g_distance_path != 2 && gX && d % 4 == 0 && M % 4 == 0 && aligned16(X) && aligned16(Y) && aligned16(E) &&
+        if (g_distance_path == 0 && gX && grad_tc_supported(X, Y, D, E, gX, B, N, M, d)) {
+            const cudaError_t e = grad_x_tc_launch(static_cast<const float*>(X), static_cast<const float*>(Y),
+                                                   static_cast<const float*>(D), static_cast<const float*>(E),
+                                                   static_cast<const float*>(g), clamp_flags, static_cast<float*>(gX),
+                                                   B, N, M, d, wait_timeout_s(), s);
+            if (e != cudaSuccess) return static_cast<sdtw_status>(e);
+            gx_done = true;
+        }
+    }
+    if constexpr (sizeof(T) == 4) {
+        if (!gx_done && g_distance_path != 2 && gX && d % 4 == 0 && M % 4 == 0 && aligned16(X) && aligned16(Y) && aligned16(E) &&
             aligned16(gX)) {
             static bool attr_set = false;
             if (!attr_set) {

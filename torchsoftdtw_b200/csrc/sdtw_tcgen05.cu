@@ -284,6 +284,404 @@ __global__ void __launch_bounds__(128) pairwise_l2_tc_kernel(const __grid_consta
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
 }
 
+// ==================================================================================================
+// grad_X = 2 g[b] (rowsum(G) X - G Y), G = E masked by the clamp of the cost matrix, on tcgen05.
+//
+// A tile is 128 rows of grad_X (UMMA M) x all features; its K loop runs over the columns j of E in chunks
+// of 32. The B operand is [Y | 1]: DPAD features (d <= 128 padded to 16/32/64/96/128) and 16 more rows,
+// the first all ones, so the accumulator's column DPAD is rowsum(G). The kernel is persistent (tiles
+// blockIdx.x, blockIdx.x + gridDim.x, ...; chunks numbered q = 0, 1, ... across them) and its warps
+// specialise, communicating only through mbarriers:
+//   * warp 0 (TMA): E[128 rows x 32 columns] (128-byte swizzled) and Y[32 rows x DPAD] (plain boxes) of
+//     chunk q into raw stage q % S;
+//   * warps 2..9 (split, 256 threads): zero the clamped cells of E in flagged pairs (sign bit of D), split
+//     E into TF32 head | tail (3xTF32) in place of the 128-byte swizzled rows of split buffer q % P, and
+//     transpose + split Y into its K-major rows; release the raw stage and mark the split buffer full;
+//   * warp 1 (MMA): 3 x 4 tcgen05.mma kind::tf32 per chunk into accumulator (tile & 1) in tensor memory,
+//     commit to the split buffer's "empty" barrier, and after a tile's last chunk to the accumulator's
+//     "full" barrier;
+//   * warps 10..13 (epilogue): read their 32 accumulator lanes (rows) with tcgen05.ld and write grad_X
+//     rows; the accumulator is double-buffered, so this overlaps the next tile's MMAs.
+// Every wait is bounded in time. A wait that runs out raises an abort word in shared memory that every
+// role polls, sets bit 1 of the library's distance error word, and the epilogue writes NaN into the rows
+// it has not finished; the TMA and MMA warps wait (bounded) for their own operations before the CTA
+// releases its tensor memory.
+// ==================================================================================================
+constexpr int kGT = 128;                    // grad_X rows per tile (UMMA M)
+constexpr int kGKC = 32;                    // columns of E per chunk (one 128-byte swizzle atom of fp32)
+constexpr int kEChunk = kGT * kGKC * 4;     // 16 KB
+constexpr int kGradSplitWarps = 16;
+constexpr int kGradSplitThreads = 32 * kGradSplitWarps;
+constexpr int kGradThreads = 32 * (2 + kGradSplitWarps + 4);  // TMA, MMA, split, epilogue
+constexpr int kGradEpiWarp0 = 2 + kGradSplitWarps;
+constexpr int kGradSmemBudget = 218 * 1024;
+
+template <int DPAD>
+struct GradGeom {
+    static constexpr int NB = DPAD + 16;                                    // UMMA N: features + ones block
+    static constexpr int YB = DPAD < 32 ? DPAD : 32;                        // features per Y box
+    static constexpr int NBOX = DPAD / YB;
+    static constexpr int YRAW = DPAD * 128;                                 // raw Y: 32 K rows x DPAD fp32
+    static constexpr int YT = NB * 128;                                     // Y^T (one of head / tail)
+    static constexpr int RAW = kEChunk + YRAW;                              // one raw stage
+    static constexpr int SPL = 2 * kEChunk + 2 * YT;                        // E head, E tail, Y^T head, Y^T tail
+    static constexpr int P = 2;                                             // split buffers
+    static constexpr int S0 = (kGradSmemBudget - P * SPL) / RAW;
+    static constexpr int S = S0 > 4 ? 4 : S0;                               // raw stages
+    static constexpr int OFF_SPL = S * RAW;
+    static constexpr int OFF_BAR = OFF_SPL + P * SPL;
+    // barriers: raw_full[S], raw_empty[S], spl_full[P], spl_empty[P], acc_full[2], acc_empty[2]
+    static constexpr int NBAR = 2 * S + 2 * P + 4;
+    static constexpr int OFF_TMEM = OFF_BAR + 8 * NBAR;
+    static constexpr int OFF_ABORT = OFF_TMEM + 8;
+    static constexpr int BYTES = OFF_ABORT + 8 + 1024;                      // + slack to align the base
+    static constexpr uint32_t ACC_COLS = NB <= 32 ? 32u : (NB <= 64 ? 64u : (NB <= 128 ? 128u : 256u));
+    static constexpr uint32_t TMEM_COLS = 2 * ACC_COLS;
+    // Y split: TPN threads per feature, KPER consecutive K rows each (whole 16-byte units).
+    static constexpr int TPN = DPAD * 8 <= kGradSplitThreads ? 8 : (DPAD * 4 <= kGradSplitThreads ? 4 : 2);
+    static constexpr int KPER = kGKC / TPN;
+    static constexpr uint32_t IDESC = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t(NB) >> 3) << 17) |
+                                      ((uint32_t(kGT) >> 4) << 24);
+    static_assert(S >= 2, "grad_X tensor-core kernel: fewer than two raw stages fit");
+    static_assert(DPAD % 16 == 0 && NB <= 256, "UMMA N");
+    static_assert(BYTES <= 227 * 1024, "shared memory");
+};
+
+__device__ __forceinline__ void umma_tf32_id(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc,
+                                             uint32_t accumulate)
+{
+    asm volatile(
+        "{ .reg .pred p; setp.ne.b32 p, %4, 0; "
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, {%5, %6, %7, %8}, p; }" ::"r"(tmem_d),
+        "l"(da), "l"(db), "r"(idesc), "r"(accumulate), "r"(0u), "r"(0u), "r"(0u), "r"(0u)
+        : "memory");
+}
+
+// 16 consecutive fp32 accumulator columns of this thread's lane (no wait).
+__device__ __forceinline__ void tmem_ld16_nowait(uint32_t taddr, float* v)
+{
+    uint32_t r[16];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, "
+        "%14, %15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ float4 split_hi(float4 v)
+{
+    return make_float4(to_tf32(v.x), to_tf32(v.y), to_tf32(v.z), to_tf32(v.w));
+}
+__device__ __forceinline__ float4 split_lo(float4 v, float4 h)
+{
+    return make_float4(to_tf32(v.x - h.x), to_tf32(v.y - h.y), to_tf32(v.z - h.z), to_tf32(v.w - h.w));
+}
+
+__device__ __forceinline__ void mbar_arrive(uint32_t bar)
+{
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+// Bounded wait that also gives up when another role of the CTA raised the abort word. On its own
+// timeout it raises the abort word and the library's distance error bit.
+__device__ __forceinline__ bool wait_role(uint32_t bar, uint32_t parity, uint64_t timeout_ns, volatile int* abort)
+{
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = global_ns();
+    unsigned ns = 32;
+    while (true) {
+#pragma unroll 1
+        for (int i = 0; i < 4; ++i)
+            if (mbar_try_wait(bar, parity)) return true;
+        __nanosleep(ns);  // back off: waiting warps leave the issue slots to the working ones
+        ns = ns < 512 ? 2 * ns : 512;
+        if (*abort) return false;
+        if (global_ns() - t0 > timeout_ns) {
+            *abort = 1;
+            atomicOr(&g_distance_err, 1u);
+            return false;
+        }
+    }
+}
+
+struct GradTcArgs {
+    const float* X;
+    const float* D;
+    const float* g;
+    const int* clamp_flags;  // may be null: every pair is masked
+    float* out;
+    int B, N, M, d;
+    int nrt;                 // row tiles per pair
+    int nk;                  // chunks per tile
+    unsigned long long timeout_ns;
+};
+
+template <int DPAD>
+__global__ void __launch_bounds__(kGradThreads, 1) grad_x_tc_kernel(const __grid_constant__ CUtensorMap me,
+                                                                    const __grid_constant__ CUtensorMap my,
+                                                                    GradTcArgs a)
+{
+    using G = GradGeom<DPAD>;
+    extern __shared__ unsigned char smem_raw[];
+    const uint32_t raw0 = smem_addr(smem_raw);
+    unsigned char* sm = smem_raw + ((1024u - (raw0 & 1023u)) & 1023u);
+    const uint32_t base = smem_addr(sm);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const uint32_t raw_full = base + G::OFF_BAR;
+    const uint32_t raw_empty = raw_full + 8 * G::S;
+    const uint32_t spl_full = raw_empty + 8 * G::S;
+    const uint32_t spl_empty = spl_full + 8 * G::P;
+    const uint32_t acc_full = spl_empty + 8 * G::P;
+    const uint32_t acc_empty = acc_full + 16;
+    volatile int* abort = reinterpret_cast<volatile int*>(sm + G::OFF_ABORT);
+
+    const int ntiles = a.B * a.nrt;
+    const int my_tiles = blockIdx.x < static_cast<unsigned>(ntiles)
+                             ? (ntiles - 1 - static_cast<int>(blockIdx.x)) / static_cast<int>(gridDim.x) + 1
+                             : 0;
+    if (tid == 0) {
+        for (int s = 0; s < G::S; ++s) {
+            mbar_init(raw_full + 8 * s, 1);
+            mbar_init(raw_empty + 8 * s, kGradSplitWarps);
+        }
+        for (int p = 0; p < G::P; ++p) {
+            mbar_init(spl_full + 8 * p, kGradSplitWarps);
+            mbar_init(spl_empty + 8 * p, 1);
+        }
+        for (int c = 0; c < 2; ++c) {
+            mbar_init(acc_full + 8 * c, 1);
+            mbar_init(acc_empty + 8 * c, 4);
+        }
+        *abort = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    // The ones block of [Y | 1]^T in every split buffer: row DPAD of the head all ones, rows DPAD+1..NB-1
+    // of the head and all 16 rows of the tail zero (written once; the split only writes rows < DPAD).
+    for (int e = tid; e < G::P * 16 * 32; e += kGradThreads) {
+        const int p = e / (16 * 32), r = (e / 32) % 16, k = e % 32;
+        float* yh = reinterpret_cast<float*>(sm + G::OFF_SPL + p * G::SPL + 2 * kEChunk + 128 * (DPAD + r));
+        yh[k] = r == 0 ? 1.f : 0.f;
+        yh[G::YT / 4 + k] = 0.f;
+    }
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(base + G::OFF_TMEM),
+                     "r"(G::TMEM_COLS)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(sm + G::OFF_TMEM);
+
+    if (warp == 0) {
+        // ---------------- TMA producer ----------------
+        if (lane == 0) {
+            const int Q = my_tiles * a.nk;  // chunks of this CTA
+            int issued = 0;
+            for (int q = 0; q < Q; ++q) {
+                const int s = q % G::S;
+                if (q >= G::S && !wait_role(raw_empty + 8 * s, ((q / G::S) - 1) & 1, a.timeout_ns, abort)) break;
+                const int t = static_cast<int>(blockIdx.x) + (q / a.nk) * static_cast<int>(gridDim.x);
+                const int b = t / a.nrt, rt = t % a.nrt, kc = q % a.nk;
+                const uint32_t dst = base + s * G::RAW;
+                mbar_expect_tx(raw_full + 8 * s, G::RAW);
+                tma_load_3d(dst, &me, raw_full + 8 * s, kc * kGKC, rt * kGT, b);
+#pragma unroll
+                for (int bx = 0; bx < G::NBOX; ++bx)
+                    tma_load_3d(dst + kEChunk + bx * (kGKC * G::YB * 4), &my, raw_full + 8 * s, bx * G::YB,
+                                kc * kGKC, b);
+                issued = q + 1;
+            }
+            // Before the CTA ends: every load issued into each stage has landed (the last one per stage
+            // completes after all earlier ones, which the split released).
+            for (int q = issued - G::S < 0 ? 0 : issued - G::S; q < issued; ++q)
+                (void)mbar_wait(raw_full + 8 * (q % G::S), (q / G::S) & 1, a.timeout_ns);
+        }
+    } else if (warp == 1) {
+        // ---------------- MMA issuer ----------------
+        if (lane == 0) {
+            int q = 0;
+            int last_commit_bar = -1;
+            uint32_t last_commit_parity = 0;
+            bool ok = true;
+            for (int tl = 0; tl < my_tiles && ok; ++tl) {
+                const int ab = tl & 1;
+                if (tl >= 2 && !wait_role(acc_empty + 8 * ab, ((tl >> 1) - 1) & 1, a.timeout_ns, abort)) break;
+                const uint32_t acc = tmem + static_cast<uint32_t>(ab) * G::ACC_COLS;
+                for (int kc = 0; kc < a.nk; ++kc, ++q) {
+                    const int p = q % G::P;
+                    if (!wait_role(spl_full + 8 * p, (q / G::P) & 1, a.timeout_ns, abort)) {
+                        ok = false;
+                        break;
+                    }
+                    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                    const uint32_t sb = base + G::OFF_SPL + p * G::SPL;
+                    const uint64_t ah = sw128_desc(sb), al = sw128_desc(sb + kEChunk);
+                    const uint64_t bh = sw128_desc(sb + 2 * kEChunk), bl = sw128_desc(sb + 2 * kEChunk + G::YT);
+#pragma unroll
+                    for (int kk = 0; kk < kGKC / 8; ++kk) {
+                        const uint64_t st = static_cast<uint64_t>((kk * 32) >> 4);  // 8 TF32 = 32 bytes along K
+                        umma_tf32_id(acc, ah + st, bh + st, G::IDESC, (kc > 0 || kk > 0) ? 1u : 0u);
+                        umma_tf32_id(acc, ah + st, bl + st, G::IDESC, 1u);
+                        umma_tf32_id(acc, al + st, bh + st, G::IDESC, 1u);
+                    }
+                    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                                     spl_empty + 8 * p)
+                                 : "memory");
+                    last_commit_bar = 0;
+                    last_commit_parity = static_cast<uint32_t>((q / G::P) & 1);
+                    if (kc == a.nk - 1) {
+                        asm volatile(
+                            "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                                acc_full + 8 * ab)
+                            : "memory");
+                    }
+                }
+                if (ok && q > 0) last_commit_bar = 1 + (q - 1) % G::P;
+            }
+            // Before the CTA ends: the last MMAs have completed (their commit arrived).
+            if (q > 0) {
+                const int ql = q - 1;
+                (void)mbar_wait(spl_empty + 8 * (ql % G::P), (ql / G::P) & 1, a.timeout_ns);
+            }
+            (void)last_commit_bar;
+            (void)last_commit_parity;
+        }
+    } else if (warp < kGradEpiWarp0) {
+        // ---------------- split ----------------
+        constexpr int EU = 8 * kGT / kGradSplitThreads;  // E units (16 bytes) per split thread
+        const int st = tid - 64;                          // 0 .. kGradSplitThreads - 1
+        const int er = st & (kGT - 1), eu0 = (st >> 7) * EU;  // E: row er, logical units eu0 .. eu0+EU-1
+        const bool y_active = st < DPAD * G::TPN;
+        const int yn = st % DPAD, yh = st / DPAD;         // Y: feature yn, K units [yh*KPER/4, ...)
+        int q = 0;
+        for (int tl = 0; tl < my_tiles; ++tl) {
+            const int t = static_cast<int>(blockIdx.x) + tl * static_cast<int>(gridDim.x);
+            const int b = t / a.nrt, rt = t % a.nrt;
+            const int i_e = rt * kGT + er;
+            const bool masked = (a.clamp_flags == nullptr || a.clamp_flags[b] != 0) && i_e < a.N;
+            const float* Drow = a.D + (static_cast<int64_t>(b) * a.N + (i_e < a.N ? i_e : 0)) * a.M;
+            bool ok = true;
+            for (int kc = 0; kc < a.nk; ++kc, ++q) {
+                const int s = q % G::S, p = q % G::P;
+                if (!wait_role(raw_full + 8 * s, (q / G::S) & 1, a.timeout_ns, abort) ||
+                    (q >= G::P && !wait_role(spl_empty + 8 * p, ((q / G::P) - 1) & 1, a.timeout_ns, abort))) {
+                    ok = false;
+                    break;
+                }
+                const unsigned char* raw = sm + s * G::RAW;
+                unsigned char* spl = sm + G::OFF_SPL + p * G::SPL;
+                const int j0 = kc * kGKC;
+#pragma unroll
+                for (int w = 0; w < EU; ++w) {
+                    const int lu = eu0 + w;
+                    const int off = 128 * er + 16 * (lu ^ (er & 7));
+                    float4 v = *reinterpret_cast<const float4*>(raw + off);
+                    if (masked) {
+                        const int j = j0 + 4 * lu;  // M % 4 == 0: the four columns are all in or all out
+                        if (j < a.M) {
+                            const float4 dv = __ldg(reinterpret_cast<const float4*>(Drow + j));
+                            if (signbit(dv.x)) v.x = 0.f;
+                            if (signbit(dv.y)) v.y = 0.f;
+                            if (signbit(dv.z)) v.z = 0.f;
+                            if (signbit(dv.w)) v.w = 0.f;
+                        }
+                    }
+                    const float4 h = split_hi(v);
+                    *reinterpret_cast<float4*>(spl + off) = h;
+                    *reinterpret_cast<float4*>(spl + kEChunk + off) = split_lo(v, h);
+                }
+                if (y_active) {
+                    const float* yr =
+                        reinterpret_cast<const float*>(raw + kEChunk + (yn / G::YB) * (kGKC * G::YB * 4)) + (yn % G::YB);
+                    unsigned char* yhb = spl + 2 * kEChunk + 128 * yn;
+#pragma unroll
+                    for (int u = 0; u < G::KPER / 4; ++u) {
+                        const int lu = yh * (G::KPER / 4) + u;
+                        float4 v;
+                        v.x = yr[(4 * lu + 0) * G::YB];
+                        v.y = yr[(4 * lu + 1) * G::YB];
+                        v.z = yr[(4 * lu + 2) * G::YB];
+                        v.w = yr[(4 * lu + 3) * G::YB];
+                        const float4 h = split_hi(v);
+                        const int off = 16 * (lu ^ (yn & 7));
+                        *reinterpret_cast<float4*>(yhb + off) = h;
+                        *reinterpret_cast<float4*>(yhb + G::YT + off) = split_lo(v, h);
+                    }
+                }
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> tensor-core reads
+                __syncwarp();
+                if (lane == 0) {
+                    mbar_arrive(raw_empty + 8 * s);
+                    mbar_arrive(spl_full + 8 * p);
+                }
+            }
+            if (!ok) break;
+        }
+    } else {
+        // ---------------- epilogue ----------------
+        const int row = 32 * (warp & 3) + lane;  // accumulator lane of this thread
+        int tl = 0;
+        for (; tl < my_tiles; ++tl) {
+            const int ab = tl & 1;
+            if (!wait_role(acc_full + 8 * ab, (tl >> 1) & 1, a.timeout_ns, abort)) break;
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            const int t = static_cast<int>(blockIdx.x) + tl * static_cast<int>(gridDim.x);
+            const int b = t / a.nrt, i = (t % a.nrt) * kGT + row;
+            const uint32_t acc = tmem + (static_cast<uint32_t>(32 * (warp & 3)) << 16) +
+                                 static_cast<uint32_t>(ab) * G::ACC_COLS;
+            float v[16];
+            tmem_ld16_nowait(acc + DPAD, v);  // column DPAD: rowsum(G)
+            asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+            const float rsum = v[0];
+            const float g2 = 2.f * a.g[b];
+            const float* xr = a.X + (static_cast<int64_t>(b) * a.N + (i < a.N ? i : 0)) * a.d;
+            float* orow = a.out + (static_cast<int64_t>(b) * a.N + i) * a.d;
+#pragma unroll
+            for (int c0 = 0; c0 < DPAD; c0 += 16) {
+                tmem_ld16_nowait(acc + c0, v);
+                asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+                if (i < a.N) {
+#pragma unroll
+                    for (int e = 0; e < 16; e += 4) {
+                        const int n = c0 + e;
+                        if (n < a.d) {
+                            const float4 xv = __ldg(reinterpret_cast<const float4*>(xr + n));
+                            float4 o;
+                            o.x = g2 * (rsum * xv.x - v[e]);
+                            o.y = g2 * (rsum * xv.y - v[e + 1]);
+                            o.z = g2 * (rsum * xv.z - v[e + 2]);
+                            o.w = g2 * (rsum * xv.w - v[e + 3]);
+                            *reinterpret_cast<float4*>(orow + n) = o;
+                        }
+                    }
+                }
+            }
+            asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+            __syncwarp();
+            if (lane == 0) mbar_arrive(acc_empty + 8 * ab);
+        }
+        // Rows of tiles not finished (a wait ran out): NaN.
+        for (; tl < my_tiles; ++tl) {
+            const int t = static_cast<int>(blockIdx.x) + tl * static_cast<int>(gridDim.x);
+            const int b = t / a.nrt, i = (t % a.nrt) * kGT + row;
+            if (i < a.N)
+                for (int n = 0; n < a.d; ++n)
+                    a.out[(static_cast<int64_t>(b) * a.N + i) * a.d + n] = __int_as_float(0x7fc00000);
+        }
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    if (warp == 1)
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(G::TMEM_COLS)
+                     : "memory");
+}
+
 // ---- host -------------------------------------------------------------------------------------------
 std::mutex g_tc_mu;
 PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
@@ -304,22 +702,108 @@ cudaError_t get_encode(PFN_cuTensorMapEncodeTiled_v12000& fn)
     return cudaSuccess;
 }
 
-// 3-D tensor map of a (batch, rows, cols) fp32 array, box of 32 columns x 128 rows x 1, 128-byte swizzle.
-bool make_map(PFN_cuTensorMapEncodeTiled_v12000 encode, CUtensorMap* map, const void* ptr, int64_t B,
-              int64_t rows, int64_t cols)
+// 3-D tensor map of a (batch, rows, cols) fp32 array with a box of box_cols x box_rows x 1. Elements
+// outside the array read as zero.
+bool make_map_box(PFN_cuTensorMapEncodeTiled_v12000 encode, CUtensorMap* map, const void* ptr, int64_t B,
+                  int64_t rows, int64_t cols, int box_cols, int box_rows, CUtensorMapSwizzle swizzle)
 {
     const cuuint64_t dims[3] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows),
                                 static_cast<cuuint64_t>(B)};
     const cuuint64_t strides[2] = {static_cast<cuuint64_t>(cols) * 4, static_cast<cuuint64_t>(rows * cols) * 4};
-    const cuuint32_t box[3] = {static_cast<cuuint32_t>(kKC), static_cast<cuuint32_t>(kT), 1};
+    const cuuint32_t box[3] = {static_cast<cuuint32_t>(box_cols), static_cast<cuuint32_t>(box_rows), 1};
     const cuuint32_t estr[3] = {1, 1, 1};
     const CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<void*>(ptr), dims, strides, box,
-                              estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                              estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS;
 }
 
+// Box of 32 columns x 128 rows, 128-byte swizzle (the operand tiles of both tensor-core kernels).
+bool make_map(PFN_cuTensorMapEncodeTiled_v12000 encode, CUtensorMap* map, const void* ptr, int64_t B,
+              int64_t rows, int64_t cols)
+{
+    return make_map_box(encode, map, ptr, B, rows, cols, kKC, kT, CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+int g_sm_count[128] = {};
+bool g_grad_attr_set[128][5] = {};
+
+template <int DPAD>
+cudaError_t grad_tc_launch_t(const float* X, const float* Y, const float* D, const float* E, const float* g,
+                             const int* clamp_flags, float* gX, int64_t B, int64_t N, int64_t M, int64_t d,
+                             double timeout_s, cudaStream_t s, int dev, int slot,
+                             PFN_cuTensorMapEncodeTiled_v12000 encode)
+{
+    using G = GradGeom<DPAD>;
+    {
+        std::lock_guard<std::mutex> lock(g_tc_mu);
+        if (!g_grad_attr_set[dev][slot]) {
+            const cudaError_t e = cudaFuncSetAttribute(grad_x_tc_kernel<DPAD>,
+                                                       cudaFuncAttributeMaxDynamicSharedMemorySize, G::BYTES);
+            if (e != cudaSuccess) return e;
+            g_grad_attr_set[dev][slot] = true;
+        }
+    }
+    CUtensorMap me, my;
+    if (!make_map(encode, &me, E, B, N, M) ||
+        !make_map_box(encode, &my, Y, B, M, d, G::YB, kGKC, CU_TENSOR_MAP_SWIZZLE_NONE))
+        return cudaErrorInvalidValue;
+    GradTcArgs a;
+    a.X = X;
+    a.D = D;
+    a.g = g;
+    a.clamp_flags = clamp_flags;
+    a.out = gX;
+    a.B = static_cast<int>(B);
+    a.N = static_cast<int>(N);
+    a.M = static_cast<int>(M);
+    a.d = static_cast<int>(d);
+    a.nrt = static_cast<int>((N + kGT - 1) / kGT);
+    a.nk = static_cast<int>((M + kGKC - 1) / kGKC);
+    a.timeout_ns = static_cast<unsigned long long>(timeout_s * 1e9);
+    const int64_t tiles = B * a.nrt;
+    const int grid = static_cast<int>(tiles < g_sm_count[dev] ? tiles : g_sm_count[dev]);
+    count_launch();
+    grad_x_tc_kernel<DPAD><<<grid, kGradThreads, G::BYTES, s>>>(me, my, a);
+    return cudaGetLastError();
+}
+
 }  // namespace
+
+bool grad_tc_supported(const void* X, const void* Y, const void* D, const void* E, const void* gX, int64_t B,
+                       int64_t N, int64_t M, int64_t d)
+{
+    const auto al = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+    return d >= 1 && d <= 128 && d % 4 == 0 && M % 4 == 0 && N >= 1 && M >= 1 && al(X) && al(Y) && al(D) &&
+           al(E) && al(gX) && N < (1 << 30) && M < (1 << 30) && B >= 1 && B * ((N + kGT - 1) / kGT) < (1ll << 31);
+}
+
+cudaError_t grad_x_tc_launch(const float* X, const float* Y, const float* D, const float* E, const float* g,
+                             const int* clamp_flags, float* gX, int64_t B, int64_t N, int64_t M, int64_t d,
+                             double timeout_s, cudaStream_t s)
+{
+    PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
+    cudaError_t e = get_encode(encode);
+    if (e != cudaSuccess) return e;
+    int dev = 0;
+    e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= 128) return cudaErrorInvalidDevice;
+    {
+        std::lock_guard<std::mutex> lock(g_tc_mu);
+        if (g_sm_count[dev] == 0) {
+            int n = 0;
+            e = cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+            if (e != cudaSuccess) return e;
+            g_sm_count[dev] = n > 0 ? n : 1;
+        }
+    }
+    if (d <= 16) return grad_tc_launch_t<16>(X, Y, D, E, g, clamp_flags, gX, B, N, M, d, timeout_s, s, dev, 0, encode);
+    if (d <= 32) return grad_tc_launch_t<32>(X, Y, D, E, g, clamp_flags, gX, B, N, M, d, timeout_s, s, dev, 1, encode);
+    if (d <= 64) return grad_tc_launch_t<64>(X, Y, D, E, g, clamp_flags, gX, B, N, M, d, timeout_s, s, dev, 2, encode);
+    if (d <= 96) return grad_tc_launch_t<96>(X, Y, D, E, g, clamp_flags, gX, B, N, M, d, timeout_s, s, dev, 3, encode);
+    return grad_tc_launch_t<128>(X, Y, D, E, g, clamp_flags, gX, B, N, M, d, timeout_s, s, dev, 4, encode);
+}
 
 bool pairwise_tc_supported(const void* X, const void* Y, const void* D, int64_t B, int64_t N, int64_t M, int64_t d)
 {

@@ -16,6 +16,17 @@ bool pairwise_tc_supported(const void* X, const void* Y, const void* D, int64_t 
 cudaError_t pairwise_tc_launch(const float* X, const float* Y, float* D, int* clamp_flags, int64_t B, int64_t N,
                                int64_t M, int64_t d, double timeout_s, cudaStream_t s);
 
+// Whether the tcgen05 grad_X kernel handles these fp32 arguments (d <= 128, d % 4 == 0, M % 4 == 0,
+// 16-byte aligned bases).
+bool grad_tc_supported(const void* X, const void* Y, const void* D, const void* E, const void* gX, int64_t B,
+                       int64_t N, int64_t M, int64_t d);
+
+// grad_X = 2 g[b] (rowsum(G) X - G Y), G = E with the clamped cells of D (sign bit) zeroed in pairs whose
+// clamp flag is set (every pair when clamp_flags is null). Every wait in the kernel is bounded by timeout_s.
+cudaError_t grad_x_tc_launch(const float* X, const float* Y, const float* D, const float* E, const float* g,
+                             const int* clamp_flags, float* gX, int64_t B, int64_t N, int64_t M, int64_t d,
+                             double timeout_s, cudaStream_t s);
+
 // Reads and clears the tensor-core kernels' error bits (1: a wait ran out and a tile was written as NaN).
 cudaError_t read_distance_errors(uint32_t& bits);
 
