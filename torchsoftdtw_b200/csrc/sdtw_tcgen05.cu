@@ -1,18 +1,10 @@
-// Squared-L2 cost matrix on the 5th-generation tensor cores (tcgen05, sm_100a).
-//
-// D[b,i,j] = (|x_i|^2 + |y_j|^2) - 2 x_i.y_j, clamped at 0 with the clamp recorded as -0.0, for fp32 X, Y.
-// One CTA (128 threads) computes a 128 x 128 tile of D:
-//   * TMA (cp.async.bulk.tensor, no multicast) brings 128 rows x 32 features of X and of Y into shared
-//     memory per K step, 128-byte swizzled, completing on an mbarrier;
-//   * each thread splits one row of each in place into a TF32 head and a TF32 tail (both rounded to
-//     nearest: x = head + tail to about 2^-22) and accumulates the row's squared norm in fp32;
-//   * one thread issues tcgen05.mma kind::tf32 (M = N = 128, K = 8) for head.head + head.tail + tail.head
-//     (3xTF32: the x.y products keep fp32 accuracy) into a 128-column fp32 accumulator in tensor memory,
-//     and tcgen05.commit signals an mbarrier when they are done;
-//   * the four warps read their 32 accumulator lanes (rows) with tcgen05.ld, form D, write it to shared
-//     memory in the 128-byte swizzled layout, and one thread stores the tile with TMA.
-// Every mbarrier wait is bounded in time; a tile whose wait runs out is written as NaN and a bit is set in
-// the library's distance error word.
+// Tensor-core (tcgen05, sm_100a) kernels of the squared-L2 module path, both fp32 with 3xTF32 products:
+// the cost matrix D = |x|^2 + |y|^2 - 2 X Y^T (clamped at 0, the clamp recorded as -0.0) and the gradient
+// grad_X = 2 g (rowsum(G) X - G Y). Both are persistent and warp-specialized: a TMA warp streams operand
+// chunks into shared memory (no multicast), split warps turn each fp32 operand into a TF32 head and tail
+// (x = head + tail to about 2^-22) so that head.head + head.tail + tail.head keeps fp32 accuracy, one thread
+// issues tcgen05.mma into fp32 accumulators in tensor memory, and epilogue warps read the accumulators back
+// with tcgen05.ld while the next tile's products run. Every mbarrier wait is bounded in time.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -29,18 +21,6 @@ namespace {
 constexpr int kT = 128;                // tile rows (X) = tile columns (Y) = UMMA M = N
 constexpr int kKC = 32;                // features per K step: one 128-byte swizzle atom of fp32
 constexpr int kChunk = kT * kKC * 4;   // 16 KB: one operand's K step
-constexpr uint32_t kTmemCols = 128;    // fp32 accumulator 128 x 128
-// Shared memory (offsets from a 1024-byte aligned base): X head, X tail, Y head, Y tail (one K step each;
-// reused as the 4 x 32-column staging of the output tile), |y|^2 of the tile's columns, two mbarriers and
-// the tensor-memory address.
-constexpr int kOffXh = 0, kOffXl = kChunk, kOffYh = 2 * kChunk, kOffYl = 3 * kChunk;
-constexpr int kOffY2 = 4 * kChunk;
-constexpr int kOffBarLoad = kOffY2 + kT * 4;
-constexpr int kOffBarMma = kOffBarLoad + 8;
-constexpr int kOffTmem = kOffBarMma + 8;
-constexpr int kSmemUsed = kOffTmem + 16;
-constexpr int kSmemBytes = kSmemUsed + 1024;  // slack for aligning the dynamic base to 1024 bytes
-
 // UMMA instruction descriptor: D fp32, A and B TF32, both K-major, M = 128, N = 128.
 constexpr uint32_t kIdesc = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t(kT) >> 3) << 17) |
                             ((uint32_t(kT) >> 4) << 24);
@@ -168,120 +148,6 @@ __device__ __forceinline__ float split_row(unsigned char* head, unsigned char* t
         *reinterpret_cast<float4*>(tail + 16 * u) = t;
     }
     return s;
-}
-
-__global__ void __launch_bounds__(128) pairwise_l2_tc_kernel(const __grid_constant__ CUtensorMap mx,
-                                                             const __grid_constant__ CUtensorMap my,
-                                                             const __grid_constant__ CUtensorMap md, float* D,
-                                                             int* clamp_flags, int N, int M, int d,
-                                                             unsigned long long timeout_ns)
-{
-    extern __shared__ unsigned char smem_raw[];
-    const uint32_t raw = smem_addr(smem_raw);
-    unsigned char* sm = smem_raw + ((1024u - (raw & 1023u)) & 1023u);
-    const uint32_t base = smem_addr(sm);
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int j0 = blockIdx.x * kT, i0 = blockIdx.y * kT, b = blockIdx.z;
-    const uint32_t bar_load = base + kOffBarLoad, bar_mma = base + kOffBarMma;
-    float* y2s = reinterpret_cast<float*>(sm + kOffY2);
-
-    if (tid == 0) {
-        mbar_init(bar_load, 1);
-        mbar_init(bar_mma, 1);
-        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    }
-    if (warp == 0) {
-        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(base + kOffTmem),
-                     "r"(kTmemCols)
-                     : "memory");
-        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
-    }
-    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-    __syncthreads();
-    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-    const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(sm + kOffTmem);
-
-    // Every thread waits on each mbarrier (bounded); the outcome is made uniform with __syncthreads_and, so
-    // the whole CTA leaves the loop together if a wait ran out.
-    bool ok = true;
-    float x2 = 0.f, y2 = 0.f;
-    const int nk = (d + kKC - 1) / kKC;
-    for (int kc = 0; kc < nk; ++kc) {
-        if (tid == 0) {
-            mbar_expect_tx(bar_load, 2 * kChunk);
-            tma_load_3d(base + kOffXh, &mx, bar_load, kc * kKC, i0, b);
-            tma_load_3d(base + kOffYh, &my, bar_load, kc * kKC, j0, b);
-        }
-        ok = __syncthreads_and(mbar_wait(bar_load, kc & 1, timeout_ns) ? 1 : 0) != 0;
-        if (!ok) break;
-        x2 += split_row(sm + kOffXh + 128 * tid, sm + kOffXl + 128 * tid, tid);
-        y2 += split_row(sm + kOffYh + 128 * tid, sm + kOffYl + 128 * tid, tid);
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> tensor-core reads
-        __syncthreads();
-        if (tid == 0) {
-            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-            const uint64_t xh = sw128_desc(base + kOffXh), xl = sw128_desc(base + kOffXl);
-            const uint64_t yh = sw128_desc(base + kOffYh), yl = sw128_desc(base + kOffYl);
-#pragma unroll
-            for (int kk = 0; kk < kKC / 8; ++kk) {
-                const uint64_t step = static_cast<uint64_t>((kk * 32) >> 4);  // 8 TF32 = 32 bytes along K
-                umma_tf32(tmem, xh + step, yh + step, (kc > 0 || kk > 0) ? 1u : 0u);
-                umma_tf32(tmem, xh + step, yl + step, 1u);
-                umma_tf32(tmem, xl + step, yh + step, 1u);
-            }
-            asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-                             bar_mma)
-                         : "memory");
-        }
-        ok = __syncthreads_and(mbar_wait(bar_mma, kc & 1, timeout_ns) ? 1 : 0) != 0;
-        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        if (!ok) break;
-    }
-    y2s[tid] = y2;
-    __syncthreads();
-
-    const int i = i0 + tid;  // this thread's row of the tile (TMEM lane = tid)
-    bool clamped = false;
-    if (ok) {
-#pragma unroll 1
-        for (int q = 0; q < kT / 32; ++q) {
-            float acc[32];
-            tmem_ld32(tmem + (static_cast<uint32_t>(warp * 32) << 16) + static_cast<uint32_t>(q * 32), acc);
-            unsigned char* row = sm + q * kChunk + 128 * tid;  // staging of columns 32q .. 32q+31
-#pragma unroll
-            for (int u = 0; u < 8; ++u) {
-                float o[4];
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    const int jl = 32 * q + 4 * u + e;
-                    float v = (x2 + y2s[jl]) - 2.f * acc[4 * u + e];
-                    clamped |= v < 0.f && i < N && j0 + jl < M;
-                    o[e] = v < 0.f ? -0.f : v;
-                }
-                *reinterpret_cast<float4*>(row + 16 * (u ^ (tid & 7))) = make_float4(o[0], o[1], o[2], o[3]);
-            }
-        }
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        __syncthreads();
-        if (tid == 0) {
-#pragma unroll 1
-            for (int q = 0; q < kT / 32; ++q) tma_store_3d(&md, base + q * kChunk, j0 + 32 * q, i0, b);
-            asm volatile("cp.async.bulk.commit_group;" ::: "memory");
-            asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
-        }
-    } else {
-        // A wait ran out: report it and leave NaN in this tile rather than stale data.
-        if (tid == 0) atomicOr(&g_distance_err, 1u);
-        if (i < N) {
-            float* dst = D + (static_cast<int64_t>(b) * N + i) * M;
-            for (int jl = 0; jl < kT && j0 + jl < M; ++jl) dst[j0 + jl] = __int_as_float(0x7fc00000);
-        }
-    }
-    if (clamp_flags && __any_sync(kFull, clamped) && lane == 0) atomicOr(clamp_flags + b, 1);
-    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-    __syncthreads();
-    if (warp == 0)
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
 }
 
 // ==================================================================================================
@@ -682,6 +548,264 @@ __global__ void __launch_bounds__(kGradThreads, 1) grad_x_tc_kernel(const __grid
                      : "memory");
 }
 
+// ==================================================================================================
+// Cost matrix, persistent and warp-specialized: D[b,i,j] = (|x_i|^2 + |y_j|^2) - 2 x_i.y_j, clamped at 0
+// with the clamp recorded as -0.0 and in clamp_flags[b].
+//
+// A tile is 128 x 128 cells of one pair (UMMA M = N = 128); its K loop runs over the features in chunks of
+// 32 (one 128-byte swizzle atom of fp32). Tiles blockIdx.x, blockIdx.x + gridDim.x, ... (the tiles of a pair
+// are consecutive, so X and Y rows are reused from L2); chunks are numbered q across the CTA's tiles.
+//   * warp 0 (TMA): X[128 rows x 32 features] and Y[128 x 32] of chunk q into stage q % S (128-byte
+//     swizzled);
+//   * warps 2..9 (split): thread r (< 128) takes X row r, thread 128 + r takes Y row r: split in place into a
+//     TF32 head and, in the stage's tail half, a TF32 tail (3xTF32), and accumulate the row's squared norm
+//     over the tile's chunks (written to norm buffer tile % 4 at the tile's last chunk);
+//   * warp 1 (MMA): 3 x 4 tcgen05.mma kind::tf32 per chunk into accumulator (tile & 1), commit to the
+//     stage's "empty" barrier (the TMA refills it), and after the tile's last chunk to "acc full";
+//   * warps 10..13 (epilogue): per 32-column slice, read the accumulator row (tcgen05.ld), form D, write
+//     it 128-byte swizzled into one of two staging buffers and store it with TMA; release the
+//     accumulator after the last slice.
+// Every wait is bounded; a wait that runs out raises the CTA's abort word and bit 1 of the distance error
+// word, and the epilogue writes NaN into the tiles it has not finished.
+// ==================================================================================================
+constexpr int kDThreads = 32 * (2 + 8 + 4);
+constexpr int kDSplit0 = 64;                        // first split thread
+constexpr int kDEpiWarp0 = 10;
+constexpr int kDStage = 4 * kChunk;                 // X head, Y head, X tail, Y tail: 64 KB
+constexpr int kDS = 2;                              // stages
+constexpr int kDOffStage = 0;
+constexpr int kDOffOut = kDS * kDStage;             // 2 x 16 KB output staging
+constexpr int kDOffNorm = kDOffOut + 2 * kChunk;    // x2[4][128], y2[4][128]
+constexpr int kDOffBar = kDOffNorm + 2 * 4 * kT * 4;
+constexpr int kDNBar = 3 * kDS + 8;                 // full[S], split[S], empty[S], acc_full[2], acc_empty[2], norm[4]
+constexpr int kDOffTmem = kDOffBar + 8 * kDNBar;
+constexpr int kDOffAbort = kDOffTmem + 8;
+constexpr int kDSmemBytes = kDOffAbort + 8 + 1024;
+constexpr uint32_t kDTmemCols = 2 * kT;             // two 128-column fp32 accumulators
+static_assert(kDSmemBytes <= 227 * 1024, "shared memory");
+
+struct PairwiseTcArgs {
+    float* D;
+    int* clamp_flags;
+    int B, N, M, d;
+    int nit, njt, nk;  // row tiles, column tiles, feature chunks
+    unsigned long long timeout_ns;
+};
+
+__global__ void __launch_bounds__(kDThreads, 1) pairwise_l2_tc_kernel(const __grid_constant__ CUtensorMap mx,
+                                                                       const __grid_constant__ CUtensorMap my,
+                                                                       const __grid_constant__ CUtensorMap md,
+                                                                       PairwiseTcArgs a)
+{
+    extern __shared__ unsigned char smem_raw[];
+    const uint32_t raw0 = smem_addr(smem_raw);
+    unsigned char* sm = smem_raw + ((1024u - (raw0 & 1023u)) & 1023u);
+    const uint32_t base = smem_addr(sm);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const uint32_t full = base + kDOffBar;
+    const uint32_t split = full + 8 * kDS;
+    const uint32_t empty = split + 8 * kDS;
+    const uint32_t acc_full = empty + 8 * kDS;
+    const uint32_t acc_empty = acc_full + 16;
+    const uint32_t norm_full = acc_empty + 16;  // [4]: the split wrote the norms of tile t (t % 4)
+    volatile int* abort = reinterpret_cast<volatile int*>(sm + kDOffAbort);
+    float* x2s = reinterpret_cast<float*>(sm + kDOffNorm);  // [4][128]
+    float* y2s = x2s + 4 * kT;                              // [4][128]
+
+    const int per_pair = a.nit * a.njt;
+    const int ntiles = a.B * per_pair;
+    const int my_tiles = blockIdx.x < static_cast<unsigned>(ntiles)
+                             ? (ntiles - 1 - static_cast<int>(blockIdx.x)) / static_cast<int>(gridDim.x) + 1
+                             : 0;
+    auto tile_of = [&](int tl, int& b, int& i0, int& j0) {
+        const int t = static_cast<int>(blockIdx.x) + tl * static_cast<int>(gridDim.x);
+        b = t / per_pair;
+        const int r = t % per_pair;
+        i0 = (r / a.njt) * kT;
+        j0 = (r % a.njt) * kT;
+    };
+
+    if (tid == 0) {
+        for (int s = 0; s < kDS; ++s) {
+            mbar_init(full + 8 * s, 1);
+            mbar_init(split + 8 * s, 8);
+            mbar_init(empty + 8 * s, 1);
+        }
+        for (int c = 0; c < 2; ++c) {
+            mbar_init(acc_full + 8 * c, 1);
+            mbar_init(acc_empty + 8 * c, 4);
+        }
+        for (int c = 0; c < 4; ++c) mbar_init(norm_full + 8 * c, 8);
+        *abort = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(base + kDOffTmem),
+                     "r"(kDTmemCols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(sm + kDOffTmem);
+
+    if (warp == 0) {
+        // ---------------- TMA producer ----------------
+        if (lane == 0) {
+            const int Q = my_tiles * a.nk;
+            int issued = 0;
+            for (int q = 0; q < Q; ++q) {
+                const int s = q % kDS;
+                if (q >= kDS && !wait_role(empty + 8 * s, ((q / kDS) - 1) & 1, a.timeout_ns, abort)) break;
+                int b, i0, j0;
+                tile_of(q / a.nk, b, i0, j0);
+                const int kc = q % a.nk;
+                const uint32_t st = base + kDOffStage + s * kDStage;
+                mbar_expect_tx(full + 8 * s, 2 * kChunk);
+                tma_load_3d(st, &mx, full + 8 * s, kc * kKC, i0, b);
+                tma_load_3d(st + kChunk, &my, full + 8 * s, kc * kKC, j0, b);
+                issued = q + 1;
+            }
+            for (int q = issued - kDS < 0 ? 0 : issued - kDS; q < issued; ++q)
+                (void)mbar_wait(full + 8 * (q % kDS), (q / kDS) & 1, a.timeout_ns);
+        }
+    } else if (warp == 1) {
+        // ---------------- MMA issuer ----------------
+        if (lane == 0) {
+            int q = 0;
+            bool ok = true;
+            for (int tl = 0; tl < my_tiles && ok; ++tl) {
+                const int ab = tl & 1;
+                if (tl >= 2 && !wait_role(acc_empty + 8 * ab, ((tl >> 1) - 1) & 1, a.timeout_ns, abort)) break;
+                const uint32_t acc = tmem + static_cast<uint32_t>(ab * kT);
+                for (int kc = 0; kc < a.nk; ++kc, ++q) {
+                    const int s = q % kDS;
+                    if (!wait_role(split + 8 * s, (q / kDS) & 1, a.timeout_ns, abort)) {
+                        ok = false;
+                        break;
+                    }
+                    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                    const uint32_t st = base + kDOffStage + s * kDStage;
+                    const uint64_t xh = sw128_desc(st), yh = sw128_desc(st + kChunk);
+                    const uint64_t xl = sw128_desc(st + 2 * kChunk), yl = sw128_desc(st + 3 * kChunk);
+#pragma unroll
+                    for (int kk = 0; kk < kKC / 8; ++kk) {
+                        const uint64_t o = static_cast<uint64_t>((kk * 32) >> 4);  // 8 TF32 = 32 bytes along K
+                        umma_tf32(acc, xh + o, yh + o, (kc > 0 || kk > 0) ? 1u : 0u);
+                        umma_tf32(acc, xh + o, yl + o, 1u);
+                        umma_tf32(acc, xl + o, yh + o, 1u);
+                    }
+                    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                                     empty + 8 * s)
+                                 : "memory");
+                    if (kc == a.nk - 1)
+                        asm volatile(
+                            "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                                acc_full + 8 * ab)
+                            : "memory");
+                }
+            }
+            if (q > 0) (void)mbar_wait(empty + 8 * ((q - 1) % kDS), ((q - 1) / kDS) & 1, a.timeout_ns);
+        }
+    } else if (warp < kDEpiWarp0) {
+        // ---------------- split ----------------
+        const int st_id = tid - kDSplit0;          // 0..255
+        const bool is_y = st_id >= kT;
+        const int row = st_id & (kT - 1);
+        int q = 0;
+        for (int tl = 0; tl < my_tiles; ++tl) {
+            float nrm = 0.f;
+            bool ok = true;
+            for (int kc = 0; kc < a.nk; ++kc, ++q) {
+                const int s = q % kDS;
+                if (!wait_role(full + 8 * s, (q / kDS) & 1, a.timeout_ns, abort)) {
+                    ok = false;
+                    break;
+                }
+                unsigned char* st = sm + kDOffStage + s * kDStage + (is_y ? kChunk : 0);
+                nrm += split_row(st + 128 * row, st + 2 * kChunk + 128 * row, row);
+                if (kc == a.nk - 1) (is_y ? y2s : x2s)[(tl & 3) * kT + row] = nrm;
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> tensor-core reads
+                __syncwarp();
+                if (lane == 0) {
+                    mbar_arrive(split + 8 * s);
+                    if (kc == a.nk - 1) mbar_arrive(norm_full + 8 * (tl & 3));
+                }
+            }
+            if (!ok) break;
+        }
+    } else {
+        // ---------------- epilogue ----------------
+        const int row = 32 * (warp & 3) + lane;     // accumulator lane = tile row
+        const int et = tid - 32 * kDEpiWarp0;       // 0..127
+        const bool leader = et == 0;
+        int tl = 0;
+        int slice = 0;  // output slices issued by this CTA (staging buffer = slice & 1)
+        for (; tl < my_tiles; ++tl) {
+            const int ab = tl & 1;
+            if (!wait_role(acc_full + 8 * ab, (tl >> 1) & 1, a.timeout_ns, abort) ||
+                !wait_role(norm_full + 8 * (tl & 3), (tl >> 2) & 1, a.timeout_ns, abort))
+                break;
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            int b, i0, j0;
+            tile_of(tl, b, i0, j0);
+            const float x2 = x2s[(tl & 3) * kT + row];
+            const float* y2 = y2s + (tl & 3) * kT;
+            const int i = i0 + row;
+            bool clamped = false;
+#pragma unroll 1
+            for (int qs = 0; qs < kT / 32; ++qs, ++slice) {
+                float acc[32];
+                tmem_ld32(tmem + (static_cast<uint32_t>(32 * (warp & 3)) << 16) + static_cast<uint32_t>(ab * kT + 32 * qs),
+                          acc);
+                // The staging buffer of this slice was last read by the store issued two slices ago.
+                if (leader) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+                asm volatile("bar.sync 1, 128;" ::: "memory");
+                unsigned char* ob = sm + kDOffOut + (slice & 1) * kChunk + 128 * row;
+#pragma unroll
+                for (int u = 0; u < 8; ++u) {
+                    float o[4];
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const int jl = 32 * qs + 4 * u + e;
+                        const float v = (x2 + y2[jl]) - 2.f * acc[4 * u + e];
+                        clamped |= v < 0.f && i < a.N && j0 + jl < a.M;
+                        o[e] = v < 0.f ? -0.f : v;
+                    }
+                    *reinterpret_cast<float4*>(ob + 16 * (u ^ (row & 7))) = make_float4(o[0], o[1], o[2], o[3]);
+                }
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                asm volatile("bar.sync 1, 128;" ::: "memory");
+                if (leader) {
+                    tma_store_3d(&md, base + kDOffOut + (slice & 1) * kChunk, j0 + 32 * qs, i0, b);
+                    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+                }
+            }
+            asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+            __syncwarp();
+            if (lane == 0) mbar_arrive(acc_empty + 8 * ab);
+            if (a.clamp_flags && __any_sync(kFull, clamped) && lane == 0) atomicOr(a.clamp_flags + b, 1);
+        }
+        if (leader) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+        if (tl < my_tiles) {
+            // A wait ran out: NaN into this thread's row of every tile not finished.
+            for (; tl < my_tiles; ++tl) {
+                int b, i0, j0;
+                tile_of(tl, b, i0, j0);
+                const int i = i0 + row;
+                if (i < a.N)
+                    for (int jl = 0; jl < kT && j0 + jl < a.M; ++jl)
+                        a.D[(static_cast<int64_t>(b) * a.N + i) * a.M + j0 + jl] = __int_as_float(0x7fc00000);
+            }
+        }
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    if (warp == 1)
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kDTmemCols) : "memory");
+}
+
 // ---- host -------------------------------------------------------------------------------------------
 std::mutex g_tc_mu;
 PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
@@ -825,20 +949,35 @@ cudaError_t pairwise_tc_launch(const float* X, const float* Y, float* D, int* cl
     {
         std::lock_guard<std::mutex> lock(g_tc_mu);
         if (!g_attr_set[dev]) {
-            e = cudaFuncSetAttribute(pairwise_l2_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+            e = cudaFuncSetAttribute(pairwise_l2_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kDSmemBytes);
             if (e != cudaSuccess) return e;
             g_attr_set[dev] = true;
+        }
+        if (g_sm_count[dev] == 0) {
+            int n = 0;
+            e = cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+            if (e != cudaSuccess) return e;
+            g_sm_count[dev] = n > 0 ? n : 1;
         }
     }
     CUtensorMap mx, my, md;
     if (!make_map(encode, &mx, X, B, N, d) || !make_map(encode, &my, Y, B, M, d) || !make_map(encode, &md, D, B, N, M))
         return cudaErrorInvalidValue;
-    const dim3 grid(static_cast<unsigned>((M + kT - 1) / kT), static_cast<unsigned>((N + kT - 1) / kT),
-                    static_cast<unsigned>(B));
+    PairwiseTcArgs a;
+    a.D = D;
+    a.clamp_flags = clamp_flags;
+    a.B = static_cast<int>(B);
+    a.N = static_cast<int>(N);
+    a.M = static_cast<int>(M);
+    a.d = static_cast<int>(d);
+    a.nit = static_cast<int>((N + kT - 1) / kT);
+    a.njt = static_cast<int>((M + kT - 1) / kT);
+    a.nk = static_cast<int>((d + kKC - 1) / kKC);
+    a.timeout_ns = static_cast<unsigned long long>(timeout_s * 1e9);
+    const int64_t tiles = B * a.nit * a.njt;
+    const int grid = static_cast<int>(tiles < g_sm_count[dev] ? tiles : g_sm_count[dev]);
     count_launch();
-    pairwise_l2_tc_kernel<<<grid, kT, kSmemBytes, s>>>(mx, my, md, D, clamp_flags, static_cast<int>(N),
-                                                       static_cast<int>(M), static_cast<int>(d),
-                                                       static_cast<unsigned long long>(timeout_s * 1e9));
+    pairwise_l2_tc_kernel<<<grid, kDThreads, kDSmemBytes, s>>>(mx, my, md, a);
     return cudaGetLastError();
 }
 
