@@ -107,12 +107,10 @@ __device__ __forceinline__ void fwd_pair_load(const T* Db, int64_t M, T* ring, i
     const int c0 = 32 * blk + lane;  // column read by row 0; row r reads column c0 - r
     if (32 * blk - 31 >= 0 && 32 * blk + 31 < M && nrows == 32) {
         const T* src = Db + c0;
-        const int64_t step = M - 1;
-#pragma unroll 8
-        for (int r = 0; r < 32; ++r) {
-            cp_async_scalar<sizeof(T)>(dst + r * kFwdStride, src, static_cast<int>(sizeof(T)));
-            src += step;
-        }
+        const int64_t step = M - 1;  // a compile-time constant in the kernels specialized on M
+#pragma unroll
+        for (int r = 0; r < 32; ++r)
+            cp_async_scalar<sizeof(T)>(dst + r * kFwdStride, src + r * step, static_cast<int>(sizeof(T)));
     } else {
         for (int r = 0; r < 32; ++r) {
             const int c = c0 - r;
@@ -133,11 +131,8 @@ __device__ __forceinline__ void fwd_pair_store(T* Rrow, int64_t pitch, int64_t M
     if (32 * blk - 31 >= 0 && 32 * blk + 31 < M && nmat == 32) {
         T* dst = Rrow + c0 + 1;
         const int64_t step = pitch - 1;
-#pragma unroll 8
-        for (int r = 0; r < 32; ++r) {
-            *dst = src[r * kFwdStride];
-            dst += step;
-        }
+#pragma unroll
+        for (int r = 0; r < 32; ++r) dst[r * step] = src[r * kFwdStride];
     } else {
         for (int r = 0; r < nmat; ++r) {
             const int c = c0 - r;
@@ -147,10 +142,9 @@ __device__ __forceinline__ void fwd_pair_store(T* Rrow, int64_t pitch, int64_t M
 }
 
 // 8 forward steps tau0 .. tau0+7 of one warp. `cell` is this lane's ring row at position tau0, `top`
-// the row above (boundary row) at column tau0, `bot` this strip's boundary row at column tau0 - 31 for
-// the lane that publishes it and a per-warp scratch area for the others.
+// the row above (boundary row) at column tau0.
 template <typename T, bool MASKED>
-__device__ __forceinline__ void fwd_pair_steps8(T* cell, const T* top, T* bot, int tau0, int A, int Z, T k, T gl,
+__device__ __forceinline__ void fwd_pair_steps8(T* cell, const T* top, int tau0, int A, int Z, T k, T gl,
                                                 int src_lane, bool lane0, T& outp, T& upp)
 {
     const T INF = Num<T>::inf();
@@ -166,19 +160,19 @@ __device__ __forceinline__ void fwd_pair_steps8(T* cell, const T* top, T* bot, i
             r = (tau >= A && tau <= Z) ? r : INF;
         }
         cell[j] = r;
-        bot[j] = r;  // lane 31: the boundary row; other lanes: a scratch word (no divergent store)
         upp = up;
         outp = r;
     }
 }
 
-// One strip of the forward. Returns false if the launch aborted.
-template <typename T>
+// One strip of the forward. Returns false if the launch aborted. MC > 0: the kernel is specialized on
+// M == MC, so every row offset in the ring's loads and stores is a compile-time constant.
+template <typename T, int MC>
 __device__ bool fwd_pair_strip(const PairFwdArgs<T>& a, T* ring, const T* bin, const int* pin, T* bout, int* pout,
-                               T* scratch, int64_t b, int s, int lane)
+                               int64_t b, int s, int lane)
 {
     const T INF = Num<T>::inf();
-    const int64_t N = a.N, M = a.M, pitch = M + 2;
+    const int64_t N = a.N, M = MC > 0 ? MC : a.M, pitch = M + 2;
     const int r0 = 32 * s;
     const int nmat = static_cast<int>(N - r0 < 32 ? N - r0 : 32);
     T* Rrow = a.R + b * (N + 2) * pitch + static_cast<int64_t>(r0 + 1) * pitch;
@@ -234,7 +228,6 @@ __device__ bool fwd_pair_strip(const PairFwdArgs<T>& a, T* ring, const T* bin, c
     T outp = INF;
     const int src_lane = (lane + 31) & 31;
     const bool lane0 = lane == 0;
-    const bool put_bot = has_consumer && lane == 31;
 
 #pragma unroll 1
     for (int blk = k0; blk <= k1; ++blk) {
@@ -243,19 +236,25 @@ __device__ bool fwd_pair_strip(const PairFwdArgs<T>& a, T* ring, const T* bin, c
         const int tau0 = 32 * blk;
         T* cell = ring + lane * kFwdStride + (blk & 1) * 32;
         const T* top = bin + tau0 + kBufPad;
-        T* bot = put_bot ? bout + tau0 - 31 + kBufPad : scratch;
+        const T* last = ring + 31 * kFwdStride + (blk & 1) * 32;  // the strip's last row, positions tau0 ..
         const bool full = tau0 >= st.Amax && tau0 + 31 <= st.Zmin;
 #pragma unroll 1
         for (int q = 0; q < 4; ++q) {
             const int t8 = tau0 + 8 * q;
             if (s > 0 && !wait_key(pin, key_in + t8 + 7, seen, a.sy, lane)) return false;
             if (full)
-                fwd_pair_steps8<T, false>(cell + 8 * q, top + 8 * q, bot + 8 * q, t8, st.A, st.Z, a.k, a.gl,
-                                          src_lane, lane0, outp, upp);
+                fwd_pair_steps8<T, false>(cell + 8 * q, top + 8 * q, t8, st.A, st.Z, a.k, a.gl, src_lane, lane0,
+                                          outp, upp);
             else
-                fwd_pair_steps8<T, true>(cell + 8 * q, top + 8 * q, bot + 8 * q, t8, st.A, st.Z, a.k, a.gl,
-                                         src_lane, lane0, outp, upp);
-            st_release_cta_if(pout, key_out + t8 + 7 - 31, put_bot);
+                fwd_pair_steps8<T, true>(cell + 8 * q, top + 8 * q, t8, st.A, st.Z, a.k, a.gl, src_lane, lane0,
+                                         outp, upp);
+            if (has_consumer) {
+                // Publish the last row's 8 new values (columns t8 - 31 .. t8 - 24) from the ring.
+                __syncwarp();
+                if (lane < 8) bout[t8 + lane - 31 + kBufPad] = last[8 * q + lane];
+                __syncwarp();
+                st_release_cta_if(pout, key_out + t8 + 7 - 31, lane == 0);
+            }
         }
         __syncwarp();
         fwd_pair_store<T>(Rrow, pitch, M, ring, blk, nmat, lane);
@@ -274,7 +273,7 @@ __device__ bool fwd_pair_strip(const PairFwdArgs<T>& a, T* ring, const T* bin, c
     return true;
 }
 
-template <typename T>
+template <typename T, int MC>
 __global__ void __launch_bounds__(SDTW_PAIR_THREADS, SDTW_PAIR_MIN_CTAS) sdtw_fwd_pair_kernel(PairFwdArgs<T> a)
 {
     extern __shared__ __align__(16) unsigned char smem[];
@@ -304,8 +303,8 @@ __global__ void __launch_bounds__(SDTW_PAIR_THREADS, SDTW_PAIR_MIN_CTAS) sdtw_fw
     for (int s = warp; s < a.S; s += W) {
         const int wp = (s + W - 1) % W;
         const T* bin = s > 0 ? bufs + static_cast<size_t>(wp) * a.BL : crow;
-        if (!fwd_pair_strip<T>(a, ring, bin, prog + wp, bufs + static_cast<size_t>(warp) * a.BL, prog + warp,
-                               scratch + static_cast<size_t>(warp) * 32, b, s, lane))
+        if (!fwd_pair_strip<T, MC>(a, ring, bin, prog + wp, bufs + static_cast<size_t>(warp) * a.BL, prog + warp, b,
+                                   s, lane))
             break;
     }
     cp_async_wait<0>();
@@ -619,7 +618,9 @@ size_t pair_bwd_smem_bytes(int W, int64_t M)
 template <typename T>
 cudaError_t pair_init_attrs(int max_smem)
 {
-    cudaError_t e = cudaFuncSetAttribute(sdtw_fwd_pair_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
+    cudaError_t e = cudaFuncSetAttribute(sdtw_fwd_pair_kernel<T, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
+    if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(sdtw_fwd_pair_kernel<T, kPairSpecialM>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
     if (e != cudaSuccess) return e;
     return cudaFuncSetAttribute(sdtw_bwd_pair_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
 }
@@ -631,7 +632,7 @@ cudaError_t pair_regs(bool backward, int& regs)
 {
     cudaFuncAttributes fa;
     const cudaError_t e = backward ? cudaFuncGetAttributes(&fa, sdtw_bwd_pair_kernel<T>)
-                                   : cudaFuncGetAttributes(&fa, sdtw_fwd_pair_kernel<T>);
+                                   : cudaFuncGetAttributes(&fa, sdtw_fwd_pair_kernel<T, 0>);
     regs = e == cudaSuccess ? fa.numRegs : 0;
     return e;
 }
@@ -683,7 +684,10 @@ cudaError_t pair_forward(const T* D, T* R, T* costs, const void* lx, const void*
     a.sy = sy;
     a.inject = inject;
     count_launch();
-    sdtw_fwd_pair_kernel<T><<<static_cast<unsigned>(B), W * 32, pair_fwd_smem_bytes<T>(W, M), stream>>>(a);
+    if (M == kPairSpecialM)
+        sdtw_fwd_pair_kernel<T, kPairSpecialM><<<static_cast<unsigned>(B), W * 32, pair_fwd_smem_bytes<T>(W, M), stream>>>(a);
+    else
+        sdtw_fwd_pair_kernel<T, 0><<<static_cast<unsigned>(B), W * 32, pair_fwd_smem_bytes<T>(W, M), stream>>>(a);
     return cudaGetLastError();
 }
 template cudaError_t pair_forward<float>(const float*, float*, float*, const void*, const void*, int, int64_t, int64_t,

@@ -23,6 +23,9 @@ constexpr int kPairMaxWarps = SDTW_PAIR_THREADS / 32;  // warps per CTA at most
 constexpr int kFwdStride = 65;     // forward ring row: 2 slots of 32 positions + 1 (odd: conflict-free)
 constexpr int kBwdStride = 97;     // backward ring row: 3 slots + 1
 constexpr int kBufPad = 64;        // boundary rows are indexed by column + kBufPad
+// Row length M for which the wavefront kernels are also compiled with M as a compile-time constant
+// (immediate row offsets in the ring loads and stores); other lengths run the generic instantiation.
+constexpr int kPairSpecialM = 512;
 
 // Shared-memory bytes of one CTA with W warps.
 template <typename T>

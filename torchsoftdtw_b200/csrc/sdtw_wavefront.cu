@@ -318,54 +318,64 @@ __device__ __forceinline__ void bwd_block(T* rowA, T* rowB, const T* bndring, T*
     }
 }
 
-// R chunk kk (padded rows r0 .. r0+rows, D-columns [32kk, 32kk+32)) -> ring rows 0..rows.
+// R chunk kk (padded rows r0 .. r0+rows, D-columns [32kk, 32kk+32)) -> ring rows 0..rows. M is a
+// compile-time constant in the kernels specialized on it (immediate row offsets in the full-strip case).
 template <typename T>
-__device__ __forceinline__ void bwd_load_chunk(const BwdArgs<T>& a, const T* Rb, T* ring, int kk, int r0, int rows,
-                                               int lane)
+__device__ __forceinline__ void bwd_load_chunk(int64_t M, const T* Rb, T* ring, int kk, int r0, int rows, int lane)
 {
-    const int64_t pitch = a.M + 2;
+    const int64_t pitch = M + 2;
     const int c = 32 * kk + lane;  // D-column; padded column c+1 exists for -1 <= c <= M
-    const bool in = c >= -1 && c <= a.M;
+    const bool in = c >= -1 && c <= M;
     const T* src = Rb + static_cast<int64_t>(r0) * pitch + (in ? c + 1 : 0);
     T* dst = ring + (c & kRingMask);
-    for (int q = 0; q <= rows; ++q)
-        cp_async_scalar<sizeof(T)>(dst + q * kRing, src + q * pitch, in ? static_cast<int>(sizeof(T)) : 0);
+    const int bytes = in ? static_cast<int>(sizeof(T)) : 0;
+    if (rows == 32) {
+#pragma unroll
+        for (int q = 0; q <= 32; ++q) cp_async_scalar<sizeof(T)>(dst + q * kRing, src + q * pitch, bytes);
+    } else {
+        for (int q = 0; q <= rows; ++q) cp_async_scalar<sizeof(T)>(dst + q * kRing, src + q * pitch, bytes);
+    }
 }
 
 template <typename T>
-__device__ __forceinline__ void bwd_store_chunk(const BwdArgs<T>& a, T* Eb, const T* ring, int kk, const Strip& st,
-                                                int lane)
+__device__ __forceinline__ void bwd_store_chunk(int64_t M, T* Eb, const T* ring, int kk, const Strip& st, int lane)
 {
     const int col = 32 * kk + lane;
     if (col < st.c_begin || col > st.c_end) return;
-    T* dst = Eb + static_cast<int64_t>(st.r0) * a.M + col;
+    T* dst = Eb + static_cast<int64_t>(st.r0) * M + col;
     const T* srcp = ring + kRing + (col & kRingMask);
-    for (int r = 0; r < st.rows; ++r) dst[r * a.M] = srcp[r * kRing];
+    if (st.rows == 32) {
+#pragma unroll
+        for (int r = 0; r < 32; ++r) dst[r * M] = srcp[r * kRing];
+    } else {
+        for (int r = 0; r < st.rows; ++r) dst[r * M] = srcp[r * kRing];
+    }
 }
 
-template <typename T>
+template <typename T, int MC>
 __device__ void bwd_strip(const BwdArgs<T>& a, T* ring, T* bndring, T* sendring, int64_t b, int s, int lane,
                           bool skip_publish)
 {
+    const int64_t M = MC > 0 ? MC : a.M;
     Strip st;
-    T* Eb = a.E + b * a.N * a.M;
+    T* Eb = a.E + b * a.N * M;
     const int nmat = static_cast<int>(a.N - 32 * s < 32 ? a.N - 32 * s : 32);  // rows of E this strip owns
-    if (!make_strip(st, a.len, b, s, a.N, a.M, a.bw, lane)) {
+    if (!make_strip(st, a.len, b, s, a.N, M, a.bw, lane)) {
         if (st.bad && s == 0 && lane == 0) atomicOr(a.sy.err, kErrBadLength);
-        T* row0 = Eb + static_cast<int64_t>(32 * s) * a.M;
+        T* row0 = Eb + static_cast<int64_t>(32 * s) * M;
         for (int r = 0; r < nmat; ++r)
-            for (int c = lane; c < a.M; c += 32) row0[r * a.M + c] = T(0);
+            for (int c = lane; c < M; c += 32) row0[r * M + c] = T(0);
         return;
     }
     // E is written in full: zeros outside the swept columns [c_begin, c_end] and in rows past the length.
     for (int r = 0; r < nmat; ++r) {
-        T* row = Eb + static_cast<int64_t>(st.r0 + r) * a.M;
-        const int lo = r < st.rows ? st.c_begin : static_cast<int>(a.M);
-        const int hi = r < st.rows ? st.c_end : static_cast<int>(a.M);
+        T* row = Eb + static_cast<int64_t>(st.r0 + r) * M;
+        const int lo = r < st.rows ? st.c_begin : static_cast<int>(M);
+        const int hi = r < st.rows ? st.c_end : static_cast<int>(M);
         for (int c = lane; c < lo; c += 32) row[c] = T(0);
-        for (int c = hi + 1 + lane; c < a.M; c += 32) row[c] = T(0);
+        for (int c = hi + 1 + lane; c < M; c += 32) row[c] = T(0);
     }
-    const int64_t pitch = a.M + 2;
+    const int64_t pitch = M + 2;
     const T* Rb = a.R + b * (a.N + 2) * pitch;
     const int k0 = st.c_begin >> 5;
     const int k1 = (st.c_end + 31) >> 5;
@@ -379,8 +389,8 @@ __device__ void bwd_strip(const BwdArgs<T>& a, T* ring, T* bndring, T* sendring,
         plo = static_cast<int>(l64);
         phi = static_cast<int>(h64);
     }
-    const T* bnd_in = a.bnd + (b * a.S + s) * a.M;
-    T* bnd_out = a.bnd + (b * a.S + (s - 1)) * a.M;
+    const T* bnd_in = a.bnd + (b * a.S + s) * M;
+    T* bnd_out = a.bnd + (b * a.S + (s - 1)) * M;
     // Terminal cell (nx-1, ny-1): E = 1 (the reference's sentinel, softdtw.cpp:225-227). Masked steps of
     // the terminal row leave `acc` = seed, so its first valid cell (column ny-1) starts from 1.
     const T seed = (st.r0 + lane == st.nx - 1) ? T(1) : T(0);
@@ -388,7 +398,7 @@ __device__ void bwd_strip(const BwdArgs<T>& a, T* ring, T* bndring, T* sendring,
 
 #pragma unroll 1
     for (int q = 0; q < 4; ++q) {
-        if (k1 - q >= kmin) bwd_load_chunk<T>(a, Rb, ring, k1 - q, st.r0, st.rows, lane);
+        if (k1 - q >= kmin) bwd_load_chunk<T>(M, Rb, ring, k1 - q, st.r0, st.rows, lane);
         cp_async_commit();
     }
 
@@ -430,9 +440,9 @@ __device__ void bwd_strip(const BwdArgs<T>& a, T* ring, T* bndring, T* sendring,
             const int c = tau0 + lane;
             if (c >= 0 && c >= st.c_begin - 1 && c <= hi0) st_relaxed(bnd_out + c, sendring[c & kSideMask]);
         }
-        bwd_store_chunk<T>(a, Eb, ring, blk, st, lane);
+        bwd_store_chunk<T>(M, Eb, ring, blk, st, lane);
         __syncwarp();
-        if (blk - 4 >= kmin) bwd_load_chunk<T>(a, Rb, ring, blk - 4, st.r0, st.rows, lane);
+        if (blk - 4 >= kmin) bwd_load_chunk<T>(M, Rb, ring, blk - 4, st.r0, st.rows, lane);
         cp_async_commit();
     }
     cp_async_wait<0>();
@@ -442,7 +452,7 @@ __device__ void bwd_strip(const BwdArgs<T>& a, T* ring, T* bndring, T* sendring,
     __syncwarp();
 }
 
-template <typename T>
+template <typename T, int MC>
 __global__ void __launch_bounds__(kWarpsPerCta * 32) sdtw_bwd_kernel(BwdArgs<T> a)
 {
     extern __shared__ __align__(16) unsigned char smem[];
@@ -462,7 +472,7 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32) sdtw_bwd_kernel(BwdArgs<T> 
         if (tk >= total) break;
         const int s = a.S - 1 - static_cast<int>(tk / a.B);
         const int64_t b = tk % a.B;
-        bwd_strip<T>(a, ring, bndring, sendring, b, s, lane, tk == a.inject_skip);
+        bwd_strip<T, MC>(a, ring, bndring, sendring, b, s, lane, tk == a.inject_skip);
     }
 }
 
@@ -518,13 +528,16 @@ cudaError_t init_kernel_attrs(int& occ_f, int& occ_b)
     cudaError_t e = cudaFuncSetAttribute(sdtw_fwd_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(fwd_smem_bytes<T>()));
     if (e != cudaSuccess) return e;
-    e = cudaFuncSetAttribute(sdtw_bwd_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    e = cudaFuncSetAttribute(sdtw_bwd_kernel<T, kPairSpecialM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(bwd_smem_bytes<T>()));
+    if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(sdtw_bwd_kernel<T, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(bwd_smem_bytes<T>()));
     if (e != cudaSuccess) return e;
     e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ_f, sdtw_fwd_kernel<T>, kWarpsPerCta * 32,
                                                       fwd_smem_bytes<T>());
     if (e != cudaSuccess) return e;
-    return cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ_b, sdtw_bwd_kernel<T>, kWarpsPerCta * 32,
+    return cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ_b, sdtw_bwd_kernel<T, 0>, kWarpsPerCta * 32,
                                                          bwd_smem_bytes<T>());
 }
 
@@ -708,7 +721,10 @@ sdtw_status launch_backward(const void* R, int64_t B, int64_t N, int64_t M, cons
     const int64_t ctas_needed = (B * S + kWarpsPerCta - 1) / kWarpsPerCta;
     const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(ctas_needed, int64_t(di->sms) * std::max(occ, 1))));
     count_launch();
-    sdtw_bwd_kernel<T><<<grid, kWarpsPerCta * 32, bwd_smem_bytes<T>(), stream>>>(a);
+    if (M == kPairSpecialM)
+        sdtw_bwd_kernel<T, kPairSpecialM><<<grid, kWarpsPerCta * 32, bwd_smem_bytes<T>(), stream>>>(a);
+    else
+        sdtw_bwd_kernel<T, 0><<<grid, kWarpsPerCta * 32, bwd_smem_bytes<T>(), stream>>>(a);
     return from_cuda(cudaGetLastError());
 }
 
