@@ -160,14 +160,15 @@ __device__ __forceinline__ float split_row(unsigned char* head, unsigned char* t
 // specialise, communicating only through mbarriers:
 //   * warp 0 (TMA): E[128 rows x 32 columns] (128-byte swizzled) and Y[32 rows x DPAD] (plain boxes) of
 //     chunk q into raw stage q % S;
-//   * warps 2..9 (split, 256 threads): zero the clamped cells of E in flagged pairs (sign bit of D), split
+//   * warps 2..17 (split, 512 threads): zero the clamped cells of E in flagged pairs (sign bit of D), split
 //     E into TF32 head | tail (3xTF32) in place of the 128-byte swizzled rows of split buffer q % P, and
 //     transpose + split Y into its K-major rows; release the raw stage and mark the split buffer full;
 //   * warp 1 (MMA): 3 x 4 tcgen05.mma kind::tf32 per chunk into accumulator (tile & 1) in tensor memory,
 //     commit to the split buffer's "empty" barrier, and after a tile's last chunk to the accumulator's
 //     "full" barrier;
-//   * warps 10..13 (epilogue): read their 32 accumulator lanes (rows) with tcgen05.ld and write grad_X
-//     rows; the accumulator is double-buffered, so this overlaps the next tile's MMAs.
+//   * the last 8 warps (epilogue, two groups of four, one per feature half): read their 32 accumulator
+//     lanes (rows) with tcgen05.ld and write grad_X rows; the accumulator is double-buffered, so this
+//     overlaps the next tile's MMAs.
 // Every wait is bounded in time. A wait that runs out raises an abort word in shared memory that every
 // role polls, sets bit 1 of the library's distance error word, and the epilogue writes NaN into the rows
 // it has not finished; the TMA and MMA warps wait (bounded) for their own operations before the CTA
@@ -178,7 +179,8 @@ constexpr int kGKC = 32;                    // columns of E per chunk (one 128-b
 constexpr int kEChunk = kGT * kGKC * 4;     // 16 KB
 constexpr int kGradSplitWarps = 16;
 constexpr int kGradSplitThreads = 32 * kGradSplitWarps;
-constexpr int kGradThreads = 32 * (2 + kGradSplitWarps + 4);  // TMA, MMA, split, epilogue
+constexpr int kGradEpiWarps = 8;  // two groups of four (one per column half), each covering the 128 lanes
+constexpr int kGradThreads = 32 * (2 + kGradSplitWarps + kGradEpiWarps);  // TMA, MMA, split, epilogue
 constexpr int kGradEpiWarp0 = 2 + kGradSplitWarps;
 constexpr int kGradSmemBudget = 218 * 1024;
 
@@ -319,7 +321,7 @@ __global__ void __launch_bounds__(kGradThreads, 1) grad_x_tc_kernel(const __grid
         }
         for (int c = 0; c < 2; ++c) {
             mbar_init(acc_full + 8 * c, 1);
-            mbar_init(acc_empty + 8 * c, 4);
+            mbar_init(acc_empty + 8 * c, kGradEpiWarps);
         }
         *abort = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -491,14 +493,28 @@ __global__ void __launch_bounds__(kGradThreads, 1) grad_x_tc_kernel(const __grid
         }
     } else {
         // ---------------- epilogue ----------------
+        // Group eg (0, 1) writes features [eg * NC, eg * NC + NC) of its rows. The row of X it needs is
+        // loaded before the accumulator wait, so its latency overlaps the tile's products.
+        constexpr int NC = DPAD / 2;
+        constexpr bool kHoist = NC <= 32;  // X half row held in registers (NC / 4 float4)
         const int row = 32 * (warp & 3) + lane;  // accumulator lane of this thread
+        const int eg = (warp - kGradEpiWarp0) >> 2;
+        const int c0 = eg * NC;
         int tl = 0;
         for (; tl < my_tiles; ++tl) {
             const int ab = tl & 1;
-            if (!wait_role(acc_full + 8 * ab, (tl >> 1) & 1, a.timeout_ns, abort)) break;
-            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
             const int t = static_cast<int>(blockIdx.x) + tl * static_cast<int>(gridDim.x);
             const int b = t / a.nrt, i = (t % a.nrt) * kGT + row;
+            const float* xr = a.X + (static_cast<int64_t>(b) * a.N + (i < a.N ? i : 0)) * a.d;
+            float4 xv[kHoist ? NC / 4 : 1];
+            if constexpr (kHoist) {
+#pragma unroll
+                for (int e = 0; e < NC / 4; ++e)
+                    xv[e] = (i < a.N && c0 + 4 * e < a.d) ? __ldg(reinterpret_cast<const float4*>(xr + c0 + 4 * e))
+                                                         : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+            if (!wait_role(acc_full + 8 * ab, (tl >> 1) & 1, a.timeout_ns, abort)) break;
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
             const uint32_t acc = tmem + (static_cast<uint32_t>(32 * (warp & 3)) << 16) +
                                  static_cast<uint32_t>(ab) * G::ACC_COLS;
             float v[16];
@@ -506,23 +522,30 @@ __global__ void __launch_bounds__(kGradThreads, 1) grad_x_tc_kernel(const __grid
             asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
             const float rsum = v[0];
             const float g2 = 2.f * a.g[b];
-            const float* xr = a.X + (static_cast<int64_t>(b) * a.N + (i < a.N ? i : 0)) * a.d;
             float* orow = a.out + (static_cast<int64_t>(b) * a.N + i) * a.d;
 #pragma unroll
-            for (int c0 = 0; c0 < DPAD; c0 += 16) {
-                tmem_ld16_nowait(acc + c0, v);
+            for (int cc = 0; cc < NC; cc += 8) {
+                uint32_t r[8];
+                asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+                             : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+                               "=r"(r[7])
+                             : "r"(acc + static_cast<uint32_t>(c0 + cc)));
                 asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
                 if (i < a.N) {
 #pragma unroll
-                    for (int e = 0; e < 16; e += 4) {
-                        const int n = c0 + e;
+                    for (int e = 0; e < 8; e += 4) {
+                        const int n = c0 + cc + e;
                         if (n < a.d) {
-                            const float4 xv = __ldg(reinterpret_cast<const float4*>(xr + n));
+                            float4 x4;
+                            if constexpr (kHoist)
+                                x4 = xv[(cc + e) / 4];
+                            else
+                                x4 = __ldg(reinterpret_cast<const float4*>(xr + n));
                             float4 o;
-                            o.x = g2 * (rsum * xv.x - v[e]);
-                            o.y = g2 * (rsum * xv.y - v[e + 1]);
-                            o.z = g2 * (rsum * xv.z - v[e + 2]);
-                            o.w = g2 * (rsum * xv.w - v[e + 3]);
+                            o.x = g2 * (rsum * x4.x - __uint_as_float(r[e]));
+                            o.y = g2 * (rsum * x4.y - __uint_as_float(r[e + 1]));
+                            o.z = g2 * (rsum * x4.z - __uint_as_float(r[e + 2]));
+                            o.w = g2 * (rsum * x4.w - __uint_as_float(r[e + 3]));
                             *reinterpret_cast<float4*>(orow + n) = o;
                         }
                     }
@@ -537,7 +560,7 @@ __global__ void __launch_bounds__(kGradThreads, 1) grad_x_tc_kernel(const __grid
             const int t = static_cast<int>(blockIdx.x) + tl * static_cast<int>(gridDim.x);
             const int b = t / a.nrt, i = (t % a.nrt) * kGT + row;
             if (i < a.N)
-                for (int n = 0; n < a.d; ++n)
+                for (int n = c0; n < c0 + NC && n < a.d; ++n)
                     a.out[(static_cast<int64_t>(b) * a.N + i) * a.d + n] = __int_as_float(0x7fc00000);
         }
     }
@@ -556,28 +579,31 @@ __global__ void __launch_bounds__(kGradThreads, 1) grad_x_tc_kernel(const __grid
 // 32 (one 128-byte swizzle atom of fp32). Tiles blockIdx.x, blockIdx.x + gridDim.x, ... (the tiles of a pair
 // are consecutive, so X and Y rows are reused from L2); chunks are numbered q across the CTA's tiles.
 //   * warp 0 (TMA): X[128 rows x 32 features] and Y[128 x 32] of chunk q into stage q % S (128-byte
-//     swizzled);
+//     swizzled); three stages, so the load of a chunk has two chunks' products to arrive in;
 //   * warps 2..9 (split): thread r (< 128) takes X row r, thread 128 + r takes Y row r: split in place into a
-//     TF32 head and, in the stage's tail half, a TF32 tail (3xTF32), and accumulate the row's squared norm
-//     over the tile's chunks (written to norm buffer tile % 4 at the tile's last chunk);
+//     TF32 head and, in tail buffer q % 2, a TF32 tail (3xTF32), and accumulate the row's squared norm over
+//     the tile's chunks (written to norm buffer tile % 4 at the tile's last chunk);
 //   * warp 1 (MMA): 3 x 4 tcgen05.mma kind::tf32 per chunk into accumulator (tile & 1), commit to the
-//     stage's "empty" barrier (the TMA refills it), and after the tile's last chunk to "acc full";
-//   * warps 10..13 (epilogue): per 32-column slice, read the accumulator row (tcgen05.ld), form D, write
-//     it 128-byte swizzled into one of two staging buffers and store it with TMA; release the
-//     accumulator after the last slice.
+//     stage's and the tail buffer's "empty" barriers, and after the tile's last chunk to "acc full";
+//   * warps 10..17 (epilogue, two groups of four, one per column half): per 32-column slice, read the
+//     accumulator row (tcgen05.ld), form D, write it 128-byte swizzled into the group's staging buffer and
+//     store it with TMA; release the accumulator after the last slice.
 // Every wait is bounded; a wait that runs out raises the CTA's abort word and bit 1 of the distance error
 // word, and the epilogue writes NaN into the tiles it has not finished.
 // ==================================================================================================
-constexpr int kDThreads = 32 * (2 + 8 + 4);
+constexpr int kDThreads = 32 * (2 + 8 + 8);
 constexpr int kDSplit0 = 64;                        // first split thread
-constexpr int kDEpiWarp0 = 10;
-constexpr int kDStage = 4 * kChunk;                 // X head, Y head, X tail, Y tail: 64 KB
-constexpr int kDS = 2;                              // stages
+constexpr int kDEpiWarp0 = 10;                      // epilogue warps 10..17: lane quarter w % 4, column half
+constexpr int kDStage = 2 * kChunk;                 // X head, Y head (TMA destination, split in place): 32 KB
+constexpr int kDS = 3;                              // stages
+constexpr int kDP = 2;                              // tail buffers (X tail, Y tail: 32 KB each)
 constexpr int kDOffStage = 0;
-constexpr int kDOffOut = kDS * kDStage;             // 2 x 16 KB output staging
+constexpr int kDOffTail = kDS * kDStage;
+constexpr int kDOffOut = kDOffTail + kDP * 2 * kChunk;  // 2 column halves x 16 KB output staging
 constexpr int kDOffNorm = kDOffOut + 2 * kChunk;    // x2[4][128], y2[4][128]
 constexpr int kDOffBar = kDOffNorm + 2 * 4 * kT * 4;
-constexpr int kDNBar = 3 * kDS + 8;                 // full[S], split[S], empty[S], acc_full[2], acc_empty[2], norm[4]
+// full[S], ready[S], empty[S], tail_empty[P], acc_full[2], acc_empty[2], norm[4]
+constexpr int kDNBar = 3 * kDS + kDP + 8;
 constexpr int kDOffTmem = kDOffBar + 8 * kDNBar;
 constexpr int kDOffAbort = kDOffTmem + 8;
 constexpr int kDSmemBytes = kDOffAbort + 8 + 1024;
@@ -603,9 +629,10 @@ __global__ void __launch_bounds__(kDThreads, 1) pairwise_l2_tc_kernel(const __gr
     const uint32_t base = smem_addr(sm);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const uint32_t full = base + kDOffBar;
-    const uint32_t split = full + 8 * kDS;
+    const uint32_t split = full + 8 * kDS;       // "ready": heads (stage) and tails (buffer) of chunk q written
     const uint32_t empty = split + 8 * kDS;
-    const uint32_t acc_full = empty + 8 * kDS;
+    const uint32_t tail_empty = empty + 8 * kDS;
+    const uint32_t acc_full = tail_empty + 8 * kDP;
     const uint32_t acc_empty = acc_full + 16;
     const uint32_t norm_full = acc_empty + 16;  // [4]: the split wrote the norms of tile t (t % 4)
     volatile int* abort = reinterpret_cast<volatile int*>(sm + kDOffAbort);
@@ -631,9 +658,10 @@ __global__ void __launch_bounds__(kDThreads, 1) pairwise_l2_tc_kernel(const __gr
             mbar_init(split + 8 * s, 8);
             mbar_init(empty + 8 * s, 1);
         }
+        for (int p = 0; p < kDP; ++p) mbar_init(tail_empty + 8 * p, 1);
         for (int c = 0; c < 2; ++c) {
             mbar_init(acc_full + 8 * c, 1);
-            mbar_init(acc_empty + 8 * c, 4);
+            mbar_init(acc_empty + 8 * c, 8);
         }
         for (int c = 0; c < 4; ++c) mbar_init(norm_full + 8 * c, 8);
         *abort = 0;
@@ -662,7 +690,7 @@ __global__ void __launch_bounds__(kDThreads, 1) pairwise_l2_tc_kernel(const __gr
                 tile_of(q / a.nk, b, i0, j0);
                 const int kc = q % a.nk;
                 const uint32_t st = base + kDOffStage + s * kDStage;
-                mbar_expect_tx(full + 8 * s, 2 * kChunk);
+                mbar_expect_tx(full + 8 * s, kDStage);
                 tma_load_3d(st, &mx, full + 8 * s, kc * kKC, i0, b);
                 tma_load_3d(st + kChunk, &my, full + 8 * s, kc * kKC, j0, b);
                 issued = q + 1;
@@ -687,8 +715,9 @@ __global__ void __launch_bounds__(kDThreads, 1) pairwise_l2_tc_kernel(const __gr
                     }
                     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
                     const uint32_t st = base + kDOffStage + s * kDStage;
+                    const uint32_t tb = base + kDOffTail + (q % kDP) * 2 * kChunk;
                     const uint64_t xh = sw128_desc(st), yh = sw128_desc(st + kChunk);
-                    const uint64_t xl = sw128_desc(st + 2 * kChunk), yl = sw128_desc(st + 3 * kChunk);
+                    const uint64_t xl = sw128_desc(tb), yl = sw128_desc(tb + kChunk);
 #pragma unroll
                     for (int kk = 0; kk < kKC / 8; ++kk) {
                         const uint64_t o = static_cast<uint64_t>((kk * 32) >> 4);  // 8 TF32 = 32 bytes along K
@@ -698,6 +727,9 @@ __global__ void __launch_bounds__(kDThreads, 1) pairwise_l2_tc_kernel(const __gr
                     }
                     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
                                      empty + 8 * s)
+                                 : "memory");
+                    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                                     tail_empty + 8 * (q % kDP))
                                  : "memory");
                     if (kc == a.nk - 1)
                         asm volatile(
@@ -718,13 +750,15 @@ __global__ void __launch_bounds__(kDThreads, 1) pairwise_l2_tc_kernel(const __gr
             float nrm = 0.f;
             bool ok = true;
             for (int kc = 0; kc < a.nk; ++kc, ++q) {
-                const int s = q % kDS;
-                if (!wait_role(full + 8 * s, (q / kDS) & 1, a.timeout_ns, abort)) {
+                const int s = q % kDS, p = q % kDP;
+                if (!wait_role(full + 8 * s, (q / kDS) & 1, a.timeout_ns, abort) ||
+                    (q >= kDP && !wait_role(tail_empty + 8 * p, ((q / kDP) - 1) & 1, a.timeout_ns, abort))) {
                     ok = false;
                     break;
                 }
                 unsigned char* st = sm + kDOffStage + s * kDStage + (is_y ? kChunk : 0);
-                nrm += split_row(st + 128 * row, st + 2 * kChunk + 128 * row, row);
+                unsigned char* tb = sm + kDOffTail + p * 2 * kChunk + (is_y ? kChunk : 0);
+                nrm += split_row(st + 128 * row, tb + 128 * row, row);
                 if (kc == a.nk - 1) (is_y ? y2s : x2s)[(tl & 3) * kT + row] = nrm;
                 asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> tensor-core reads
                 __syncwarp();
@@ -737,11 +771,15 @@ __global__ void __launch_bounds__(kDThreads, 1) pairwise_l2_tc_kernel(const __gr
         }
     } else {
         // ---------------- epilogue ----------------
+        // Two groups of four warps; group h writes column slices 2h and 2h+1 of every tile through its own
+        // two staging buffers, synchronised by named barrier 1 + h.
         const int row = 32 * (warp & 3) + lane;     // accumulator lane = tile row
-        const int et = tid - 32 * kDEpiWarp0;       // 0..127
+        const int eg = (warp - kDEpiWarp0) >> 2;    // column half
+        const int et = tid - 32 * kDEpiWarp0 - 128 * eg;  // 0..127 within the group
         const bool leader = et == 0;
+        const uint32_t gbar = 1 + eg;
+        unsigned char* const gout = sm + kDOffOut + eg * kChunk;
         int tl = 0;
-        int slice = 0;  // output slices issued by this CTA (staging buffer = slice & 1)
         for (; tl < my_tiles; ++tl) {
             const int ab = tl & 1;
             if (!wait_role(acc_full + 8 * ab, (tl >> 1) & 1, a.timeout_ns, abort) ||
@@ -755,14 +793,14 @@ __global__ void __launch_bounds__(kDThreads, 1) pairwise_l2_tc_kernel(const __gr
             const int i = i0 + row;
             bool clamped = false;
 #pragma unroll 1
-            for (int qs = 0; qs < kT / 32; ++qs, ++slice) {
+            for (int qs = 2 * eg; qs < 2 * eg + 2; ++qs) {
                 float acc[32];
                 tmem_ld32(tmem + (static_cast<uint32_t>(32 * (warp & 3)) << 16) + static_cast<uint32_t>(ab * kT + 32 * qs),
                           acc);
-                // The staging buffer of this slice was last read by the store issued two slices ago.
-                if (leader) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
-                asm volatile("bar.sync 1, 128;" ::: "memory");
-                unsigned char* ob = sm + kDOffOut + (slice & 1) * kChunk + 128 * row;
+                // The group's staging buffer was last read by its previous store.
+                if (leader) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+                asm volatile("bar.sync %0, 128;" ::"r"(gbar) : "memory");
+                unsigned char* ob = gout + 128 * row;
 #pragma unroll
                 for (int u = 0; u < 8; ++u) {
                     float o[4];
@@ -776,9 +814,9 @@ __global__ void __launch_bounds__(kDThreads, 1) pairwise_l2_tc_kernel(const __gr
                     *reinterpret_cast<float4*>(ob + 16 * (u ^ (row & 7))) = make_float4(o[0], o[1], o[2], o[3]);
                 }
                 asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-                asm volatile("bar.sync 1, 128;" ::: "memory");
+                asm volatile("bar.sync %0, 128;" ::"r"(gbar) : "memory");
                 if (leader) {
-                    tma_store_3d(&md, base + kDOffOut + (slice & 1) * kChunk, j0 + 32 * qs, i0, b);
+                    tma_store_3d(&md, smem_addr(gout), j0 + 32 * qs, i0, b);
                     asm volatile("cp.async.bulk.commit_group;" ::: "memory");
                 }
             }
@@ -795,7 +833,7 @@ __global__ void __launch_bounds__(kDThreads, 1) pairwise_l2_tc_kernel(const __gr
                 tile_of(tl, b, i0, j0);
                 const int i = i0 + row;
                 if (i < a.N)
-                    for (int jl = 0; jl < kT && j0 + jl < a.M; ++jl)
+                    for (int jl = 64 * eg; jl < 64 * eg + 64 && j0 + jl < a.M; ++jl)
                         a.D[(static_cast<int64_t>(b) * a.N + i) * a.M + j0 + jl] = __int_as_float(0x7fc00000);
             }
         }
