@@ -1,7 +1,7 @@
 // Tensor-core (tcgen05, sm_100a) kernels of the squared-L2 module path, both fp32 with 3xTF32 products:
 // the cost matrix D = |x|^2 + |y|^2 - 2 X Y^T (clamped at 0, the clamp recorded as -0.0) and the gradient
 // grad_X = 2 g (rowsum(G) X - G Y). Both are persistent and warp-specialized: a TMA warp streams operand
-// chunks into shared memory (no multicast), split warps turn each fp32 operand into a TF32 head and tail
+// chunks into this CTA's own shared memory, split warps turn each fp32 operand into a TF32 head and tail
 // (x = head + tail to about 2^-22) so that head.head + head.tail + tail.head keeps fp32 accuracy, one thread
 // issues tcgen05.mma into fp32 accumulators in tensor memory, and epilogue warps read the accumulators back
 // with tcgen05.ld while the next tile's products run. Every mbarrier wait is bounded in time.
