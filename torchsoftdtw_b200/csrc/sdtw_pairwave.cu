@@ -43,6 +43,53 @@ __device__ __forceinline__ void st_release_cta_if(int* p, int v, bool pred)
         : "memory");
 }
 
+// ---- forward progress barriers -------------------------------------------------------------------
+// The forward publishes its strip's last row in groups of 8 steps. Group g (= step / 8) of the strip held
+// by warp w completes mbarrier g of warp w's array (count 1, arrived by lane 0 after the group's values
+// are in shared memory). Each barrier completes exactly once per non-empty strip that warp sweeps (the
+// groups the sweep does not reach are completed when the strip ends), so the consumer of the strip in
+// round r of that warp waits for parity r & 1. A round can only complete a barrier after the consumer of
+// the previous round has passed it: the strip W positions later depends, through the W-1 strips between,
+// on that consumer being 4 groups further on. An empty strip (rows past the pair's length) completes
+// nothing, and nothing waits after it. A waiting warp is suspended by mbarrier.try_wait instead of polling.
+__device__ __forceinline__ void fbar_init(uint32_t bar) { asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(bar) : "memory"); }
+__device__ __forceinline__ void fbar_arrive(uint32_t bar)
+{
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ bool fbar_try_wait(uint32_t bar, uint32_t parity)
+{
+    uint32_t ok;
+    asm volatile(
+        "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3; selp.b32 %0, 1, 0, p; }"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity), "r"(20000u)
+        : "memory");
+    return ok != 0;
+}
+// Warp-collective bounded wait for the phase of `bar` with the given parity. Returns false if the launch
+// aborted or the wait ran out (which raises kErrTimeout and aborts the launch).
+__device__ __forceinline__ bool fbar_wait(uint32_t bar, uint32_t parity, const Sync& sy, int lane)
+{
+    if (fbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = global_ns();
+    while (true) {
+        if (fbar_try_wait(bar, parity)) return true;
+        int stop = 0;
+        if (lane == 0) {
+            if (aborted(sy)) {
+                stop = 1;
+            } else if (global_ns() - t0 > sy.timeout_ns) {
+                raise_error(sy, kErrTimeout);
+                stop = 1;
+            }
+        }
+        if (__shfl_sync(kFull, stop, 0)) return false;
+    }
+}
+// Progress barriers per warp for rows of M columns: groups 0 .. 4 * (blocks + 1) - 1.
+inline __host__ __device__ int fwd_groups(int64_t M) { return 4 * (static_cast<int>((M + 30) / 32) + 2); }
+
 // Warp-collective bounded wait until *prog >= need. `seen` caches the last value read (all lanes read
 // the same word, so it is warp-uniform). Keys count columns, so need - seen is the number of steps the
 // producer still has to take: the warp sleeps for about that many steps (~100 ns each, at most 2 us)
@@ -92,7 +139,7 @@ struct PairFwdArgs {
     T* costs;
     Lengths len;
     int64_t B, N, M, bw;
-    int S, W, BL, P;
+    int S, W, BL, G;  // strips, warps, boundary row length, progress barriers per warp
     T k, gl;
     Sync sy;
     int64_t inject;  // b * S + s: that strip never publishes its boundary row (failure-path test); -1 = none
@@ -168,8 +215,8 @@ __device__ __forceinline__ void fwd_pair_steps8(T* cell, const T* top, int tau0,
 // One strip of the forward. Returns false if the launch aborted. MC > 0: the kernel is specialized on
 // M == MC, so every row offset in the ring's loads and stores is a compile-time constant.
 template <typename T, int MC>
-__device__ bool fwd_pair_strip(const PairFwdArgs<T>& a, T* ring, const T* bin, const int* pin, T* bout, int* pout,
-                               int64_t b, int s, int lane)
+__device__ bool fwd_pair_strip(const PairFwdArgs<T>& a, T* ring, const T* bin, uint32_t bars_in, uint32_t par_in,
+                               T* bout, uint32_t bars_out, int64_t b, int s, int lane)
 {
     const T INF = Num<T>::inf();
     const int64_t N = a.N, M = MC > 0 ? MC : a.M, pitch = M + 2;
@@ -188,6 +235,9 @@ __device__ bool fwd_pair_strip(const PairFwdArgs<T>& a, T* ring, const T* bin, c
         }
         for (int r = 0; r < nmat; ++r)
             for (int c = lane; c < M + 2; c += 32) Rrow[r * pitch + c] = INF;
+        // No barrier arrivals: every later strip of this pair is empty too, so nothing waits on this
+        // warp's barriers again (arriving here could lap the phase the strip below the previous round
+        // is still waiting for).
         return true;
     }
     const int k0 = st.c_begin >> 5;
@@ -219,11 +269,11 @@ __device__ bool fwd_pair_strip(const PairFwdArgs<T>& a, T* ring, const T* bin, c
     const int tstar = static_cast<int>(st.ny - 1) + lstar;
     const int bstar = (lstar >= 0 && lstar < 32) ? (tstar >> 5) : INT_MIN;
 
-    const int P = a.P;
-    const int key_in = (s - 1) * P + 32;  // the strip above has written its last row through column c: key_in + c
-    const int key_out = s * P + 32;       // after step tau this strip's last row is final through tau - 31
-    int seen = INT_MIN;
-    if (s > 0 && !wait_key(pin, key_in + 32 * k0 + 7, seen, a.sy, lane)) return false;
+    // Group g of the strip above publishes its last row through column 8g - 24, so the columns up to
+    // 8g + 7 that group g of this strip reads are complete with its group g + 4 (or, past its sweep, with
+    // the barriers completed when it ends).
+    const int glast = a.G - 1;
+    if (s > 0 && !fbar_wait(bars_in + 8 * min(4 * k0 + 4, glast), par_in, a.sy, lane)) return false;
     T upp = lane == 0 ? bin[32 * k0 - 1 + kBufPad] : INF;  // lane 0's diagonal predecessor
     T outp = INF;
     const int src_lane = (lane + 31) & 31;
@@ -241,19 +291,19 @@ __device__ bool fwd_pair_strip(const PairFwdArgs<T>& a, T* ring, const T* bin, c
 #pragma unroll 1
         for (int q = 0; q < 4; ++q) {
             const int t8 = tau0 + 8 * q;
-            if (s > 0 && !wait_key(pin, key_in + t8 + 7, seen, a.sy, lane)) return false;
+            if (s > 0 && !fbar_wait(bars_in + 8 * min(t8 / 8 + 4, glast), par_in, a.sy, lane)) return false;
             if (full)
                 fwd_pair_steps8<T, false>(cell + 8 * q, top + 8 * q, t8, st.A, st.Z, a.k, a.gl, src_lane, lane0,
                                           outp, upp);
             else
                 fwd_pair_steps8<T, true>(cell + 8 * q, top + 8 * q, t8, st.A, st.Z, a.k, a.gl, src_lane, lane0,
                                          outp, upp);
-            if (has_consumer) {
+            if (!skip) {
                 // Publish the last row's 8 new values (columns t8 - 31 .. t8 - 24) from the ring.
                 __syncwarp();
-                if (lane < 8) bout[t8 + lane - 31 + kBufPad] = last[8 * q + lane];
+                if (has_consumer && lane < 8) bout[t8 + lane - 31 + kBufPad] = last[8 * q + lane];
                 __syncwarp();
-                st_release_cta_if(pout, key_out + t8 + 7 - 31, lane == 0);
+                if (lane == 0) fbar_arrive(bars_out + 8 * (t8 / 8));
             }
         }
         __syncwarp();
@@ -263,12 +313,14 @@ __device__ bool fwd_pair_strip(const PairFwdArgs<T>& a, T* ring, const T* bin, c
         if (blk + 2 <= k1) fwd_pair_load<T>(Db, M, ring, blk + 2, st.rows, lane);
         cp_async_commit();
     }
-    if (has_consumer) {
+    if (!skip) {
         // The strip below may read columns past this sweep as its row above: they are out of band (+inf).
-        for (int c = 32 * k1 + 1 + lane; c + kBufPad < a.BL; c += 32) bout[c + kBufPad] = INF;
-        __threadfence_block();
+        if (has_consumer)
+            for (int c = 32 * k1 + 1 + lane; c + kBufPad < a.BL; c += 32) bout[c + kBufPad] = INF;
         __syncwarp();
-        st_release_cta_if(pout, s * P + P - 1, lane == 0);
+        // Complete the barriers of the groups this sweep did not reach (every barrier once per strip).
+        for (int g = lane; g < a.G; g += 32)
+            if (g < 4 * k0 || g > 4 * k1 + 3) fbar_arrive(bars_out + 8 * g);
     }
     return true;
 }
@@ -284,14 +336,15 @@ __global__ void __launch_bounds__(SDTW_PAIR_THREADS, SDTW_PAIR_MIN_CTAS) sdtw_fw
     T* bufs = rings + static_cast<size_t>(W) * 32 * kFwdStride;
     T* crow = bufs + static_cast<size_t>(W) * a.BL;
     T* scratch = crow + a.BL;  // 32 elements per warp
-    int* prog = reinterpret_cast<int*>(scratch + static_cast<size_t>(W) * 32);
+    const uint32_t bars = (smem_addr(scratch + static_cast<size_t>(W) * 32) + 7u) & ~7u;  // [W][G] mbarriers
     const int64_t b = blockIdx.x;
     const T INF = Num<T>::inf();
     // Zero the rings and boundary rows (stale shared memory must not feed NaN patterns to masked
     // cells); the row above strip 0 is +inf with R[-1][-1] = 0.
     for (int e = threadIdx.x; e < W * (32 * kFwdStride + a.BL); e += blockDim.x) rings[e] = T(0);
     for (int e = threadIdx.x; e < a.BL; e += blockDim.x) crow[e] = e == kBufPad - 1 ? T(0) : INF;
-    if (threadIdx.x < W) prog[threadIdx.x] = -1;
+    for (int e = threadIdx.x; e < W * a.G; e += blockDim.x) fbar_init(bars + 8 * e);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     // Padded rows 0 and N+1 of R (softdtw.cpp:114-121: +inf with R[b,0,0] = 0).
     T* Rb = a.R + b * (a.N + 2) * (a.M + 2);
     for (int64_t e = threadIdx.x; e < a.M + 2; e += blockDim.x) {
@@ -303,8 +356,9 @@ __global__ void __launch_bounds__(SDTW_PAIR_THREADS, SDTW_PAIR_MIN_CTAS) sdtw_fw
     for (int s = warp; s < a.S; s += W) {
         const int wp = (s + W - 1) % W;
         const T* bin = s > 0 ? bufs + static_cast<size_t>(wp) * a.BL : crow;
-        if (!fwd_pair_strip<T, MC>(a, ring, bin, prog + wp, bufs + static_cast<size_t>(warp) * a.BL, prog + warp, b,
-                                   s, lane))
+        const uint32_t par_in = static_cast<uint32_t>(((s - 1) / W) & 1);  // round of the strip above in its warp
+        if (!fwd_pair_strip<T, MC>(a, ring, bin, bars + 8 * wp * a.G, par_in, bufs + static_cast<size_t>(warp) * a.BL,
+                                   bars + 8 * warp * a.G, b, s, lane))
             break;
     }
     cp_async_wait<0>();
@@ -606,7 +660,7 @@ template <typename T>
 size_t pair_fwd_smem_bytes(int W, int64_t M)
 {
     return (static_cast<size_t>(W) * (32 * kFwdStride + 32) + static_cast<size_t>(W + 1) * buf_len(M)) * sizeof(T) +
-           static_cast<size_t>(W) * sizeof(int);
+           8 + static_cast<size_t>(W) * fwd_groups(M) * 8;
 }
 template <typename T>
 size_t pair_bwd_smem_bytes(int W, int64_t M)
@@ -678,7 +732,7 @@ cudaError_t pair_forward(const T* D, T* R, T* costs, const void* lx, const void*
     a.S = static_cast<int>(N > 0 ? (N + 31) / 32 : 1);
     a.W = W;
     a.BL = buf_len(M);
-    a.P = static_cast<int>(M + 128);
+    a.G = fwd_groups(M);
     a.k = static_cast<T>(1.4426950408889634 / gamma);
     a.gl = static_cast<T>(gamma * 0.6931471805599453);
     a.sy = sy;
