@@ -152,3 +152,46 @@ def test_identical_sequences_clamp(cuda):
     c = T.SoftDTW(gamma=0.1)(X, X.detach())
     c.sum().backward()
     assert torch.isfinite(c).all() and torch.isfinite(X.grad).all()
+
+
+@pytest.mark.parametrize("distance", ["l2_squared", "cosine"])
+def test_dp_dtype_float64_conditions_fp32_gradients(cuda, distance):
+    """dp_dtype=float64 with float32 inputs: costs and gradients come back in float32 and match the fp64
+    oracle to float32 rounding, on a configuration (small gamma, long paths) where the float32 dynamic
+    program's gradients are visibly noisy."""
+    g = torch.Generator().manual_seed(77)
+    B, N, M, d, gamma = 3, 96, 80, 32, 0.05
+    X = torch.randn(B, N, d, generator=g)
+    Y = torch.randn(B, M, d, generator=g)
+    lx, ly = torch.tensor([96, 90, 70]), torch.tensor([80, 80, 65])
+    Xd = X.to(cuda).requires_grad_(True)
+    costs = T.SoftDTW(gamma=gamma, distance=distance, dp_dtype=torch.float64)(Xd, Y.to(cuda), lx.to(cuda),
+                                                                               ly.to(cuda))
+    costs.sum().backward()
+    torch.cuda.synchronize()
+    T.check_errors(cuda)
+    assert costs.dtype == torch.float32 and Xd.grad.dtype == torch.float32
+    # reference in float64 through the same module with float64 inputs
+    X64 = X.double().to(cuda).requires_grad_(True)
+    c64 = T.SoftDTW(gamma=gamma, distance=distance)(X64, Y.double().to(cuda), lx.to(cuda), ly.to(cuda))
+    c64.sum().backward()
+    torch.cuda.synchronize()
+    np.testing.assert_allclose(costs.detach().cpu().numpy(), c64.detach().cpu().numpy(), rtol=1e-6)
+    g64 = X64.grad.cpu().numpy()
+    err = float(np.max(np.abs(Xd.grad.cpu().numpy().astype(np.float64) - g64)))
+    assert err <= 1e-5 * float(np.max(np.abs(g64))) + 1e-7, err
+    if distance == "l2_squared":
+        c_, gx64, _ = O.module_forward_backward(X.double().numpy(), Y.double().numpy(), lx.numpy(), ly.numpy(),
+                                                gamma)
+        np.testing.assert_allclose(g64, gx64, rtol=1e-8, atol=1e-10)
+
+
+def test_benchmark_sweep_runs(cuda, kernel_path):
+    """python -m torchsoftdtw_b200.benchmark: every configuration and spread is timed without error."""
+    if kernel_path != "auto":
+        pytest.skip("the sweep runs once, with the kernels chosen by shape")
+    from torchsoftdtw_b200 import benchmark as bm
+
+    rows = bm.run(min_time=0.002)
+    assert len(rows) == len(bm.GRID) * len(bm.SPREADS)
+    assert all(r["fwd_ms"] > 0 and r["fwdbwd_ms"] > 0 for r in rows)

@@ -208,3 +208,23 @@ def test_workloads_are_seeded_and_shaped():
 def test_headline_cell_count():
     _, _, lx, ly, w = workloads.make_inputs("medium", batch=2, d=1)
     assert workloads.count_cells(lx, ly, w.bandwidth) == 2 * 512 * 512
+
+
+def test_benchmark_sweep_batches_and_table():
+    """The sweep's batches follow the spread rules (lengths in [ceil-ish fraction * L, L], frames past a
+    sample's length zeroed) and the table has one row per measurement."""
+    import torch
+
+    from torchsoftdtw_b200 import benchmark as bm
+
+    for spread, lo in bm.SPREADS.items():
+        X, Y, lx, ly = bm.make_batch(16, 40, 3, spread, torch.device("cpu"), seed=1)
+        assert X.shape == (16, 40, 3) and Y.shape == (16, 40, 3)
+        first = max(1, round(lo * 40))
+        for t, lens in ((X, lx), (Y, ly)):
+            assert int(lens.min()) >= first and int(lens.max()) <= 40
+            for b in range(16):
+                assert torch.count_nonzero(t[b, int(lens[b]):]) == 0
+    rows = [{"B": 2, "L": 8, "D": 1, "spread": "none", "cells": 128.0, "fwd_ms": 0.5, "fwdbwd_ms": 1.0}]
+    text = bm.table(rows, "dev")
+    assert text.count("\n| 2 | 8 | 1 | none |") == 1 and "2.560e+05" in text

@@ -115,6 +115,7 @@ def soft_dtw(
     lengths_y: torch.Tensor | None = None,
     gamma: float = 1.0,
     bandwidth: int = -1,
+    dp_dtype: torch.dtype | None = None,
 ) -> torch.Tensor:
     """Compute soft-DTW on a pre-computed cost matrix.
 
@@ -126,6 +127,12 @@ def soft_dtw(
         bandwidth: Sakoe-Chiba bandwidth around the diagonal joining (0, 0) to (lengths_x - 1, lengths_y - 1),
             in steps along the longer axis. Floored at half the diagonal's slope so that a warping path always
             exists. -1 means no constraint.
+        dp_dtype: dtype the dynamic program runs in (None: D's accumulation dtype, as in the reference).
+            ``torch.float64`` for a float32 D is the better-conditioned option: the backward's softmin
+            weights come from differences of neighbouring R values, which in float32 carry an absolute
+            error of about ulp(R) and, divided by a small gamma, make float32 gradients noisy; in float64
+            they do not. Costs and gradients are returned in D's dtype. An addition of this package (the
+            reference has no such argument); the default leaves the reference's behaviour unchanged.
 
     Returns:
         costs: (B,) soft-DTW values.
@@ -135,6 +142,8 @@ def soft_dtw(
         lengths_x = torch.full((B,), N, dtype=torch.long, device=D.device)
     if lengths_y is None:
         lengths_y = torch.full((B,), M, dtype=torch.long, device=D.device)
+    if dp_dtype is not None and dp_dtype != D.dtype:
+        return SoftDTWAutograd.apply(D.to(dp_dtype), lengths_x, lengths_y, gamma, bandwidth).to(D.dtype)
     return SoftDTWAutograd.apply(D, lengths_x, lengths_y, gamma, bandwidth)
 
 
@@ -145,6 +154,7 @@ class SoftDTW(nn.Module):
         bandwidth: int = -1,
         normalize: bool = False,
         distance: str = "l2_squared",
+        dp_dtype: torch.dtype | None = None,
     ):
         """
         Args:
@@ -155,6 +165,10 @@ class SoftDTW(nn.Module):
             normalize: Divide the cost by path length (lengths_x + lengths_y - 1).
             distance: Pairwise distance used to build the cost matrix from X, Y.
                 One of "l2_squared", "l1", "cosine".
+            dp_dtype: dtype of the computation (None: the inputs' accumulation dtype, as in the reference).
+                ``torch.float64`` with float32 inputs is the better-conditioned option (see ``soft_dtw``):
+                the cost matrix and the dynamic program run in float64 and the costs and gradients come back
+                in the inputs' dtype. Not an argument of the reference; the default keeps its behaviour.
         """
         super().__init__()
         if distance not in PAIRWISE_DISTANCES:
@@ -163,6 +177,7 @@ class SoftDTW(nn.Module):
         self.bandwidth = bandwidth
         self.normalize = normalize
         self.distance = distance
+        self.dp_dtype = dp_dtype
 
     def forward(
         self,
@@ -186,6 +201,10 @@ class SoftDTW(nn.Module):
             X = X.unsqueeze(0)
         if Y.dim() == 2:
             Y = Y.unsqueeze(0)
+        out_dtype = None
+        if self.dp_dtype is not None and (X.dtype != self.dp_dtype or Y.dtype != self.dp_dtype):
+            out_dtype = torch.promote_types(X.dtype, Y.dtype)
+            X, Y = X.to(self.dp_dtype), Y.to(self.dp_dtype)
 
         B = X.size(0)
 
@@ -197,12 +216,10 @@ class SoftDTW(nn.Module):
             D = PAIRWISE_DISTANCES[self.distance](X, Y)
             costs = soft_dtw(D, lengths_x, lengths_y, self.gamma, self.bandwidth)
 
-        if not self.normalize:
-            return costs
-
-        if lengths_x is None:
-            lengths_x = torch.full((B,), X.size(1), dtype=torch.long, device=X.device)
-        if lengths_y is None:
-            lengths_y = torch.full((B,), Y.size(1), dtype=torch.long, device=Y.device)
-
-        return costs / (lengths_x + lengths_y - 1).to(costs.dtype)
+        if self.normalize:
+            if lengths_x is None:
+                lengths_x = torch.full((B,), X.size(1), dtype=torch.long, device=X.device)
+            if lengths_y is None:
+                lengths_y = torch.full((B,), Y.size(1), dtype=torch.long, device=Y.device)
+            costs = costs / (lengths_x + lengths_y - 1).to(costs.dtype)
+        return costs if out_dtype is None else costs.to(out_dtype)
