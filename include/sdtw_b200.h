@@ -134,6 +134,25 @@ sdtw_status sdtw_grad_l2(sdtw_dtype dtype, const void* X, const void* Y, const v
                          const void* g, const int* clamp_flags, int64_t B, int64_t N, int64_t M, int64_t d,
                          void* grad_X, void* grad_Y, void* stream);
 
+/* ---------------------------------------------------------------------------------------------------
+ * L1 and cosine cost matrices (the module's distance="l1" / "cosine" path) and their gradients.
+ * Replace the reference's pairwise_l1 and pairwise_cosine (src/torchsoftdtw/distances.py:21-50) and their
+ * autograd; the reference's L1 expression materialises a (B, N, M, d) difference tensor, these do not.
+ *   kind SDTW_DIST_L1:      D[b,i,j] = sum_k |x_ik - y_jk|                     (eps unused, must be > 0)
+ *   kind SDTW_DIST_COSINE:  D[b,i,j] = 1 - x_i.y_j / (max(|x_i|, eps) max(|y_j|, eps))
+ * sdtw_grad_dist returns the gradient of sum_b g[b] * sum_ij E[b,i,j] D[b,i,j] (E from sdtw_backward,
+ * g the (B,) upstream gradient of the costs): sgn(0) = 0 for L1, and no gradient through the eps floor of
+ * a norm for cosine (torch's abs and clamp_min). D (the cost matrix) is read by the cosine gradient only.
+ * grad_X / grad_Y may be NULL to skip them. CUDA-core kernels, fp32 or fp64.
+ * ------------------------------------------------------------------------------------------------- */
+#define SDTW_DIST_L1 1
+#define SDTW_DIST_COSINE 2
+sdtw_status sdtw_pairwise_dist(sdtw_dtype dtype, int kind, const void* X, const void* Y, int64_t B, int64_t N,
+                               int64_t M, int64_t d, double eps, void* D, void* stream);
+sdtw_status sdtw_grad_dist(sdtw_dtype dtype, int kind, const void* X, const void* Y, const void* D, const void* E,
+                           const void* g, int64_t B, int64_t N, int64_t M, int64_t d, double eps, void* grad_X,
+                           void* grad_Y, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -261,6 +261,64 @@ std::tuple<Tensor, Tensor> l2_backward_cuda(const Tensor& X, const Tensor& Y, co
     return {gX, gY};
 }
 
+// ---------------------------------------------------------------------------------------------------
+// torchsoftdtw_b200::dist_forward / dist_backward — the SoftDTW module's L1 (kind 1) and cosine (kind 2)
+// paths: the cost matrix from X, Y in this library's kernels, then the same wavefront ops.
+// ---------------------------------------------------------------------------------------------------
+void kind_check(int64_t kind, double eps)
+{
+    TORCH_CHECK(kind == SDTW_DIST_L1 || kind == SDTW_DIST_COSINE, "distance kind must be 1 (l1) or 2 (cosine)");
+    TORCH_CHECK(eps > 0, "eps must be positive");
+}
+
+// Returns (costs, R, D).
+std::tuple<Tensor, Tensor, Tensor> dist_forward_cuda(const Tensor& X, const Tensor& Y, const Tensor& lengths_x,
+                                                     const Tensor& lengths_y, double gamma, int64_t bandwidth,
+                                                     int64_t kind, double eps)
+{
+    xy_checks(X, Y, lengths_x, lengths_y, gamma);
+    kind_check(kind, eps);
+    const c10::cuda::CUDAGuard guard(X.device());
+    const auto acc = acc_type(X.scalar_type());
+    const Tensor Xc = X.to(acc).contiguous(), Yc = Y.to(acc).contiguous();
+    const int64_t B = Xc.size(0), N = Xc.size(1), M = Yc.size(1), d = Xc.size(2);
+    Tensor D = at::empty({B, N, M}, Xc.options());
+    cudaStream_t stream = at::cuda::getCurrentCUDAStream(X.get_device()).stream();
+    check_status(sdtw_pairwise_dist(code_of(acc), static_cast<int>(kind), Xc.data_ptr(), Yc.data_ptr(), B, N, M, d,
+                                    eps, D.data_ptr(), stream),
+                 "pairwise_dist");
+    auto [costs, R] = run_forward(D, prep_lengths(lengths_x), prep_lengths(lengths_y), gamma, bandwidth);
+    return {costs, R, D};
+}
+
+std::tuple<Tensor, Tensor> dist_backward_cuda(const Tensor& X, const Tensor& Y, const Tensor& D, const Tensor& R,
+                                              const Tensor& lengths_x, const Tensor& lengths_y,
+                                              const Tensor& grad_costs, double gamma, int64_t bandwidth,
+                                              int64_t kind, double eps, bool need_x, bool need_y)
+{
+    xy_checks(X, Y, lengths_x, lengths_y, gamma);
+    kind_check(kind, eps);
+    const c10::cuda::CUDAGuard guard(X.device());
+    const auto acc = acc_type(X.scalar_type());
+    const Tensor Xc = X.to(acc).contiguous(), Yc = Y.to(acc).contiguous();
+    const int64_t B = Xc.size(0), N = Xc.size(1), M = Yc.size(1), d = Xc.size(2);
+    TORCH_CHECK(D.sizes() == at::IntArrayRef({B, N, M}) && D.scalar_type() == acc, "D has the wrong shape or dtype");
+    TORCH_CHECK(R.sizes() == at::IntArrayRef({B, N + 2, M + 2}) && R.scalar_type() == acc,
+                "R has the wrong shape or dtype");
+    Tensor E = run_backward(R.contiguous(), prep_lengths(lengths_x), prep_lengths(lengths_y), gamma, bandwidth, N, M);
+    const Tensor g = grad_costs.to(acc).contiguous();
+    Tensor gX = need_x ? at::empty({B, N, d}, Xc.options()) : at::empty({0}, X.options());
+    Tensor gY = need_y ? at::empty({B, M, d}, Xc.options()) : at::empty({0}, Y.options());
+    cudaStream_t stream = at::cuda::getCurrentCUDAStream(X.get_device()).stream();
+    check_status(sdtw_grad_dist(code_of(acc), static_cast<int>(kind), Xc.data_ptr(), Yc.data_ptr(),
+                                D.contiguous().data_ptr(), E.data_ptr(), g.data_ptr(), B, N, M, d, eps,
+                                need_x ? gX.data_ptr() : nullptr, need_y ? gY.data_ptr() : nullptr, stream),
+                 "grad_dist");
+    if (need_x && gX.scalar_type() != X.scalar_type()) gX = gX.to(X.scalar_type());
+    if (need_y && gY.scalar_type() != Y.scalar_type()) gY = gY.to(Y.scalar_type());
+    return {gX, gY};
+}
+
 Tensor error_bits(const Tensor& like)
 {
     // Reads and clears the sticky device error word of like's device (synchronises the current stream).
@@ -298,6 +356,11 @@ TORCH_LIBRARY(torchsoftdtw_b200, m)
     m.def("l2_backward(Tensor X, Tensor Y, Tensor D, Tensor R, Tensor clamp_flags, Tensor lengths_x, "
           "Tensor lengths_y, Tensor grad_costs, float gamma, int bandwidth, bool need_x, bool need_y) "
           "-> (Tensor, Tensor)");
+    m.def("dist_forward(Tensor X, Tensor Y, Tensor lengths_x, Tensor lengths_y, float gamma, int bandwidth, "
+          "int kind, float eps) -> (Tensor, Tensor, Tensor)");
+    m.def("dist_backward(Tensor X, Tensor Y, Tensor D, Tensor R, Tensor lengths_x, Tensor lengths_y, "
+          "Tensor grad_costs, float gamma, int bandwidth, int kind, float eps, bool need_x, bool need_y) "
+          "-> (Tensor, Tensor)");
     m.def("error_bits(Tensor like) -> Tensor");
 }
 
@@ -305,5 +368,7 @@ TORCH_LIBRARY_IMPL(torchsoftdtw_b200, CUDA, m)
 {
     m.impl("l2_forward", &l2_forward_cuda);
     m.impl("l2_backward", &l2_backward_cuda);
+    m.impl("dist_forward", &dist_forward_cuda);
+    m.impl("dist_backward", &dist_backward_cuda);
     m.impl("error_bits", &error_bits);
 }

@@ -1,10 +1,10 @@
 """Pairwise cost functions, with the reference's names and semantics
 (``src/torchsoftdtw/distances.py:4-57``).
 
-These are differentiable tensor expressions usable on any device. On CUDA, the ``SoftDTW`` module does
-not call :func:`pairwise_l2_squared` for ``distance="l2_squared"``: it runs the squared-L2 cost, the
-wavefront and the gradient contraction in this library's kernels (``torchsoftdtw_b200::l2_forward`` /
-``l2_backward``). ``l1`` and ``cosine`` build D with these expressions and then run the Soft-DTW kernels.
+These are differentiable tensor expressions usable on any device. On CUDA the ``SoftDTW`` module does
+not call them: it computes the cost matrix, the wavefront and the gradient contraction in this library's
+kernels (``torchsoftdtw_b200::l2_forward`` / ``l2_backward`` for ``l2_squared``, ``dist_forward`` /
+``dist_backward`` for ``l1`` and ``cosine``, with the same eps = 1e-8 floor of the cosine norms).
 """
 
 import torch

@@ -63,6 +63,21 @@ def _l2_backward_fake(X, Y, D, R, clamp_flags, lengths_x, lengths_y, grad_costs,
     return gX, gY
 
 
+@torch.library.register_fake("torchsoftdtw_b200::dist_forward")
+def _dist_forward_fake(X, Y, lengths_x, lengths_y, gamma, bandwidth, kind, eps):
+    B, N, M = X.shape[0], X.shape[1], Y.shape[1]
+    acc = _acc_dtype(X.dtype)
+    return (X.new_empty((B,), dtype=acc), X.new_empty((B, N + 2, M + 2), dtype=acc),
+            X.new_empty((B, N, M), dtype=acc))
+
+
+@torch.library.register_fake("torchsoftdtw_b200::dist_backward")
+def _dist_backward_fake(X, Y, D, R, lengths_x, lengths_y, grad_costs, gamma, bandwidth, kind, eps, need_x, need_y):
+    gX = X.new_empty(X.shape) if need_x else X.new_empty((0,))
+    gY = Y.new_empty(Y.shape) if need_y else Y.new_empty((0,))
+    return gX, gY
+
+
 class SoftDTWAutograd(Function):
     """Autograd of the op pair (``softdtw.py:33-48``): saves D and R, returns grad_output * E."""
 
@@ -107,6 +122,36 @@ class _SoftDTWL2(Function):
             X, Y, D, R, flags, lengths_x, lengths_y, grad_costs.contiguous(), ctx.gamma, ctx.bandwidth, need_x, need_y
         )
         return (gX if need_x else None), (gY if need_y else None), None, None, None, None
+
+
+# distance name -> kind code of the native L1 / cosine cost kernels
+_DIST_KIND = {"l1": 1, "cosine": 2}
+_COSINE_EPS = 1e-8  # pairwise_cosine's default floor of the norms (distances.py:34)
+
+
+class _SoftDTWDist(Function):
+    """L1 / cosine path: the cost matrix from (X, Y) in native kernels, the Soft-DTW ops, and the gradient
+    w.r.t. X and Y contracted in native kernels (no (B, N, M, d) difference tensor, no grad_output * E).
+    Mathematically the composition pairwise_l1 / pairwise_cosine -> SoftDTWAutograd."""
+
+    @staticmethod
+    @torch.amp.custom_fwd(device_type="cuda")
+    def forward(ctx, X, Y, lengths_x, lengths_y, gamma, bandwidth, kind, eps):
+        costs, R, D = torch.ops.torchsoftdtw_b200.dist_forward(X, Y, lengths_x, lengths_y, gamma, bandwidth, kind,
+                                                               eps)
+        ctx.save_for_backward(X, Y, D, R, lengths_x, lengths_y)
+        ctx.gamma, ctx.bandwidth, ctx.kind, ctx.eps = gamma, bandwidth, kind, eps
+        return costs
+
+    @staticmethod
+    @torch.amp.custom_bwd(device_type="cuda")
+    def backward(ctx, grad_costs):
+        X, Y, D, R, lengths_x, lengths_y = ctx.saved_tensors
+        need_x, need_y = bool(ctx.needs_input_grad[0]), bool(ctx.needs_input_grad[1])
+        gX, gY = torch.ops.torchsoftdtw_b200.dist_backward(
+            X, Y, D, R, lengths_x, lengths_y, grad_costs.contiguous(), ctx.gamma, ctx.bandwidth, ctx.kind, ctx.eps,
+            need_x, need_y)
+        return (gX if need_x else None), (gY if need_y else None), None, None, None, None, None, None
 
 
 def soft_dtw(
@@ -208,10 +253,14 @@ class SoftDTW(nn.Module):
 
         B = X.size(0)
 
-        if self.distance == "l2_squared" and X.is_cuda and Y.is_cuda and X.dtype == Y.dtype:
+        if X.is_cuda and Y.is_cuda and X.dtype == Y.dtype:
             lx = lengths_x if lengths_x is not None else torch.full((B,), X.size(1), dtype=torch.long, device=X.device)
             ly = lengths_y if lengths_y is not None else torch.full((B,), Y.size(1), dtype=torch.long, device=X.device)
-            costs = _SoftDTWL2.apply(X, Y, lx, ly, self.gamma, self.bandwidth)
+            if self.distance == "l2_squared":
+                costs = _SoftDTWL2.apply(X, Y, lx, ly, self.gamma, self.bandwidth)
+            else:
+                costs = _SoftDTWDist.apply(X, Y, lx, ly, self.gamma, self.bandwidth, _DIST_KIND[self.distance],
+                                           _COSINE_EPS)
         else:
             D = PAIRWISE_DISTANCES[self.distance](X, Y)
             costs = soft_dtw(D, lengths_x, lengths_y, self.gamma, self.bandwidth)
