@@ -143,15 +143,20 @@ sdtw_status sdtw_grad_l2(sdtw_dtype dtype, const void* X, const void* Y, const v
  * sdtw_grad_dist returns the gradient of sum_b g[b] * sum_ij E[b,i,j] D[b,i,j] (E from sdtw_backward,
  * g the (B,) upstream gradient of the costs): sgn(0) = 0 for L1, and no gradient through the eps floor of
  * a norm for cosine (torch's abs and clamp_min). D (the cost matrix) is read by the cosine gradient only.
- * grad_X / grad_Y may be NULL to skip them. CUDA-core kernels, fp32 or fp64.
+ * grad_X / grad_Y may be NULL to skip them. fp32 or fp64. L1: CUDA-core kernels. Cosine in fp32 with
+ * d % 4 == 0, M % 4 == 0 (and d <= 128 for grad_X) and 16-byte aligned arrays: the cost matrix and grad_X
+ * run on the tcgen05 tensor cores (3xTF32), grad_X only when a workspace of
+ * sdtw_grad_dist_workspace_bytes(B, M, dtype) bytes (device memory, any content, 16-byte aligned) is
+ * given; with workspace NULL, or otherwise, CUDA-core kernels.
  * ------------------------------------------------------------------------------------------------- */
 #define SDTW_DIST_L1 1
 #define SDTW_DIST_COSINE 2
 sdtw_status sdtw_pairwise_dist(sdtw_dtype dtype, int kind, const void* X, const void* Y, int64_t B, int64_t N,
                                int64_t M, int64_t d, double eps, void* D, void* stream);
+size_t sdtw_grad_dist_workspace_bytes(int64_t B, int64_t M, sdtw_dtype dtype);
 sdtw_status sdtw_grad_dist(sdtw_dtype dtype, int kind, const void* X, const void* Y, const void* D, const void* E,
-                           const void* g, int64_t B, int64_t N, int64_t M, int64_t d, double eps, void* grad_X,
-                           void* grad_Y, void* stream);
+                           const void* g, int64_t B, int64_t N, int64_t M, int64_t d, double eps, void* workspace,
+                           void* grad_X, void* grad_Y, void* stream);
 
 #ifdef __cplusplus
 }

@@ -6,7 +6,10 @@ ctypes front end for two CPU checkers:
   (``src/torchsoftdtw/csrc/softdtw.cpp:97-285``, ``band.h:23-38``), built by ``make -C oracle``;
 * ``_ref/libsoftdtw_ref_cpu.so`` — the reference's own CPU operator compiled from its source file
   (``make -C oracle ref``; only possible where the reference sources exist). It registers the ops
-  ``torch.ops.torchsoftdtw_ref.forward/backward`` with the reference's schemas.
+  ``torch.ops.torchsoftdtw_ref.forward/backward`` with the reference's schemas;
+* ``_ref/libsoftdtw_ref_cuda.so`` — the reference's CUDA operator (``csrc/cuda/softdtw.cu``) compiled from
+  its sources for sm_100 (``make -C oracle ref-cuda``), ops ``torch.ops.torchsoftdtw_refcu.forward/backward``:
+  the GPU implementation the tests compare against on the same device.
 
 Only ``tests/``, ``__graft_entry__.smoke()`` and ``bench.py`` (CPU baseline / reference arm) use it.
 """
@@ -22,9 +25,11 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 ORACLE_SO = os.path.join(HERE, "liboracle_softdtw.so")
 REF_SO = os.path.join(HERE, "_ref", "libsoftdtw_ref_cpu.so")
+REF_CUDA_SO = os.path.join(HERE, "_ref", "libsoftdtw_ref_cuda.so")
 
 _lib = None
 _ref_loaded = False
+_ref_cuda_loaded = False
 
 _i64 = ctypes.c_int64
 _p = ctypes.c_void_p
@@ -34,7 +39,7 @@ def build() -> None:
     """Compile the C restatement (and the reference, when its sources are mounted)."""
     subprocess.run(["make", "-s", "-C", HERE, "all"], check=True)
     if os.path.isdir("/root/reference/src"):
-        subprocess.run(["make", "-s", "-C", HERE, "ref"], check=True)
+        subprocess.run(["make", "-s", "-C", HERE, "ref", "ref-cuda"], check=True)
 
 
 def lib() -> ctypes.CDLL:
@@ -165,3 +170,17 @@ def load_ref():
         torch.ops.load_library(REF_SO)
         _ref_loaded = True
     return torch.ops.torchsoftdtw_ref
+
+
+def load_ref_cuda():
+    """Load the compiled reference CUDA operator; returns torch.ops.torchsoftdtw_refcu (its CPU kernels
+    are registered too)."""
+    global _ref_cuda_loaded
+    import torch
+
+    if not _ref_cuda_loaded:
+        if not os.path.exists(REF_CUDA_SO):
+            raise FileNotFoundError(f"{REF_CUDA_SO} is missing: build it with `make -C oracle ref-cuda`")
+        torch.ops.load_library(REF_CUDA_SO)
+        _ref_cuda_loaded = True
+    return torch.ops.torchsoftdtw_refcu

@@ -42,14 +42,17 @@ def dist(kind, X, Y, eps=EPS):
     return D
 
 
-def grad(kind, X, Y, D, E, g, need_x=True, need_y=True, eps=EPS):
+def grad(kind, X, Y, D, E, g, need_x=True, need_y=True, eps=EPS, workspace=True):
     lib = _ext.capi()
     B, N, d = X.shape
     M = Y.shape[1]
+    dt = 1 if X.dtype == torch.float64 else 0
     gX = torch.empty_like(X) if need_x else None
     gY = torch.empty_like(Y) if need_y else None
-    st = lib.sdtw_grad_dist(1 if X.dtype == torch.float64 else 0, KIND[kind], p(X), p(Y), p(D), p(E), p(g), B, N, M,
-                            d, eps, p(gX), p(gY), stream())
+    ws = torch.empty(lib.sdtw_grad_dist_workspace_bytes(B, M, dt), dtype=torch.uint8, device=X.device) if workspace \
+        else None
+    st = lib.sdtw_grad_dist(dt, KIND[kind], p(X), p(Y), p(D), p(E), p(g), B, N, M, d, eps, p(ws), p(gX), p(gY),
+                            stream())
     assert st == 0, lib.sdtw_status_string(st)
     torch.cuda.synchronize()
     return gX, gY
@@ -75,13 +78,26 @@ def inputs(B, N, M, d, seed, dtype, zero_rows=False):
     return X, Y
 
 
-SHAPES = [(1, 1, 1, 1), (2, 7, 5, 3), (3, 64, 64, 16), (2, 65, 130, 17), (1, 200, 96, 40), (2, 33, 300, 129)]
+SHAPES = [(1, 1, 1, 1), (2, 7, 5, 3), (3, 64, 64, 16), (2, 65, 130, 17), (1, 200, 96, 40), (2, 33, 300, 129),
+          (2, 130, 260, 64), (1, 300, 132, 128), (3, 129, 64, 12), (1, 64, 520, 200)]
+
+# Cosine in fp32 runs the tcgen05 kernels where the shape allows (auto); "cuda_cores" forces the
+# CUDA-core kernels.
+DISTANCE_PATHS = {"auto": 0, "cuda_cores": 2}
+
+
+@pytest.fixture(params=list(DISTANCE_PATHS))
+def distance_path(request):
+    lib = _ext.capi()
+    lib.sdtw_debug_force_distance_path(DISTANCE_PATHS[request.param])
+    yield request.param
+    lib.sdtw_debug_force_distance_path(0)
 
 
 @pytest.mark.parametrize("kind", ["l1", "cosine"])
 @pytest.mark.parametrize("B,N,M,d", SHAPES)
 @pytest.mark.parametrize("dtype", [torch.float32, torch.float64])
-def test_cost_matches_fp64(cuda, kind, B, N, M, d, dtype):
+def test_cost_matches_fp64(cuda, distance_path, kind, B, N, M, d, dtype):
     X, Y = inputs(B, N, M, d, 1000 + N + M + d, dtype, zero_rows=(kind == "cosine"))
     Xd, Yd = X.to(dtype), Y.to(dtype)
     D = dist(kind, Xd.to(cuda), Yd.to(cuda)).cpu().double().numpy()
@@ -98,7 +114,7 @@ def test_cost_matches_fp64(cuda, kind, B, N, M, d, dtype):
 @pytest.mark.parametrize("kind", ["l1", "cosine"])
 @pytest.mark.parametrize("B,N,M,d", SHAPES[1:])
 @pytest.mark.parametrize("dtype", [torch.float32, torch.float64])
-def test_grad_matches_autograd_fp64(cuda, kind, B, N, M, d, dtype):
+def test_grad_matches_autograd_fp64(cuda, distance_path, kind, B, N, M, d, dtype):
     X, Y = inputs(B, N, M, d, 2000 + N + M + d, dtype, zero_rows=(kind == "cosine"))
     gen = torch.Generator().manual_seed(7)
     E = torch.rand(B, N, M, generator=gen, dtype=torch.float64)
@@ -112,21 +128,28 @@ def test_grad_matches_autograd_fp64(cuda, kind, B, N, M, d, dtype):
 
     Xc, Yc = X.to(dtype).to(cuda), Y.to(dtype).to(cuda)
     D = dist(kind, Xc, Yc)
-    gX, gY = grad(kind, Xc, Yc, D, E.to(dtype).to(cuda), g.to(dtype).to(cuda))
-    for ours, ref in ((gX, Xr.grad), (gY, Yr.grad)):
+    Ec, gc = E.to(dtype).to(cuda), g.to(dtype).to(cuda)
+    gX, gY = grad(kind, Xc, Yc, D, Ec, gc)
+    gX_nows, _ = grad(kind, Xc, Yc, D, Ec, gc, need_y=False, workspace=False)  # no workspace: CUDA cores
+    tol = 1e-11 if dtype == torch.float64 else 2e-5
+    for ours, ref, A in ((gX, Xr.grad, X), (gY, Yr.grad, Y), (gX_nows, Xr.grad, X)):
         ours = ours.cpu().double()
-        scale = ref.abs().max().item() + 1e-30
-        tol = 1e-11 if dtype == torch.float64 else 2e-5
-        err = (ours - ref).abs().max().item() / scale
-        assert err < tol, (kind, err)
+        # rows of zero norm (cosine) have gradients ~1/eps: check them and the others at their own scales
+        live = A.norm(dim=-1) > 0
+        for sel in (live, ~live):
+            if sel.any():
+                scale = ref[sel].abs().max().item() + 1e-30
+                err = (ours[sel] - ref[sel]).abs().max().item() / scale
+                assert err < tol, (kind, err)
 
 
 @pytest.mark.parametrize("kind", ["l1", "cosine"])
-def test_grad_selection(cuda, kind):
-    X, Y = inputs(2, 40, 30, 9, 5, torch.float32)
+@pytest.mark.parametrize("M,d", [(30, 9), (32, 16)])
+def test_grad_selection(cuda, kind, M, d):
+    X, Y = inputs(2, 40, M, d, 5, torch.float32)
     Xc, Yc = X.float().to(cuda), Y.float().to(cuda)
     D = dist(kind, Xc, Yc)
-    E = torch.rand(2, 40, 30, device=cuda)
+    E = torch.rand(2, 40, M, device=cuda)
     g = torch.ones(2, device=cuda)
     gx_both, gy_both = grad(kind, Xc, Yc, D, E, g)
     gx, none = grad(kind, Xc, Yc, D, E, g, need_y=False)
@@ -146,12 +169,13 @@ def test_invalid_arguments_are_rejected(cuda):
 
 @pytest.mark.parametrize("distance", ["l1", "cosine"])
 @pytest.mark.parametrize("dtype", [torch.float32, torch.float64])
-def test_module_matches_unfused_composition(cuda, distance, dtype):
+@pytest.mark.parametrize("M,d", [(37, 6), (36, 8)])  # (36, 8) takes the tensor-core cosine kernels in fp32
+def test_module_matches_unfused_composition(cuda, distance, dtype, M, d):
     g = torch.Generator().manual_seed(41)
-    X = torch.randn(4, 50, 6, generator=g, dtype=dtype)
-    Y = torch.randn(4, 37, 6, generator=g, dtype=dtype)
+    X = torch.randn(4, 50, d, generator=g, dtype=dtype)
+    Y = torch.randn(4, M, d, generator=g, dtype=dtype)
     lx = torch.tensor([50, 44, 20, 1])
-    ly = torch.tensor([37, 30, 37, 5])
+    ly = torch.tensor([M, 30, M, 5])
     module = T.SoftDTW(gamma=0.3, normalize=True, bandwidth=12, distance=distance)
 
     X1 = X.to(cuda).requires_grad_(True)

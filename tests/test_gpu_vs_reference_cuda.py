@@ -1,0 +1,163 @@
+"""GPU: this library against the reference's own CUDA operator on the same device.
+
+The reference's CUDA op (``src/torchsoftdtw/csrc/cuda/softdtw.cu`` with ``csrc/softdtw.cpp``, built from
+its sources for sm_100 by ``make -C oracle ref-cuda``, ops ``torch.ops.torchsoftdtw_refcu``) is the GPU
+implementation a user switches from. These tests check
+
+* parity: costs, R and E of ``torch.ops.torchsoftdtw.forward/backward`` against the reference op on the
+  same D (fp64 to 1e-10; fp32 costs to 1e-5 and E against fp64 at a well-conditioned gamma), with bands,
+  ragged lengths and a length above 1024 (the reference's one-launch-per-anti-diagonal path);
+* speed on the headline workload (B=256, N=M=512, d=64, fp32, gamma=0.1): the forward op, the backward
+  op, and the module's forward + backward (the reference module composes ``pairwise_l2_squared``, its
+  ops and torch autograd, ``softdtw.py:33-142``). Times are CUDA-event medians; the table is printed
+  (run with ``-s``) and this library must be faster on each line.
+"""
+
+import statistics
+
+import pytest
+import torch
+
+import torchsoftdtw_b200 as T
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def refcu(cuda):
+    return O.load_ref_cuda()
+
+
+def ours_ops():
+    return torch.ops.torchsoftdtw
+
+
+CASES = [
+    # B, N, M, gamma, bandwidth, ragged
+    (4, 40, 33, 1.0, -1, False),
+    (6, 130, 97, 0.3, 16, True),
+    (3, 257, 300, 0.1, -1, True),
+    (2, 1100, 900, 1.0, 200, True),
+]
+
+
+def make_case(B, N, M, ragged, dtype, dev, seed):
+    g = torch.Generator().manual_seed(seed)
+    D = torch.rand(B, N, M, generator=g, dtype=torch.float64) * 2.0
+    if ragged:
+        lx = torch.randint(max(1, N // 3), N + 1, (B,), generator=g)
+        ly = torch.randint(max(1, M // 3), M + 1, (B,), generator=g)
+        lx[0], ly[0] = N, M
+    else:
+        lx = torch.full((B,), N, dtype=torch.long)
+        ly = torch.full((B,), M, dtype=torch.long)
+    return D.to(dtype).to(dev), lx.to(dev), ly.to(dev)
+
+
+@pytest.mark.parametrize("B,N,M,gamma,bw,ragged", CASES)
+def test_parity_fp64_with_reference_cuda(cuda, refcu, kernel_path, B, N, M, gamma, bw, ragged):
+    D, lx, ly = make_case(B, N, M, ragged, torch.float64, cuda, 100 + N)
+    c_ref, R_ref = refcu.forward(D, lx, ly, gamma, bw)
+    E_ref = refcu.backward(D, R_ref, lx, ly, gamma, bw)
+    c, R = ours_ops().forward(D, lx, ly, gamma, bw)
+    E = ours_ops().backward(D, R, lx, ly, gamma, bw)
+    torch.cuda.synchronize()
+    torch.testing.assert_close(c, c_ref, rtol=1e-10, atol=1e-12)
+    torch.testing.assert_close(R, R_ref, rtol=1e-10, atol=1e-12)
+    torch.testing.assert_close(E, E_ref, rtol=1e-10, atol=1e-12)
+
+
+@pytest.mark.parametrize("B,N,M,gamma,bw,ragged", CASES[:3])
+def test_parity_fp32_with_reference_cuda(cuda, refcu, B, N, M, gamma, bw, ragged):
+    D, lx, ly = make_case(B, N, M, ragged, torch.float32, cuda, 200 + N)
+    c_ref, R_ref = refcu.forward(D, lx, ly, gamma, bw)
+    c, R = ours_ops().forward(D, lx, ly, gamma, bw)
+    torch.testing.assert_close(c, c_ref, rtol=1e-5, atol=1e-6)
+    # E in fp32 is ill-conditioned at small gamma for any implementation: both against fp64 on the same D
+    D64 = D.double()
+    _, R64 = ours_ops().forward(D64, lx, ly, gamma, bw)
+    E64 = ours_ops().backward(D64, R64, lx, ly, gamma, bw)
+    E = ours_ops().backward(D, R, lx, ly, gamma, bw).double()
+    E_ref = refcu.backward(D, R_ref, lx, ly, gamma, bw).double()
+    err = (E - E64).abs().max().item()
+    err_ref = (E_ref - E64).abs().max().item()
+    assert err <= max(1e-4, 2.0 * err_ref), (err, err_ref)
+
+
+class _RefAutograd(torch.autograd.Function):
+    """The reference's SoftDTWAutograd (softdtw.py:33-77) over its CUDA ops."""
+
+    @staticmethod
+    def forward(ctx, D, lx, ly, gamma, bw, ops):
+        costs, R = ops.forward(D, lx, ly, gamma, bw)
+        ctx.save_for_backward(D, R, lx, ly)
+        ctx.gamma, ctx.bw, ctx.ops = gamma, bw, ops
+        return costs
+
+    @staticmethod
+    def backward(ctx, grad):
+        D, R, lx, ly = ctx.saved_tensors
+        E = ctx.ops.backward(D, R, lx, ly, ctx.gamma, ctx.bw)
+        return grad.view(-1, 1, 1) * E, None, None, None, None, None
+
+
+def _median_ms(fn, reps=7, warmup=3):
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    out = []
+    for _ in range(reps):
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record()
+        fn()
+        b.record()
+        b.synchronize()
+        out.append(a.elapsed_time(b))
+    return statistics.median(out)
+
+
+def test_faster_than_reference_cuda_on_headline_workload(cuda, refcu):
+    B, N, d, gamma = 256, 512, 64, 0.1
+    g = torch.Generator().manual_seed(0)
+    X = torch.randn(B, N, d, generator=g).to(cuda)
+    Y = torch.randn(B, N, d, generator=g).to(cuda)
+    lx = torch.full((B,), N, device=cuda, dtype=torch.long)
+    ly = lx.clone()
+    D = T.pairwise_l2_squared(X, Y).contiguous()
+    ours = ours_ops()
+
+    c_o, R_o = ours.forward(D, lx, ly, gamma, -1)
+    c_r, R_r = refcu.forward(D, lx, ly, gamma, -1)
+    torch.testing.assert_close(c_o, c_r, rtol=1e-5, atol=1e-6)
+
+    rows = {}
+    rows["forward op"] = (_median_ms(lambda: ours.forward(D, lx, ly, gamma, -1)),
+                          _median_ms(lambda: refcu.forward(D, lx, ly, gamma, -1)))
+    rows["backward op"] = (_median_ms(lambda: ours.backward(D, R_o, lx, ly, gamma, -1)),
+                           _median_ms(lambda: refcu.backward(D, R_r, lx, ly, gamma, -1)))
+
+    module = T.SoftDTW(gamma=gamma)
+    Xo = X.clone().requires_grad_(True)
+    Xr = X.clone().requires_grad_(True)
+
+    def step_ours():
+        Xo.grad = None
+        module(Xo, Y, lx, ly).sum().backward()
+
+    def step_ref():
+        Xr.grad = None
+        _RefAutograd.apply(T.pairwise_l2_squared(Xr, Y), lx, ly, gamma, -1, refcu).sum().backward()
+
+    rows["module fwd+bwd"] = (_median_ms(step_ours), _median_ms(step_ref))
+    T.check_errors(cuda)
+
+    cells = B * N * N
+    print(f"\nB200, B={B} N=M={N} d={d} fp32 gamma={gamma}: this library vs the reference CUDA op (sm_100)")
+    print("| call | this library ms | reference CUDA ms | speed-up | this library cells/s | reference cells/s |")
+    print("|---|---|---|---|---|---|")
+    for name, (mo, mr) in rows.items():
+        print(f"| {name} | {mo:.3f} | {mr:.3f} | {mr / mo:.1f}x | {cells / mo * 1e3:.3e} | {cells / mr * 1e3:.3e} |")
+    for name, (mo, mr) in rows.items():
+        assert mo < mr, (name, mo, mr)

@@ -62,7 +62,8 @@ SIGNATURES: dict[str, tuple] = {
     "sdtw_pairwise_l2": (_i, [_i, _p, _p, _i64, _i64, _i64, _i64, _p, _p, _p]),
     "sdtw_grad_l2": (_i, [_i, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _p, _p, _p]),
     "sdtw_pairwise_dist": (_i, [_i, _i, _p, _p, _i64, _i64, _i64, _i64, _d, _p, _p]),
-    "sdtw_grad_dist": (_i, [_i, _i, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _d, _p, _p, _p]),
+    "sdtw_grad_dist_workspace_bytes": (_sz, [_i64, _i64, _i]),
+    "sdtw_grad_dist": (_i, [_i, _i, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _d, _p, _p, _p, _p]),
 }
 # Test and tuning hooks (declared in the .cu, not part of the public header).
 DEBUG_SIGNATURES: dict[str, tuple] = {

@@ -8,7 +8,8 @@ third-party implementations; this one times this package's module alone, forward
 (loss = costs.sum(), gradient w.r.t. X), with CUDA events after a warm-up, and reports the time per call
 and the DP cells per second (cells = in-range cells of every pair, counted exactly).
 
-    python -m torchsoftdtw_b200.benchmark [--min-time 0.2] [--forward-only] [--output FILE]
+    python -m torchsoftdtw_b200.benchmark [--min-time 0.2] [--forward-only] [--distance l2_squared|l1|cosine]
+                                          [--output FILE]
 """
 
 from __future__ import annotations
@@ -67,11 +68,11 @@ def time_call(fn, min_time: float) -> float:
     return statistics.median(samples)
 
 
-def run(min_time: float = 0.2, forward_only: bool = False) -> list[dict]:
+def run(min_time: float = 0.2, forward_only: bool = False, distance: str = "l2_squared") -> list[dict]:
     import torchsoftdtw_b200 as T
 
     dev = torch.device("cuda", torch.cuda.current_device())
-    module = T.SoftDTW(gamma=GAMMA)
+    module = T.SoftDTW(gamma=GAMMA, distance=distance)
     rows = []
     for batch, length, feat in GRID:
         for spread in SPREADS:
@@ -92,9 +93,9 @@ def run(min_time: float = 0.2, forward_only: bool = False) -> list[dict]:
     return rows
 
 
-def table(rows: list[dict], device_name: str) -> str:
+def table(rows: list[dict], device_name: str, distance: str = "l2_squared") -> str:
     has_bwd = "fwdbwd_ms" in rows[0]
-    head = f"SoftDTW module, {device_name}, gamma = {GAMMA}, fp32\n\n"
+    head = f"SoftDTW module, {device_name}, gamma = {GAMMA}, distance = {distance}, fp32\n\n"
     cols = "| B | L | D | spread | fwd ms | fwd cells/s |" + (" fwd+bwd ms | fwd+bwd cells/s |" if has_bwd else "")
     sep = "|---|---|---|---|---|---|" + ("---|---|" if has_bwd else "")
     lines = [head + cols, sep]
@@ -111,13 +112,14 @@ def main(argv: list[str] | None = None) -> int:
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     ap.add_argument("--min-time", type=float, default=0.2, help="seconds of timed calls per measurement")
     ap.add_argument("--forward-only", action="store_true")
+    ap.add_argument("--distance", default="l2_squared", choices=["l2_squared", "l1", "cosine"])
     ap.add_argument("--output", default=None, help="also write the table to this file")
     args = ap.parse_args(argv)
     if not torch.cuda.is_available():
         print("torchsoftdtw_b200.benchmark needs a CUDA device", file=sys.stderr)
         return 1
-    rows = run(args.min_time, args.forward_only)
-    text = table(rows, torch.cuda.get_device_name())
+    rows = run(args.min_time, args.forward_only, args.distance)
+    text = table(rows, torch.cuda.get_device_name(), args.distance)
     print(text)
     if args.output:
         with open(args.output, "w") as f:

@@ -468,6 +468,11 @@ namespace {
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
 int g_distance_path = 0;  // 0: automatic, 1: mma.sync kernels (no tcgen05), 2: CUDA-core kernels only
+}  // namespace
+
+int distance_path() { return g_distance_path; }
+
+namespace {
 
 template <typename T>
 sdtw_status launch_pairwise(const void* X, const void* Y, int64_t B, int64_t N, int64_t M, int64_t d, void* D,

@@ -1,10 +1,12 @@
 // L1 and cosine cost matrices and their gradients for the module path (reference
 // src/torchsoftdtw/distances.py:21-50 and their autograd), behind the C ABI of include/sdtw_b200.h.
 //
-// Both are CUDA-core tiled kernels (64 x 64 outputs per CTA, 256 threads, 4 x 4 per thread, feature or
-// sequence chunks of 16 staged in shared memory). The L1 cost is not a contraction (no tensor-core form);
-// the cosine cost is one, at O(d) per cell, next to the wavefront's O(1) per cell but 3 exponentials, and
-// these distances are not the headline path.
+// The L1 kernels run on CUDA cores (64 x 64 outputs per CTA, 256 threads, 4 x 4 per thread, feature or
+// sequence chunks of 16 staged in shared memory): the L1 cost is not a contraction. The cosine cost and
+// grad_X are contractions and run in fp32 on the tcgen05 kernels of sdtw_tcgen05.cu (cost: the epilogue
+// forms 1 - acc / (n(x) n(y)); grad_X: B operand Y / n(Y), with the inverse norms of Y from
+// row_inv_norm_kernel in the caller's workspace); fp64, unsupported shapes and grad_Y use the CUDA-core
+// kernels here.
 //
 //   L1:      D[b,i,j] = sum_k |x_ik - y_jk|
 //            dD/dx_ik = sgn(x_ik - y_jk), dD/dy_jk = -sgn(x_ik - y_jk), sgn(0) = 0 (torch's abs backward)
@@ -14,6 +16,7 @@
 // The gradient kernels compute sum_b g[b] * sum_ij E[b,i,j] dD[b,i,j] without forming g * E.
 #include "sdtw_b200.h"
 #include "sdtw_common.cuh"
+#include "sdtw_tcgen05.h"
 
 namespace sdtw {
 
@@ -27,6 +30,110 @@ __device__ __forceinline__ T rsqrt_floor(T sumsq, T eps)  // 1 / max(sqrt(sumsq)
 {
     const T n = sqrt(sumsq);
     return T(1) / (n > eps ? n : eps);
+}
+
+// out[r] = 1 / max(|A_r|, eps) for `rows` rows of d features: one warp per row.
+__global__ void __launch_bounds__(256) row_inv_norm_kernel(const float* __restrict__ A, int64_t rows, int64_t d,
+                                                           float eps, float* __restrict__ out)
+{
+    const int64_t r = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (r >= rows) return;
+    const float* a = A + r * d;
+    float ss = 0.f;
+    for (int64_t k = lane; k < d; k += 32) ss = fmaf(a[k], a[k], ss);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if (lane == 0) out[r] = rsqrt_floor(ss, eps);
+}
+
+// n consecutive values from 16-byte aligned shared memory, in 16-byte loads.
+template <int n>
+__device__ __forceinline__ void lds_vec(const float* p, float* v)
+{
+#pragma unroll
+    for (int u = 0; u < n; u += 4) {
+        const float4 f = *reinterpret_cast<const float4*>(p + u);
+        v[u] = f.x;
+        v[u + 1] = f.y;
+        v[u + 2] = f.z;
+        v[u + 3] = f.w;
+    }
+}
+template <int n>
+__device__ __forceinline__ void lds_vec(const double* p, double* v)
+{
+#pragma unroll
+    for (int u = 0; u < n; u += 2) {
+        const double2 f = *reinterpret_cast<const double2*>(p + u);
+        v[u] = f.x;
+        v[u + 1] = f.y;
+    }
+}
+
+// L1 cost matrix: 128 x 64 cells per CTA, 256 threads, 8 rows x 4 columns per thread; features in chunks
+// of 16 staged transposed in shared memory (row strides 132 / 68: 16-byte aligned rows, at most 2-way
+// bank conflicts on the transposing stores). Per feature a thread reads its 8 + 4 operands in 16-byte
+// loads and does 32 x (subtract, add |.|): the FP32 pipe bounds it (2 instructions per cell-feature).
+constexpr int kL1R = 128, kL1C = 64, kL1XS = kL1R + 4, kL1YS = kL1C + 4;
+
+template <typename T>
+__global__ void __launch_bounds__(256) pairwise_l1_kernel(const T* __restrict__ X, const T* __restrict__ Y,
+                                                          T* __restrict__ D, int64_t N, int64_t M, int64_t d)
+{
+    __shared__ __align__(16) T Xs[kDK][kL1XS];
+    __shared__ __align__(16) T Ys[kDK][kL1YS];
+    const int64_t b = blockIdx.z;
+    const int64_t i0 = static_cast<int64_t>(blockIdx.y) * kL1R, j0 = static_cast<int64_t>(blockIdx.x) * kL1C;
+    const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+    const T* Xb = X + b * N * d;
+    const T* Yb = Y + b * M * d;
+    T acc[8][4];
+#pragma unroll
+    for (int p = 0; p < 8; ++p)
+#pragma unroll
+        for (int q = 0; q < 4; ++q) acc[p][q] = T(0);
+    for (int64_t k0 = 0; k0 < d; k0 += kDK) {
+        // 16 consecutive threads read 16 consecutive features of one row
+        for (int e = threadIdx.x; e < kL1R * kDK; e += 256) {
+            const int kk = e & (kDK - 1), r = e >> 4;
+            const int64_t gk = k0 + kk, gi = i0 + r;
+            Xs[kk][r] = (gi < N && gk < d) ? Xb[gi * d + gk] : T(0);
+        }
+        for (int e = threadIdx.x; e < kL1C * kDK; e += 256) {
+            const int kk = e & (kDK - 1), r = e >> 4;
+            const int64_t gk = k0 + kk, gj = j0 + r;
+            Ys[kk][r] = (gj < M && gk < d) ? Yb[gj * d + gk] : T(0);
+        }
+        __syncthreads();
+#pragma unroll
+        for (int kk = 0; kk < kDK; ++kk) {
+            T xa[8], yb[4];
+            lds_vec<8>(&Xs[kk][8 * ty], xa);
+            lds_vec<4>(&Ys[kk][4 * tx], yb);
+#pragma unroll
+            for (int p = 0; p < 8; ++p)
+#pragma unroll
+                for (int q = 0; q < 4; ++q) acc[p][q] += fabs(xa[p] - yb[q]);
+        }
+        __syncthreads();
+    }
+    T* Db = D + b * N * M;
+    const int64_t j = j0 + 4 * tx;
+#pragma unroll
+    for (int p = 0; p < 8; ++p) {
+        const int64_t i = i0 + 8 * ty + p;
+        if (i >= N) continue;
+        if constexpr (sizeof(T) == 4) {
+            if (M % 4 == 0 && j + 3 < M) {  // 16-byte aligned: D's base is, and so is every row
+                *reinterpret_cast<float4*>(Db + i * M + j) = make_float4(acc[p][0], acc[p][1], acc[p][2], acc[p][3]);
+                continue;
+            }
+        }
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+            if (j + q < M) Db[i * M + j + q] = acc[p][q];
+    }
 }
 
 template <typename T, int KIND>
@@ -196,8 +303,10 @@ __global__ void __launch_bounds__(256) grad_dist_kernel(const T* __restrict__ A,
                 for (int p = 0; p < 4; ++p)
 #pragma unroll
                     for (int q = 0; q < 4; ++q) {
-                        const T v = av[p][q] - bq[q];
-                        acc[p][q] += v > T(0) ? gp[p] : (v < T(0) ? -gp[p] : T(0));
+                        // gp * sgn(a - b) as two compare-to-float and two FMAs (a > b iff a - b > 0 without
+                        // flush-to-zero; a tie adds nothing)
+                        acc[p][q] = fma(gp[p], T(av[p][q] > bq[q]), acc[p][q]);
+                        acc[p][q] = fma(-gp[p], T(av[p][q] < bq[q]), acc[p][q]);
                     }
             } else {
                 const T w = inv_nb[ss];
@@ -245,12 +354,22 @@ template <typename T>
 sdtw_status launch_pairwise_dist(int kind, const void* X, const void* Y, int64_t B, int64_t N, int64_t M, int64_t d,
                                  double eps, void* D, cudaStream_t s)
 {
+    if constexpr (sizeof(T) == 4) {
+        if (kind == SDTW_DIST_COSINE && distance_path() == 0 && d > 0 && pairwise_tc_supported(X, Y, D, B, N, M, d)) {
+            const cudaError_t e =
+                pairwise_tc_launch(static_cast<const float*>(X), static_cast<const float*>(Y), static_cast<float*>(D),
+                                   nullptr, B, N, M, d, wait_timeout_s(), s, true, static_cast<float>(eps));
+            return e == cudaSuccess ? SDTW_OK : static_cast<sdtw_status>(e);
+        }
+    }
     const dim3 grid(static_cast<unsigned>((M + kDT - 1) / kDT), static_cast<unsigned>((N + kDT - 1) / kDT),
                     static_cast<unsigned>(B));
     count_launch();
     if (kind == SDTW_DIST_L1)
-        pairwise_dist_kernel<T, SDTW_DIST_L1><<<grid, 256, 0, s>>>(static_cast<const T*>(X), static_cast<const T*>(Y),
-                                                                   static_cast<T*>(D), N, M, d, static_cast<T>(eps));
+        pairwise_l1_kernel<T><<<dim3(static_cast<unsigned>((M + kL1C - 1) / kL1C),
+                                     static_cast<unsigned>((N + kL1R - 1) / kL1R), static_cast<unsigned>(B)),
+                                256, 0, s>>>(static_cast<const T*>(X), static_cast<const T*>(Y), static_cast<T*>(D), N,
+                                             M, d);
     else
         pairwise_dist_kernel<T, SDTW_DIST_COSINE><<<grid, 256, 0, s>>>(
             static_cast<const T*>(X), static_cast<const T*>(Y), static_cast<T*>(D), N, M, d, static_cast<T>(eps));
@@ -277,9 +396,27 @@ void launch_grad_dist_kind(const T* X, const T* Y, const T* D, const T* E, const
 
 template <typename T>
 sdtw_status launch_grad_dist(int kind, const void* X, const void* Y, const void* D, const void* E, const void* g,
-                             int64_t B, int64_t N, int64_t M, int64_t d, double eps, void* gX, void* gY,
+                             int64_t B, int64_t N, int64_t M, int64_t d, double eps, void* ws, void* gX, void* gY,
                              cudaStream_t s)
 {
+    if constexpr (sizeof(T) == 4) {
+        if (kind == SDTW_DIST_COSINE && ws && gX && distance_path() == 0 && (reinterpret_cast<uintptr_t>(ws) & 15) == 0 &&
+            grad_tc_supported(X, Y, D, E, gX, B, N, M, d)) {
+            float* ry = static_cast<float*>(ws);
+            count_launch();
+            row_inv_norm_kernel<<<static_cast<unsigned>((B * M + 7) / 8), 256, 0, s>>>(
+                static_cast<const float*>(Y), B * M, d, static_cast<float>(eps), ry);
+            cudaError_t e = cudaGetLastError();
+            if (e != cudaSuccess) return static_cast<sdtw_status>(e);
+            e = grad_x_tc_launch(static_cast<const float*>(X), static_cast<const float*>(Y),
+                                 static_cast<const float*>(D), static_cast<const float*>(E),
+                                 static_cast<const float*>(g), nullptr, static_cast<float*>(gX), B, N, M, d,
+                                 wait_timeout_s(), s, ry, static_cast<float>(eps));
+            if (e != cudaSuccess) return static_cast<sdtw_status>(e);
+            gX = nullptr;  // done; grad_Y (if asked) below
+            if (!gY) return SDTW_OK;
+        }
+    }
     if (kind == SDTW_DIST_L1)
         launch_grad_dist_kind<T, SDTW_DIST_L1>(static_cast<const T*>(X), static_cast<const T*>(Y),
                                                static_cast<const T*>(D), static_cast<const T*>(E),
@@ -314,9 +451,15 @@ sdtw_status sdtw_pairwise_dist(sdtw_dtype dtype, int kind, const void* X, const 
                              : launch_pairwise_dist<double>(kind, X, Y, B, N, M, d, eps, D, s);
 }
 
+size_t sdtw_grad_dist_workspace_bytes(int64_t B, int64_t M, sdtw_dtype dtype)
+{
+    if (B < 0 || M < 0) return 0;
+    return static_cast<size_t>(B * M) * (dtype == SDTW_F64 ? 8 : 4) + 16;
+}
+
 sdtw_status sdtw_grad_dist(sdtw_dtype dtype, int kind, const void* X, const void* Y, const void* D, const void* E,
-                           const void* g, int64_t B, int64_t N, int64_t M, int64_t d, double eps, void* grad_X,
-                           void* grad_Y, void* stream)
+                           const void* g, int64_t B, int64_t N, int64_t M, int64_t d, double eps, void* workspace,
+                           void* grad_X, void* grad_Y, void* stream)
 {
     if (dtype != SDTW_F32 && dtype != SDTW_F64) return SDTW_EDTYPE;
     if ((kind != SDTW_DIST_L1 && kind != SDTW_DIST_COSINE) || !dist_sizes_ok(B, N, M, d) || !(eps > 0))
@@ -324,8 +467,9 @@ sdtw_status sdtw_grad_dist(sdtw_dtype dtype, int kind, const void* X, const void
     if (B == 0 || d == 0 || (!grad_X && !grad_Y)) return SDTW_OK;
     if (!X || !Y || !g || (N * M > 0 && (!E || (kind == SDTW_DIST_COSINE && !D)))) return SDTW_EINVAL;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    return dtype == SDTW_F32 ? launch_grad_dist<float>(kind, X, Y, D, E, g, B, N, M, d, eps, grad_X, grad_Y, s)
-                             : launch_grad_dist<double>(kind, X, Y, D, E, g, B, N, M, d, eps, grad_X, grad_Y, s);
+    return dtype == SDTW_F32
+               ? launch_grad_dist<float>(kind, X, Y, D, E, g, B, N, M, d, eps, workspace, grad_X, grad_Y, s)
+               : launch_grad_dist<double>(kind, X, Y, D, E, g, B, N, M, d, eps, workspace, grad_X, grad_Y, s);
 }
 
 }  // extern "C"

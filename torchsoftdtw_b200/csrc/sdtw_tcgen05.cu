@@ -280,6 +280,8 @@ struct GradTcArgs {
     const float* D;
     const float* g;
     const int* clamp_flags;  // may be null: every pair is masked
+    const float* ry;         // cosine: 1 / max(|y_j|, eps) per row of Y (B x M); null: squared L2
+    float eps;               // cosine: the floor of the norms
     float* out;
     int B, N, M, d;
     int nrt;                 // row tiles per pair
@@ -432,7 +434,7 @@ __global__ void __launch_bounds__(kGradThreads, 1) grad_x_tc_kernel(const __grid
             const int t = static_cast<int>(blockIdx.x) + tl * static_cast<int>(gridDim.x);
             const int b = t / a.nrt, rt = t % a.nrt;
             const int i_e = rt * kGT + er;
-            const bool masked = (a.clamp_flags == nullptr || a.clamp_flags[b] != 0) && i_e < a.N;
+            const bool masked = !a.ry && (a.clamp_flags == nullptr || a.clamp_flags[b] != 0) && i_e < a.N;
             const float* Drow = a.D + (static_cast<int64_t>(b) * a.N + (i_e < a.N ? i_e : 0)) * a.M;
             bool ok = true;
             for (int kc = 0; kc < a.nk; ++kc, ++q) {
@@ -476,6 +478,17 @@ __global__ void __launch_bounds__(kGradThreads, 1) grad_x_tc_kernel(const __grid
                         v.y = yr[(4 * lu + 1) * G::YB];
                         v.z = yr[(4 * lu + 2) * G::YB];
                         v.w = yr[(4 * lu + 3) * G::YB];
+                        if (a.ry) {  // cosine: rows of Y / n(Y); M % 4 == 0, the four rows all in or all out
+                            const int j = j0 + 4 * lu;
+                            if (j < a.M) {
+                                const float4 r4 =
+                                    __ldg(reinterpret_cast<const float4*>(a.ry + static_cast<int64_t>(b) * a.M + j));
+                                v.x *= r4.x;
+                                v.y *= r4.y;
+                                v.z *= r4.z;
+                                v.w *= r4.w;
+                            }
+                        }
                         const float4 h = split_hi(v);
                         const int off = 16 * (lu ^ (yn & 7));
                         *reinterpret_cast<float4*>(yhb + off) = h;
@@ -517,12 +530,72 @@ __global__ void __launch_bounds__(kGradThreads, 1) grad_x_tc_kernel(const __grid
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
             const uint32_t acc = tmem + (static_cast<uint32_t>(32 * (warp & 3)) << 16) +
                                  static_cast<uint32_t>(ab) * G::ACC_COLS;
+            float* orow = a.out + (static_cast<int64_t>(b) * a.N + i) * a.d;
+            if (a.ry) {
+                // Cosine: P = G (Y / n(Y)) in the accumulator. Pass 1 over the whole row: |x_i|^2 and x_i.P;
+                // pass 2 over this group's features: -g / n(x_i) (P - c(x_i) (x_i.P) x_i / n(x_i)^2).
+                float ss = 0.f, dot = 0.f;
+#pragma unroll
+                for (int cc = 0; cc < DPAD; cc += 8) {
+                    uint32_t r[8];
+                    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+                                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]),
+                                   "=r"(r[6]), "=r"(r[7])
+                                 : "r"(acc + static_cast<uint32_t>(cc)));
+                    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+                    for (int e = 0; e < 8; e += 4) {
+                        if (i < a.N && cc + e < a.d) {
+                            const float4 x4 = __ldg(reinterpret_cast<const float4*>(xr + cc + e));
+                            ss = fmaf(x4.x, x4.x, ss);
+                            ss = fmaf(x4.y, x4.y, ss);
+                            ss = fmaf(x4.z, x4.z, ss);
+                            ss = fmaf(x4.w, x4.w, ss);
+                            dot = fmaf(x4.x, __uint_as_float(r[e]), dot);
+                            dot = fmaf(x4.y, __uint_as_float(r[e + 1]), dot);
+                            dot = fmaf(x4.z, __uint_as_float(r[e + 2]), dot);
+                            dot = fmaf(x4.w, __uint_as_float(r[e + 3]), dot);
+                        }
+                    }
+                }
+                const float nrm = sqrtf(ss);
+                const float inv = 1.f / fmaxf(nrm, a.eps);
+                const float coef = nrm >= a.eps ? dot * inv * inv : 0.f;
+                const float ginv = a.g[b] * inv;
+#pragma unroll
+                for (int cc = 0; cc < NC; cc += 8) {
+                    uint32_t r[8];
+                    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+                                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]),
+                                   "=r"(r[6]), "=r"(r[7])
+                                 : "r"(acc + static_cast<uint32_t>(c0 + cc)));
+                    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+                    if (i < a.N) {
+#pragma unroll
+                        for (int e = 0; e < 8; e += 4) {
+                            const int n = c0 + cc + e;
+                            if (n < a.d) {
+                                const float4 x4 = __ldg(reinterpret_cast<const float4*>(xr + n));
+                                float4 o;
+                                o.x = -ginv * (__uint_as_float(r[e]) - coef * x4.x);
+                                o.y = -ginv * (__uint_as_float(r[e + 1]) - coef * x4.y);
+                                o.z = -ginv * (__uint_as_float(r[e + 2]) - coef * x4.z);
+                                o.w = -ginv * (__uint_as_float(r[e + 3]) - coef * x4.w);
+                                *reinterpret_cast<float4*>(orow + n) = o;
+                            }
+                        }
+                    }
+                }
+                asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+                __syncwarp();
+                if (lane == 0) mbar_arrive(acc_empty + 8 * ab);
+                continue;
+            }
             float v[16];
             tmem_ld16_nowait(acc + DPAD, v);  // column DPAD: rowsum(G)
             asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
             const float rsum = v[0];
             const float g2 = 2.f * a.g[b];
-            float* orow = a.out + (static_cast<int64_t>(b) * a.N + i) * a.d;
 #pragma unroll
             for (int cc = 0; cc < NC; cc += 8) {
                 uint32_t r[8];
@@ -613,6 +686,8 @@ static_assert(kDSmemBytes <= 227 * 1024, "shared memory");
 struct PairwiseTcArgs {
     float* D;
     int* clamp_flags;
+    int cosine;  // 0: squared L2; 1: D = 1 - x.y / (n(x) n(y)), n(v) = max(|v|, eps), no clamp
+    float eps;
     int B, N, M, d;
     int nit, njt, nk;  // row tiles, column tiles, feature chunks
     unsigned long long timeout_ns;
@@ -759,7 +834,8 @@ __global__ void __launch_bounds__(kDThreads, 1) pairwise_l2_tc_kernel(const __gr
                 unsigned char* st = sm + kDOffStage + s * kDStage + (is_y ? kChunk : 0);
                 unsigned char* tb = sm + kDOffTail + p * 2 * kChunk + (is_y ? kChunk : 0);
                 nrm += split_row(st + 128 * row, tb + 128 * row, row);
-                if (kc == a.nk - 1) (is_y ? y2s : x2s)[(tl & 3) * kT + row] = nrm;
+                if (kc == a.nk - 1)
+                    (is_y ? y2s : x2s)[(tl & 3) * kT + row] = a.cosine ? 1.f / fmaxf(sqrtf(nrm), a.eps) : nrm;
                 asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> tensor-core reads
                 __syncwarp();
                 if (lane == 0) {
@@ -807,9 +883,13 @@ __global__ void __launch_bounds__(kDThreads, 1) pairwise_l2_tc_kernel(const __gr
 #pragma unroll
                     for (int e = 0; e < 4; ++e) {
                         const int jl = 32 * qs + 4 * u + e;
-                        const float v = (x2 + y2[jl]) - 2.f * acc[4 * u + e];
-                        clamped |= v < 0.f && i < a.N && j0 + jl < a.M;
-                        o[e] = v < 0.f ? -0.f : v;
+                        if (a.cosine) {  // x2, y2 hold the inverse norms
+                            o[e] = 1.f - acc[4 * u + e] * (x2 * y2[jl]);
+                        } else {
+                            const float v = (x2 + y2[jl]) - 2.f * acc[4 * u + e];
+                            clamped |= v < 0.f && i < a.N && j0 + jl < a.M;
+                            o[e] = v < 0.f ? -0.f : v;
+                        }
                     }
                     *reinterpret_cast<float4*>(ob + 16 * (u ^ (row & 7))) = make_float4(o[0], o[1], o[2], o[3]);
                 }
@@ -894,7 +974,7 @@ template <int DPAD>
 cudaError_t grad_tc_launch_t(const float* X, const float* Y, const float* D, const float* E, const float* g,
                              const int* clamp_flags, float* gX, int64_t B, int64_t N, int64_t M, int64_t d,
                              double timeout_s, cudaStream_t s, int dev, int slot,
-                             PFN_cuTensorMapEncodeTiled_v12000 encode)
+                             PFN_cuTensorMapEncodeTiled_v12000 encode, const float* ry, float eps)
 {
     using G = GradGeom<DPAD>;
     {
@@ -915,6 +995,8 @@ cudaError_t grad_tc_launch_t(const float* X, const float* Y, const float* D, con
     a.D = D;
     a.g = g;
     a.clamp_flags = clamp_flags;
+    a.ry = ry;
+    a.eps = eps;
     a.out = gX;
     a.B = static_cast<int>(B);
     a.N = static_cast<int>(N);
@@ -942,7 +1024,7 @@ bool grad_tc_supported(const void* X, const void* Y, const void* D, const void* 
 
 cudaError_t grad_x_tc_launch(const float* X, const float* Y, const float* D, const float* E, const float* g,
                              const int* clamp_flags, float* gX, int64_t B, int64_t N, int64_t M, int64_t d,
-                             double timeout_s, cudaStream_t s)
+                             double timeout_s, cudaStream_t s, const float* ry, float eps)
 {
     PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
     cudaError_t e = get_encode(encode);
@@ -960,11 +1042,11 @@ cudaError_t grad_x_tc_launch(const float* X, const float* Y, const float* D, con
             g_sm_count[dev] = n > 0 ? n : 1;
         }
     }
-    if (d <= 16) return grad_tc_launch_t<16>(X, Y, D, E, g, clamp_flags, gX, B, N, M, d, timeout_s, s, dev, 0, encode);
-    if (d <= 32) return grad_tc_launch_t<32>(X, Y, D, E, g, clamp_flags, gX, B, N, M, d, timeout_s, s, dev, 1, encode);
-    if (d <= 64) return grad_tc_launch_t<64>(X, Y, D, E, g, clamp_flags, gX, B, N, M, d, timeout_s, s, dev, 2, encode);
-    if (d <= 96) return grad_tc_launch_t<96>(X, Y, D, E, g, clamp_flags, gX, B, N, M, d, timeout_s, s, dev, 3, encode);
-    return grad_tc_launch_t<128>(X, Y, D, E, g, clamp_flags, gX, B, N, M, d, timeout_s, s, dev, 4, encode);
+    if (d <= 16) return grad_tc_launch_t<16>(X, Y, D, E, g, clamp_flags, gX, B, N, M, d, timeout_s, s, dev, 0, encode, ry, eps);
+    if (d <= 32) return grad_tc_launch_t<32>(X, Y, D, E, g, clamp_flags, gX, B, N, M, d, timeout_s, s, dev, 1, encode, ry, eps);
+    if (d <= 64) return grad_tc_launch_t<64>(X, Y, D, E, g, clamp_flags, gX, B, N, M, d, timeout_s, s, dev, 2, encode, ry, eps);
+    if (d <= 96) return grad_tc_launch_t<96>(X, Y, D, E, g, clamp_flags, gX, B, N, M, d, timeout_s, s, dev, 3, encode, ry, eps);
+    return grad_tc_launch_t<128>(X, Y, D, E, g, clamp_flags, gX, B, N, M, d, timeout_s, s, dev, 4, encode, ry, eps);
 }
 
 bool pairwise_tc_supported(const void* X, const void* Y, const void* D, int64_t B, int64_t N, int64_t M, int64_t d)
@@ -975,7 +1057,7 @@ bool pairwise_tc_supported(const void* X, const void* Y, const void* D, int64_t 
 }
 
 cudaError_t pairwise_tc_launch(const float* X, const float* Y, float* D, int* clamp_flags, int64_t B, int64_t N,
-                               int64_t M, int64_t d, double timeout_s, cudaStream_t s)
+                               int64_t M, int64_t d, double timeout_s, cudaStream_t s, bool cosine, float eps)
 {
     PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
     cudaError_t e = get_encode(encode);
@@ -1004,6 +1086,8 @@ cudaError_t pairwise_tc_launch(const float* X, const float* Y, float* D, int* cl
     PairwiseTcArgs a;
     a.D = D;
     a.clamp_flags = clamp_flags;
+    a.cosine = cosine ? 1 : 0;
+    a.eps = eps;
     a.B = static_cast<int>(B);
     a.N = static_cast<int>(N);
     a.M = static_cast<int>(M);

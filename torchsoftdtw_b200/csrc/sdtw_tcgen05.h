@@ -12,9 +12,11 @@ namespace sdtw {
 bool pairwise_tc_supported(const void* X, const void* Y, const void* D, int64_t B, int64_t N, int64_t M, int64_t d);
 
 // D = clamp(|x|^2 + |y|^2 - 2 X Y^T) for fp32 X (B,N,d), Y (B,M,d); clamp_flags (optional) as for
-// sdtw_pairwise_l2. Every wait in the kernel is bounded by timeout_s.
+// sdtw_pairwise_l2. With cosine: D = 1 - X Y^T / (n(x) n(y)), n(v) = max(|v|, eps), no clamp. Every wait in
+// the kernel is bounded by timeout_s.
 cudaError_t pairwise_tc_launch(const float* X, const float* Y, float* D, int* clamp_flags, int64_t B, int64_t N,
-                               int64_t M, int64_t d, double timeout_s, cudaStream_t s);
+                               int64_t M, int64_t d, double timeout_s, cudaStream_t s, bool cosine = false,
+                               float eps = 0.f);
 
 // Whether the tcgen05 grad_X kernel handles these fp32 arguments (d <= 128, d % 4 == 0, M % 4 == 0,
 // 16-byte aligned bases).
@@ -22,10 +24,16 @@ bool grad_tc_supported(const void* X, const void* Y, const void* D, const void* 
                        int64_t N, int64_t M, int64_t d);
 
 // grad_X = 2 g[b] (rowsum(G) X - G Y), G = E with the clamped cells of D (sign bit) zeroed in pairs whose
-// clamp flag is set (every pair when clamp_flags is null). Every wait in the kernel is bounded by timeout_s.
+// clamp flag is set (every pair when clamp_flags is null). With ry (cosine; 1 / n(y_j) per row of Y, B x M,
+// 16-byte aligned): P = E (Y / n(Y)) and grad_X = -g[b] / n(x_i) (P - [|x_i| >= eps] (x_i.P) x_i / n(x_i)^2);
+// D and clamp_flags are not read. Every wait in the kernel is bounded by timeout_s.
 cudaError_t grad_x_tc_launch(const float* X, const float* Y, const float* D, const float* E, const float* g,
                              const int* clamp_flags, float* gX, int64_t B, int64_t N, int64_t M, int64_t d,
-                             double timeout_s, cudaStream_t s);
+                             double timeout_s, cudaStream_t s, const float* ry = nullptr, float eps = 0.f);
+
+// The distance kernel family forced by sdtw_debug_force_distance_path (0: automatic, 1: no tcgen05,
+// 2: CUDA cores only).
+int distance_path();
 
 // Reads and clears the tensor-core kernels' error bits (1: a wait ran out and a tile was written as NaN).
 cudaError_t read_distance_errors(uint32_t& bits);

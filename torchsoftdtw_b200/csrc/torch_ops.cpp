@@ -309,10 +309,13 @@ std::tuple<Tensor, Tensor> dist_backward_cuda(const Tensor& X, const Tensor& Y, 
     const Tensor g = grad_costs.to(acc).contiguous();
     Tensor gX = need_x ? at::empty({B, N, d}, Xc.options()) : at::empty({0}, X.options());
     Tensor gY = need_y ? at::empty({B, M, d}, Xc.options()) : at::empty({0}, Y.options());
+    const size_t ws_bytes = sdtw_grad_dist_workspace_bytes(B, M, code_of(acc));
+    Tensor ws = at::empty({static_cast<int64_t>(ws_bytes)}, Xc.options().dtype(at::kByte));
     cudaStream_t stream = at::cuda::getCurrentCUDAStream(X.get_device()).stream();
     check_status(sdtw_grad_dist(code_of(acc), static_cast<int>(kind), Xc.data_ptr(), Yc.data_ptr(),
                                 D.contiguous().data_ptr(), E.data_ptr(), g.data_ptr(), B, N, M, d, eps,
-                                need_x ? gX.data_ptr() : nullptr, need_y ? gY.data_ptr() : nullptr, stream),
+                                ws.data_ptr(), need_x ? gX.data_ptr() : nullptr, need_y ? gY.data_ptr() : nullptr,
+                                stream),
                  "grad_dist");
     if (need_x && gX.scalar_type() != X.scalar_type()) gX = gX.to(X.scalar_type());
     if (need_y && gY.scalar_type() != Y.scalar_type()) gY = gY.to(Y.scalar_type());
