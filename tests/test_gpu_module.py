@@ -195,3 +195,8 @@ def test_benchmark_sweep_runs(cuda, kernel_path):
     rows = bm.run(min_time=0.002)
     assert len(rows) == len(bm.GRID) * len(bm.SPREADS)
     assert all(r["fwd_ms"] > 0 and r["fwdbwd_ms"] > 0 for r in rows)
+    for distance in ("l1", "cosine"):
+        rows = bm.run(min_time=0.002, distance=distance, unfused=True)
+        assert all(r["fwdbwd_ms"] > 0 and r["unfused_fwdbwd_ms"] > 0 for r in rows)
+    rows = bm.run(min_time=0.002, distance="cosine", grid="headline", gamma=0.1)
+    assert len(rows) == 1 and rows[0]["B"] == 256 and rows[0]["fwdbwd_ms"] > 0

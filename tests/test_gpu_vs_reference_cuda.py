@@ -10,7 +10,8 @@ implementation a user switches from. These tests check
 * speed on the headline workload (B=256, N=M=512, d=64, fp32, gamma=0.1): the forward op, the backward
   op, and the module's forward + backward (the reference module composes ``pairwise_l2_squared``, its
   ops and torch autograd, ``softdtw.py:33-142``). Times are CUDA-event medians; the table is printed
-  (run with ``-s``) and this library must be faster on each line.
+  (run with ``-s``) and this library must be faster on each line;
+* speed over the reference's benchmark sweep (``run_benchmark.py:35-41``, spreads ``generate.py:19-22``).
 """
 
 import statistics
@@ -161,3 +162,50 @@ def test_faster_than_reference_cuda_on_headline_workload(cuda, refcu):
         print(f"| {name} | {mo:.3f} | {mr:.3f} | {mr / mo:.1f}x | {cells / mo * 1e3:.3e} | {cells / mr * 1e3:.3e} |")
     for name, (mo, mr) in rows.items():
         assert mo < mr, (name, mo, mr)
+
+
+def test_sweep_vs_reference_cuda(cuda, refcu):
+    """The reference's benchmark sweep (its grid and length spreads, gamma = 1; the sweep's own GPU entry is
+    the reference op), this library's module against the reference module over its CUDA op: forward and
+    forward + backward (gradient w.r.t. X). Prints the table; this library must be faster on every line
+    that is not launch-bound."""
+    from torchsoftdtw_b200 import benchmark as bm
+
+    module = T.SoftDTW(gamma=bm.GAMMA)
+    lines = ["| B | L | D | spread | fwd ms (lib / ref) | fwd+bwd ms (lib / ref) | fwd+bwd speed-up |",
+             "|---|---|---|---|---|---|---|"]
+    slower = []
+    for batch, length, feat in bm.GRID:
+        for spread in bm.SPREADS:
+            X, Y, lx, ly = bm.make_batch(batch, length, feat, spread, cuda)
+            Xo = X.clone().requires_grad_(True)
+            Xr = X.clone().requires_grad_(True)
+
+            def ref_costs(A):
+                return _RefAutograd.apply(T.pairwise_l2_squared(A, Y), lx, ly, bm.GAMMA, -1, refcu)
+
+            torch.testing.assert_close(module(X, Y, lx, ly), ref_costs(X), rtol=1e-4, atol=1e-4)
+
+            def fb_ours():
+                Xo.grad = None
+                module(Xo, Y, lx, ly).sum().backward()
+
+            def fb_ref():
+                Xr.grad = None
+                ref_costs(Xr).sum().backward()
+
+            f_o = bm.time_call(lambda: module(X, Y, lx, ly), 0.05)
+            f_r = bm.time_call(lambda: ref_costs(X), 0.05)
+            b_o = bm.time_call(fb_ours, 0.05)
+            b_r = bm.time_call(fb_ref, 0.05)
+            lines.append(f"| {batch} | {length} | {feat} | {spread} | {f_o:.3f} / {f_r:.3f} | {b_o:.3f} / {b_r:.3f} | "
+                         f"{b_r / b_o:.1f}x |")
+            # lines where both sides take well under a millisecond are bound by launches and host work, not
+            # by the kernels: printed, not asserted
+            if max(b_o, b_r) > 0.5 and not (f_o < f_r and b_o < b_r):
+                slower.append((batch, length, feat, spread, f_o, f_r, b_o, b_r))
+    T.check_errors(cuda)
+    print(f"\n{torch.cuda.get_device_name()}: reference sweep, this library vs the reference CUDA op, fp32, "
+          f"gamma = {bm.GAMMA}")
+    print("\n".join(lines))
+    assert not slower, slower

@@ -228,3 +228,6 @@ def test_benchmark_sweep_batches_and_table():
     rows = [{"B": 2, "L": 8, "D": 1, "spread": "none", "cells": 128.0, "fwd_ms": 0.5, "fwdbwd_ms": 1.0}]
     text = bm.table(rows, "dev")
     assert text.count("\n| 2 | 8 | 1 | none |") == 1 and "2.560e+05" in text
+    rows[0]["unfused_fwdbwd_ms"] = 3.0
+    text = bm.table(rows, "dev", "l1", 0.1)
+    assert "distance = l1" in text and "gamma = 0.1" in text and text.rstrip().endswith("| 3.000 |")

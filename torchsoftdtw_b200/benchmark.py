@@ -9,7 +9,11 @@ third-party implementations; this one times this package's module alone, forward
 and the DP cells per second (cells = in-range cells of every pair, counted exactly).
 
     python -m torchsoftdtw_b200.benchmark [--min-time 0.2] [--forward-only] [--distance l2_squared|l1|cosine]
-                                          [--output FILE]
+                                          [--grid sweep|headline] [--gamma 1.0] [--unfused] [--output FILE]
+
+``--grid headline`` times the single headline workload (B=256, L=512, D=64, every sample full length);
+``--unfused`` also times the composition a user of the reference runs (the distance's torch expression
+for D, then ``soft_dtw`` and torch autograd through the expression).
 """
 
 from __future__ import annotations
@@ -24,6 +28,7 @@ GAMMA = 1.0
 SEED = 0
 # (batch size, padded length, feature size)
 GRID = [(64, 16, 8), (64, 64, 8), (64, 256, 12), (32, 256, 16), (16, 512, 16)]
+GRIDS = {"sweep": GRID, "headline": [(256, 512, 64)]}
 # lower end of the drawn lengths, as a fraction of the padded length
 SPREADS = {"none": 1.0, "small": 0.9, "large": 0.25}
 
@@ -68,14 +73,17 @@ def time_call(fn, min_time: float) -> float:
     return statistics.median(samples)
 
 
-def run(min_time: float = 0.2, forward_only: bool = False, distance: str = "l2_squared") -> list[dict]:
+def run(min_time: float = 0.2, forward_only: bool = False, distance: str = "l2_squared", grid: str = "sweep",
+        gamma: float = GAMMA, unfused: bool = False) -> list[dict]:
     import torchsoftdtw_b200 as T
+    from torchsoftdtw_b200.distances import PAIRWISE_DISTANCES
 
     dev = torch.device("cuda", torch.cuda.current_device())
-    module = T.SoftDTW(gamma=GAMMA, distance=distance)
+    module = T.SoftDTW(gamma=gamma, distance=distance)
+    expr = PAIRWISE_DISTANCES[distance]
     rows = []
-    for batch, length, feat in GRID:
-        for spread in SPREADS:
+    for batch, length, feat in GRIDS[grid]:
+        for spread in (SPREADS if grid == "sweep" else ["none"]):
             X, Y, lx, ly = make_batch(batch, length, feat, spread, dev)
             cells = float((lx * ly).sum().item())
             row = {"B": batch, "L": length, "D": feat, "spread": spread, "cells": cells}
@@ -88,22 +96,32 @@ def run(min_time: float = 0.2, forward_only: bool = False, distance: str = "l2_s
                     module(Xg, Y, lx, ly).sum().backward()
 
                 row["fwdbwd_ms"] = time_call(step, min_time)
+                if unfused:
+                    def step_unfused():
+                        Xg.grad = None
+                        T.soft_dtw(expr(Xg, Y), lx, ly, gamma).sum().backward()
+
+                    row["unfused_fwdbwd_ms"] = time_call(step_unfused, min_time)
             T.check_errors(dev)
             rows.append(row)
     return rows
 
 
-def table(rows: list[dict], device_name: str, distance: str = "l2_squared") -> str:
+def table(rows: list[dict], device_name: str, distance: str = "l2_squared", gamma: float = GAMMA) -> str:
     has_bwd = "fwdbwd_ms" in rows[0]
-    head = f"SoftDTW module, {device_name}, gamma = {GAMMA}, distance = {distance}, fp32\n\n"
+    has_unf = "unfused_fwdbwd_ms" in rows[0]
+    head = f"SoftDTW module, {device_name}, gamma = {gamma}, distance = {distance}, fp32\n\n"
     cols = "| B | L | D | spread | fwd ms | fwd cells/s |" + (" fwd+bwd ms | fwd+bwd cells/s |" if has_bwd else "")
-    sep = "|---|---|---|---|---|---|" + ("---|---|" if has_bwd else "")
+    cols += " unfused fwd+bwd ms |" if has_unf else ""
+    sep = "|---|---|---|---|---|---|" + ("---|---|" if has_bwd else "") + ("---|" if has_unf else "")
     lines = [head + cols, sep]
     for r in rows:
         line = (f"| {r['B']} | {r['L']} | {r['D']} | {r['spread']} | {r['fwd_ms']:.3f} | "
                 f"{r['cells'] / (r['fwd_ms'] / 1e3):.3e} |")
         if has_bwd:
             line += f" {r['fwdbwd_ms']:.3f} | {r['cells'] / (r['fwdbwd_ms'] / 1e3):.3e} |"
+        if has_unf:
+            line += f" {r['unfused_fwdbwd_ms']:.3f} |"
         lines.append(line)
     return "\n".join(lines) + "\n"
 
@@ -113,13 +131,16 @@ def main(argv: list[str] | None = None) -> int:
     ap.add_argument("--min-time", type=float, default=0.2, help="seconds of timed calls per measurement")
     ap.add_argument("--forward-only", action="store_true")
     ap.add_argument("--distance", default="l2_squared", choices=["l2_squared", "l1", "cosine"])
+    ap.add_argument("--grid", default="sweep", choices=list(GRIDS))
+    ap.add_argument("--gamma", type=float, default=GAMMA)
+    ap.add_argument("--unfused", action="store_true", help="also time the unfused composition")
     ap.add_argument("--output", default=None, help="also write the table to this file")
     args = ap.parse_args(argv)
     if not torch.cuda.is_available():
         print("torchsoftdtw_b200.benchmark needs a CUDA device", file=sys.stderr)
         return 1
-    rows = run(args.min_time, args.forward_only, args.distance)
-    text = table(rows, torch.cuda.get_device_name(), args.distance)
+    rows = run(args.min_time, args.forward_only, args.distance, args.grid, args.gamma, args.unfused)
+    text = table(rows, torch.cuda.get_device_name(), args.distance, args.gamma)
     print(text)
     if args.output:
         with open(args.output, "w") as f:
