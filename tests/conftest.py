@@ -36,14 +36,15 @@ def cuda():
     return torch.device("cuda", 0)
 
 
-KERNEL_PATHS = {"auto": 0, "ticket": 1, "pair": 2}
+KERNEL_PATHS = {"auto": 0, "ticket": 1, "pair": 2, "warp": 3}
 
 
 @pytest.fixture(params=list(KERNEL_PATHS))
 def kernel_path(request):
     """Runs a GPU test once per wavefront kernel family: chosen by shape ("auto"), the strip-ticket
-    kernels (strips claimed from a global counter, boundaries in global memory) and the pair-resident
-    kernels (one CTA per pair, boundaries in shared memory)."""
+    kernels (strips claimed from a global counter, boundaries in global memory), the pair-resident
+    kernels (one CTA per pair, boundaries in shared memory) and the warp-per-pair kernels (one warp per
+    pair, strips in sequence, operands in global memory)."""
     from torchsoftdtw_b200 import _ext
 
     lib = _ext.capi()

@@ -141,3 +141,26 @@ def test_tensor_core_paths_agree(cuda):
     scale = (X * X).sum(-1)[:, :, None] + (Y * Y).sum(-1)[:, None, :]
     assert float(((D_tc - D_mma).abs() / scale).max()) < 2e-6
     assert torch.equal(f_tc, f_mma)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float64])
+def test_batches_above_the_grid_limit(cuda, dtype):
+    """B = 65537 pairs (more than one launch's grid.z): the entry points run the batch in chunks; every
+    pair's cost matrix and gradient match those computed pair-chunk by pair-chunk in fp64."""
+    B, N, M, d = 65537, 5, 3, 4
+    g0 = torch.Generator().manual_seed(3)
+    X = torch.randn(B, N, d, generator=g0, dtype=torch.float64)
+    Y = torch.randn(B, M, d, generator=g0, dtype=torch.float64)
+    E = torch.rand(B, N, M, generator=g0, dtype=torch.float64)
+    gg = torch.rand(B, generator=g0, dtype=torch.float64)
+    Xc, Yc = X.to(dtype).to(cuda), Y.to(dtype).to(cuda)
+    D, fl = pairwise(Xc, Yc)
+    ref = (X.pow(2).sum(-1)[:, :, None] + Y.pow(2).sum(-1)[:, None, :] - 2 * X @ Y.transpose(1, 2)).clamp_min(0)
+    tol = 1e-10 if dtype == torch.float64 else 1e-4
+    torch.testing.assert_close(D.double().cpu(), ref, rtol=tol, atol=tol)
+    gX, gY = grad(Xc, Yc, D, E.to(dtype).to(cuda), gg.to(dtype).to(cuda), fl)
+    G = E * gg[:, None, None] * (ref > 0)
+    gx_ref = 2 * (G.sum(2, keepdim=True) * X - G @ Y)
+    gy_ref = 2 * (G.sum(1).unsqueeze(-1) * Y - G.transpose(1, 2) @ X)
+    torch.testing.assert_close(gX.double().cpu(), gx_ref, rtol=tol, atol=tol)
+    torch.testing.assert_close(gY.double().cpu(), gy_ref, rtol=tol, atol=tol)

@@ -205,3 +205,23 @@ def test_module_gradcheck(cuda, distance):
     ly = torch.tensor([7, 7], device=cuda)
     module = T.SoftDTW(gamma=0.5, distance=distance)
     assert torch.autograd.gradcheck(lambda a, b: module(a, b, lx, ly), (X, Y), eps=1e-6, atol=1e-6)
+
+
+@pytest.mark.parametrize("kind", ["l1", "cosine"])
+def test_batches_above_the_grid_limit(cuda, kind):
+    """B = 65537 pairs: cost matrices and gradients of the chunked launches against fp64 autograd."""
+    B, N, M, d = 65537, 5, 4, 8
+    X, Y = inputs(B, N, M, d, 9, torch.float32)
+    gen = torch.Generator().manual_seed(10)
+    E = torch.rand(B, N, M, generator=gen, dtype=torch.float64)
+    g = torch.rand(B, generator=gen, dtype=torch.float64)
+    Xr = X.float().double().requires_grad_(True)
+    Yr = Y.float().double().requires_grad_(True)
+    Dr = (T.pairwise_l1 if kind == "l1" else T.pairwise_cosine)(Xr, Yr)
+    (g[:, None, None] * E * Dr).sum().backward()
+    Xc, Yc = X.float().to(cuda), Y.float().to(cuda)
+    D = dist(kind, Xc, Yc)
+    torch.testing.assert_close(D.double().cpu(), Dr.detach(), rtol=1e-5, atol=1e-5)
+    gX, gY = grad(kind, Xc, Yc, D, E.float().to(cuda), g.float().to(cuda))
+    torch.testing.assert_close(gX.double().cpu(), Xr.grad, rtol=1e-4, atol=1e-4)
+    torch.testing.assert_close(gY.double().cpu(), Yr.grad, rtol=1e-4, atol=1e-4)

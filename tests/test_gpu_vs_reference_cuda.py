@@ -209,3 +209,55 @@ def test_sweep_vs_reference_cuda(cuda, refcu):
           f"gamma = {bm.GAMMA}")
     print("\n".join(lines))
     assert not slower, slower
+
+
+def test_workloads_vs_reference_cuda(cuda, refcu):
+    """The five measured workloads (README example, headline, ragged + banded, long + banded, fp64 large
+    batch): module forward and forward + backward (gradient w.r.t. X), cells counted exactly (in band,
+    inside the lengths), this library against the reference module over its CUDA op. Prints the table;
+    this library must be faster on every workload that is not launch-bound."""
+    from torchsoftdtw_b200 import workloads
+
+    lines = ["| workload | cells | fwd ms (lib / ref) | fwd+bwd ms (lib / ref) | lib fwd+bwd cells/s | "
+             "ref fwd+bwd cells/s | speed-up |", "|---|---|---|---|---|---|---|"]
+    slower = []
+    for name in ("readme", "medium", "ragged", "long", "largebatch"):
+        X, Y, lx, ly, w = workloads.make_inputs(name)
+        X, Y, lx, ly = X.to(cuda), Y.to(cuda), lx.to(cuda), ly.to(cuda)
+        cells = workloads.count_cells(lx.cpu(), ly.cpu(), w.bandwidth)
+        module = T.SoftDTW(gamma=w.gamma, bandwidth=w.bandwidth, normalize=w.normalize)
+        Xo = X.clone().requires_grad_(True)
+        Xr = X.clone().requires_grad_(True)
+
+        def ref_module(A):  # softdtw.py:106-142 over the reference CUDA op
+            c = _RefAutograd.apply(T.pairwise_l2_squared(A, Y), lx, ly, w.gamma, w.bandwidth, refcu)
+            return c / (lx + ly - 1).to(c.dtype) if w.normalize else c
+
+        ours_c = module(X, Y, lx, ly)
+        ref_c = ref_module(X)
+        tol = dict(rtol=1e-10, atol=1e-10) if w.dtype == torch.float64 else dict(rtol=1e-4, atol=1e-4)
+        torch.testing.assert_close(ours_c, ref_c, **tol)
+
+        def fb_ours():
+            Xo.grad = None
+            module(Xo, Y, lx, ly).sum().backward()
+
+        def fb_ref():
+            Xr.grad = None
+            ref_module(Xr).sum().backward()
+
+        reps = 3 if name == "long" else 7
+        f_o = _median_ms(lambda: module(X, Y, lx, ly), reps=reps)
+        f_r = _median_ms(lambda: ref_module(X), reps=reps, warmup=1)
+        b_o = _median_ms(fb_ours, reps=reps)
+        b_r = _median_ms(fb_ref, reps=reps, warmup=1)
+        lines.append(f"| {name} | {cells} | {f_o:.3f} / {f_r:.3f} | {b_o:.3f} / {b_r:.3f} | "
+                     f"{cells / b_o * 1e3:.3e} | {cells / b_r * 1e3:.3e} | {b_r / b_o:.1f}x |")
+        if max(b_o, b_r) > 0.5 and not (f_o < f_r and b_o < b_r):
+            slower.append((name, f_o, f_r, b_o, b_r))
+        del X, Y, Xo, Xr
+        torch.cuda.empty_cache()
+    T.check_errors(cuda)
+    print(f"\n{torch.cuda.get_device_name()}: workloads, this library vs the reference CUDA op")
+    print("\n".join(lines))
+    assert not slower, slower

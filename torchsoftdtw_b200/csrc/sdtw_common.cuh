@@ -14,6 +14,20 @@ void count_launch();
 // Upper bound (seconds) of every device-side wait (sdtw_set_wait_timeout). Defined in sdtw_wavefront.cu.
 double wait_timeout_s();
 
+// Largest number of pairs one launch of the cost and gradient kernels takes (they index pairs by grid.z);
+// the C-ABI entry points run larger batches in chunks of this many pairs.
+constexpr int64_t kBatchChunk = 65535;
+
+// p advanced by `elems` elements of `es` bytes (null stays null).
+inline const void* at_elem(const void* p, int64_t elems, size_t es)
+{
+    return p ? static_cast<const void*>(static_cast<const char*>(p) + static_cast<size_t>(elems) * es) : nullptr;
+}
+inline void* at_elem(void* p, int64_t elems, size_t es)
+{
+    return p ? static_cast<void*>(static_cast<char*>(p) + static_cast<size_t>(elems) * es) : nullptr;
+}
+
 // --------------------------------------------------------------------------------------------------
 // Tiling constants of the strip wavefront.
 //   A strip is 32 consecutive rows of one pair, owned by one warp (lane l <-> row r0 + l).

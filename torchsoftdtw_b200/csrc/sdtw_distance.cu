@@ -573,8 +573,8 @@ sdtw_status launch_grad(const void* X, const void* Y, const void* D, const void*
 
 bool sizes_ok(int64_t B, int64_t N, int64_t M, int64_t d)
 {
-    return B >= 0 && N >= 0 && M >= 0 && d >= 0 && B < 65536 * 1024 && N < (int64_t(1) << 31) / kTile * kTile &&
-           M < (int64_t(1) << 31) / kTile * kTile && B <= 65535;
+    return B >= 0 && N >= 0 && M >= 0 && d >= 0 && B < (int64_t(1) << 31) && N < (int64_t(1) << 31) / kTile * kTile &&
+           M < (int64_t(1) << 31) / kTile * kTile;
 }
 }  // namespace
 }  // namespace sdtw
@@ -600,8 +600,19 @@ sdtw_status sdtw_pairwise_l2(sdtw_dtype dtype, const void* X, const void* Y, int
     }
     if (N == 0 || M == 0) return SDTW_OK;
     if (!D || (d > 0 && (!X || !Y))) return SDTW_EINVAL;
-    return dtype == SDTW_F32 ? launch_pairwise<float>(X, Y, B, N, M, d, D, clamp_flags, s)
-                             : launch_pairwise<double>(X, Y, B, N, M, d, D, clamp_flags, s);
+    const size_t es = dtype == SDTW_F32 ? 4 : 8;
+    // Pairs in chunks of kBatchChunk: the kernels index pairs by grid.z (at most 65535).
+    for (int64_t b0 = 0; b0 < B; b0 += kBatchChunk) {
+        const int64_t nb = B - b0 < kBatchChunk ? B - b0 : kBatchChunk;
+        const void* Xc = at_elem(X, b0 * N * d, es);
+        const void* Yc = at_elem(Y, b0 * M * d, es);
+        void* Dc = at_elem(D, b0 * N * M, es);
+        int* fc = clamp_flags ? clamp_flags + b0 : nullptr;
+        const sdtw_status st = dtype == SDTW_F32 ? launch_pairwise<float>(Xc, Yc, nb, N, M, d, Dc, fc, s)
+                                                 : launch_pairwise<double>(Xc, Yc, nb, N, M, d, Dc, fc, s);
+        if (st != SDTW_OK) return st;
+    }
+    return SDTW_OK;
 }
 
 sdtw_status sdtw_grad_l2(sdtw_dtype dtype, const void* X, const void* Y, const void* D, const void* E, const void* g,
@@ -613,8 +624,27 @@ sdtw_status sdtw_grad_l2(sdtw_dtype dtype, const void* X, const void* Y, const v
     if (B == 0 || d == 0 || (!grad_X && !grad_Y)) return SDTW_OK;
     if (!X || !Y || !g || ((N * M > 0) && (!D || !E))) return SDTW_EINVAL;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    return dtype == SDTW_F32 ? launch_grad<float>(X, Y, D, E, g, clamp_flags, B, N, M, d, grad_X, grad_Y, s)
-                             : launch_grad<double>(X, Y, D, E, g, clamp_flags, B, N, M, d, grad_X, grad_Y, s);
+    // An empty side has an empty gradient; the other side's is zero (its contraction has no terms).
+    if (N == 0) grad_X = nullptr;
+    if (M == 0) grad_Y = nullptr;
+    if (!grad_X && !grad_Y) return SDTW_OK;
+    const size_t es = dtype == SDTW_F32 ? 4 : 8;
+    for (int64_t b0 = 0; b0 < B; b0 += kBatchChunk) {
+        const int64_t nb = B - b0 < kBatchChunk ? B - b0 : kBatchChunk;
+        const void* Xc = at_elem(X, b0 * N * d, es);
+        const void* Yc = at_elem(Y, b0 * M * d, es);
+        const void* Dc = at_elem(D, b0 * N * M, es);
+        const void* Ec = at_elem(E, b0 * N * M, es);
+        const void* gc = at_elem(g, b0, es);
+        const int* fc = clamp_flags ? clamp_flags + b0 : nullptr;
+        void* gXc = grad_X ? at_elem(grad_X, b0 * N * d, es) : nullptr;
+        void* gYc = grad_Y ? at_elem(grad_Y, b0 * M * d, es) : nullptr;
+        const sdtw_status st = dtype == SDTW_F32
+                                   ? launch_grad<float>(Xc, Yc, Dc, Ec, gc, fc, nb, N, M, d, gXc, gYc, s)
+                                   : launch_grad<double>(Xc, Yc, Dc, Ec, gc, fc, nb, N, M, d, gXc, gYc, s);
+        if (st != SDTW_OK) return st;
+    }
+    return SDTW_OK;
 }
 
 }  // extern "C"

@@ -345,9 +345,9 @@ __global__ void __launch_bounds__(256) grad_dist_kernel(const T* __restrict__ A,
 
 bool dist_sizes_ok(int64_t B, int64_t N, int64_t M, int64_t d)
 {
-    // grid.y = ceil(N / 64) (or M) and grid.z = B are limited to 65535
-    return B >= 0 && N >= 0 && M >= 0 && d >= 0 && B <= 65535 && N <= 65535 * kDT && M <= 65535 * kDT &&
-           d < (int64_t(1) << 30);
+    // grid.y = ceil(N / 64) (or M) is limited to 65535; batches run in chunks of kBatchChunk pairs
+    return B >= 0 && N >= 0 && M >= 0 && d >= 0 && B < (int64_t(1) << 31) && N <= 65535 * kDT &&
+           M <= 65535 * kDT && d < (int64_t(1) << 30);
 }
 
 template <typename T>
@@ -447,8 +447,17 @@ sdtw_status sdtw_pairwise_dist(sdtw_dtype dtype, int kind, const void* X, const 
     if (B == 0 || N == 0 || M == 0) return SDTW_OK;
     if (!D || (d > 0 && (!X || !Y))) return SDTW_EINVAL;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    return dtype == SDTW_F32 ? launch_pairwise_dist<float>(kind, X, Y, B, N, M, d, eps, D, s)
-                             : launch_pairwise_dist<double>(kind, X, Y, B, N, M, d, eps, D, s);
+    const size_t es = dtype == SDTW_F32 ? 4 : 8;
+    for (int64_t b0 = 0; b0 < B; b0 += kBatchChunk) {
+        const int64_t nb = B - b0 < kBatchChunk ? B - b0 : kBatchChunk;
+        const void* Xc = at_elem(X, b0 * N * d, es);
+        const void* Yc = at_elem(Y, b0 * M * d, es);
+        void* Dc = at_elem(D, b0 * N * M, es);
+        const sdtw_status st = dtype == SDTW_F32 ? launch_pairwise_dist<float>(kind, Xc, Yc, nb, N, M, d, eps, Dc, s)
+                                                 : launch_pairwise_dist<double>(kind, Xc, Yc, nb, N, M, d, eps, Dc, s);
+        if (st != SDTW_OK) return st;
+    }
+    return SDTW_OK;
 }
 
 size_t sdtw_grad_dist_workspace_bytes(int64_t B, int64_t M, sdtw_dtype dtype)
@@ -467,9 +476,24 @@ sdtw_status sdtw_grad_dist(sdtw_dtype dtype, int kind, const void* X, const void
     if (B == 0 || d == 0 || (!grad_X && !grad_Y)) return SDTW_OK;
     if (!X || !Y || !g || (N * M > 0 && (!E || (kind == SDTW_DIST_COSINE && !D)))) return SDTW_EINVAL;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    return dtype == SDTW_F32
-               ? launch_grad_dist<float>(kind, X, Y, D, E, g, B, N, M, d, eps, workspace, grad_X, grad_Y, s)
-               : launch_grad_dist<double>(kind, X, Y, D, E, g, B, N, M, d, eps, workspace, grad_X, grad_Y, s);
+    const size_t es = dtype == SDTW_F32 ? 4 : 8;
+    // Chunks run in stream order, so each may reuse the start of the workspace.
+    for (int64_t b0 = 0; b0 < B; b0 += kBatchChunk) {
+        const int64_t nb = B - b0 < kBatchChunk ? B - b0 : kBatchChunk;
+        const void* Xc = at_elem(X, b0 * N * d, es);
+        const void* Yc = at_elem(Y, b0 * M * d, es);
+        const void* Dc = at_elem(D, b0 * N * M, es);
+        const void* Ec = at_elem(E, b0 * N * M, es);
+        const void* gc = at_elem(g, b0, es);
+        void* gXc = at_elem(grad_X, b0 * N * d, es);
+        void* gYc = at_elem(grad_Y, b0 * M * d, es);
+        const sdtw_status st =
+            dtype == SDTW_F32
+                ? launch_grad_dist<float>(kind, Xc, Yc, Dc, Ec, gc, nb, N, M, d, eps, workspace, gXc, gYc, s)
+                : launch_grad_dist<double>(kind, Xc, Yc, Dc, Ec, gc, nb, N, M, d, eps, workspace, gXc, gYc, s);
+        if (st != SDTW_OK) return st;
+    }
+    return SDTW_OK;
 }
 
 }  // extern "C"

@@ -35,6 +35,7 @@
 
 #include "sdtw_b200.h"
 #include "sdtw_pairwave.h"
+#include "sdtw_warppair.h"
 #include "sdtw_tcgen05.h"
 #include "sdtw_strip.cuh"
 
@@ -495,7 +496,7 @@ double wait_timeout_s() { return g_timeout_s; }
 namespace {
 
 int g_inject_skip = -1;  // set only through sdtw_debug_inject_stall (tests of the failure path)
-int g_force_path = 0;    // 0: automatic, 1: strip-ticket kernels, 2: pair-resident kernels
+int g_force_path = 0;    // 0: automatic, 1: strip-ticket kernels, 2: pair-resident kernels, 3: warp-per-pair
 int g_pair_warps = kPairMaxWarps;  // warps per CTA of the pair-resident kernels (upper bound)
 
 struct DeviceInfo {
@@ -635,6 +636,18 @@ int choose_pair_warps(const DeviceInfo& di, bool backward, int64_t B, int64_t N,
     return W > 0 ? W : pair_warps<T>(backward, N, M, g_pair_warps, static_cast<size_t>(di.max_smem));
 }
 
+// Warp-per-pair kernels for large batches of short pairs (at most 4 strips): one warp per pair and no
+// shared-memory rings, so an SM holds as many warps as its registers allow. Measured on B200 (B = 65536,
+// N = M = 64, fp64): see the kernels' file. Forced with path 3 whenever the row buffers fit.
+template <typename T>
+bool use_warp_kernels(const DeviceInfo& di, int64_t B, int64_t N, int64_t M)
+{
+    const bool fits = warp_fwd_smem_bytes<T>(M) <= 48 * 1024 && warp_bwd_smem_bytes<T>(M) <= 48 * 1024;
+    if (!fits || g_force_path == 1 || g_force_path == 2) return false;
+    if (g_force_path == 3) return true;
+    return strips_of(N) <= 4 && B >= 8 * static_cast<int64_t>(di.sms);
+}
+
 template <typename T>
 sdtw_status launch_forward(const void* D, int64_t B, int64_t N, int64_t M, const void* lx, const void* ly, int is32,
                            double gamma, int64_t bw, void* R, void* costs, void* ws, uint32_t* err,
@@ -643,6 +656,9 @@ sdtw_status launch_forward(const void* D, int64_t B, int64_t N, int64_t M, const
     const DeviceInfo* di = nullptr;
     cudaError_t e = device_info(di);
     if (e != cudaSuccess) return from_cuda(e);
+    if (use_warp_kernels<T>(*di, B, N, M))
+        return from_cuda(warp_forward<T>(static_cast<const T*>(D), static_cast<T*>(R), static_cast<T*>(costs), lx, ly,
+                                         is32, B, N, M, clamp_bw(bw, N, M), gamma, err, stream));
     const int64_t S = strips_of(N);
     e = cudaMemsetAsync(ws, 0, kHeader, stream);
     if (e != cudaSuccess) return from_cuda(e);
@@ -694,6 +710,9 @@ sdtw_status launch_backward(const void* R, int64_t B, int64_t N, int64_t M, cons
     const DeviceInfo* di = nullptr;
     cudaError_t e = device_info(di);
     if (e != cudaSuccess) return from_cuda(e);
+    if (use_warp_kernels<T>(*di, B, N, M))
+        return from_cuda(warp_backward<T>(static_cast<const T*>(R), static_cast<T*>(E), lx, ly, is32, B, N, M,
+                                          clamp_bw(bw, N, M), gamma, err, stream));
     const int64_t S = strips_of(N);
     e = cudaMemsetAsync(ws, 0, kHeader, stream);
     if (e != cudaSuccess) return from_cuda(e);
@@ -798,13 +817,14 @@ void sdtw_set_wait_timeout(double seconds)
 void sdtw_debug_inject_stall(int ticket) { g_inject_skip = ticket; }
 
 /* Test and tuning hooks (not in the public header): `path` 0 chooses the kernels by shape, 1 forces the
- * strip-ticket kernels, 2 the pair-resident kernels (when a CTA fits); `warps` caps the pair-resident
+ * strip-ticket kernels, 2 the pair-resident kernels (when a CTA fits), 3 the warp-per-pair kernels (when
+ * their row buffers fit); `warps` caps the pair-resident
  * kernels' warps per CTA (1..16). With the pair-resident kernels, sdtw_debug_inject_stall's argument
  * names strip s of pair b as b * ceil(N/32) + s. */
 /* Number of kernels this library has launched in this process (all entry points). */
 uint64_t sdtw_debug_kernel_launches(void) { return g_launches.load(std::memory_order_relaxed); }
 
-void sdtw_debug_force_path(int path) { g_force_path = (path >= 0 && path <= 2) ? path : 0; }
+void sdtw_debug_force_path(int path) { g_force_path = (path >= 0 && path <= 3) ? path : 0; }
 void sdtw_debug_set_pair_warps(int warps) { g_pair_warps = (warps >= 1 && warps <= kPairMaxWarps) ? warps : kPairMaxWarps; }
 
 size_t sdtw_forward_workspace_bytes(int64_t B, int64_t N, int64_t M, sdtw_dtype dtype)
