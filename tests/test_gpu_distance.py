@@ -52,8 +52,9 @@ def grad(X, Y, D, E, g, flags, need_x=True, need_y=True):
 SHAPES = [(3, 130, 70, 64), (2, 64, 64, 4), (2, 33, 257, 16), (1, 300, 200, 128), (2, 5, 7, 8), (2, 128, 128, 12),
           (1, 17, 19, 3), (2, 130, 132, 64), (3, 64, 64, 36), (2, 257, 260, 8), (1, 129, 4, 4), (1, 40, 384, 100)]
 
-# 0: chosen by shape (tcgen05 where d % 4 == 0 and M % 4 == 0), 1: mma.sync kernels, 2: CUDA-core kernels
-DISTANCE_PATHS = [0, 1, 2]
+# 0: chosen by shape (tcgen05 where d % 4 == 0 and M % 4 == 0, then the narrow kernels where d <= 16),
+# 1: mma.sync kernels, 2: tiled CUDA-core kernels, 3: narrow CUDA-core kernels (d <= 16)
+DISTANCE_PATHS = [0, 1, 2, 3]
 
 
 @pytest.fixture(params=DISTANCE_PATHS)
@@ -82,7 +83,7 @@ def test_pairwise_fp32_accuracy_and_clamp_sign(cuda, distance_path, B, N, M, d):
     assert np.array_equal(fl.cpu().numpy() != 0, neg.reshape(B, -1).any(1))
 
 
-def test_pairwise_fp64_matches_numpy(cuda):
+def test_pairwise_fp64_matches_numpy(cuda, distance_path):
     g = torch.Generator().manual_seed(3)
     X = torch.rand(4, 40, 4, generator=g, dtype=torch.float64) * 2 - 1
     Y = torch.rand(4, 33, 4, generator=g, dtype=torch.float64) * 2 - 1

@@ -12,6 +12,7 @@
 
 #include "sdtw_common.cuh"
 #include "sdtw_b200.h"
+#include "sdtw_narrow.h"
 #include "sdtw_tcgen05.h"
 
 namespace sdtw {
@@ -467,7 +468,10 @@ __global__ void __launch_bounds__(256, 2) grad_x_mma_kernel(const float* __restr
 namespace {
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
-int g_distance_path = 0;  // 0: automatic, 1: mma.sync kernels (no tcgen05), 2: CUDA-core kernels only
+// 0: automatic (tcgen05, then the narrow kernels for d <= 16, then mma.sync, then the tiled CUDA-core
+// kernels), 1: mma.sync kernels (no tcgen05), 2: tiled CUDA-core kernels only, 3: narrow kernels where
+// d <= 16, else the tiled CUDA-core kernels.
+int g_distance_path = 0;
 }  // namespace
 
 int distance_path() { return g_distance_path; }
@@ -486,8 +490,13 @@ sdtw_status launch_pairwise(const void* X, const void* Y, int64_t B, int64_t N, 
             return e == cudaSuccess ? SDTW_OK : static_cast<sdtw_status>(e);
         }
     }
+    if ((g_distance_path == 0 || g_distance_path == 3) && narrow_supported(B, N, M, d)) {
+        const cudaError_t e = narrow_pairwise_l2<T>(static_cast<const T*>(X), static_cast<const T*>(Y),
+                                                    static_cast<T*>(D), clamp_flags, B, N, M, d, s);
+        return e == cudaSuccess ? SDTW_OK : static_cast<sdtw_status>(e);
+    }
     if constexpr (sizeof(T) == 4) {
-        if (g_distance_path != 2 && d % 4 == 0 && aligned16(X) && aligned16(Y)) {
+        if (g_distance_path < 2 && d % 4 == 0 && aligned16(X) && aligned16(Y)) {
             static bool attr_set = false;
             if (!attr_set) {
                 const cudaError_t e = cudaFuncSetAttribute(pairwise_l2_mma_kernel,
@@ -532,8 +541,17 @@ sdtw_status launch_grad(const void* X, const void* Y, const void* D, const void*
             gx_done = true;
         }
     }
+    if ((g_distance_path == 0 || g_distance_path == 3) && narrow_supported(B, N, M, d)) {
+        // grad_X (unless the tensor cores took it) and grad_Y
+        const cudaError_t e = narrow_grad_l2<T>(static_cast<const T*>(X), static_cast<const T*>(Y),
+                                                static_cast<const T*>(D), static_cast<const T*>(E),
+                                                static_cast<const T*>(g), clamp_flags,
+                                                gx_done ? nullptr : static_cast<T*>(gX), static_cast<T*>(gY), B, N, M,
+                                                d, s);
+        return e == cudaSuccess ? SDTW_OK : static_cast<sdtw_status>(e);
+    }
     if constexpr (sizeof(T) == 4) {
-        if (!gx_done && g_distance_path != 2 && gX && d % 4 == 0 && M % 4 == 0 && aligned16(X) && aligned16(Y) && aligned16(E) &&
+        if (!gx_done && g_distance_path < 2 && gX && d % 4 == 0 && M % 4 == 0 && aligned16(X) && aligned16(Y) && aligned16(E) &&
             aligned16(gX)) {
             static bool attr_set = false;
             if (!attr_set) {
@@ -585,7 +603,7 @@ extern "C" {
 
 /* Test hook (not in the public header): 0 chooses the cost-matrix kernel by shape (tcgen05 where
  * supported), 1 forces the mma.sync kernels, 2 the CUDA-core kernels. */
-void sdtw_debug_force_distance_path(int path) { g_distance_path = (path >= 0 && path <= 2) ? path : 0; }
+void sdtw_debug_force_distance_path(int path) { g_distance_path = (path >= 0 && path <= 3) ? path : 0; }
 
 sdtw_status sdtw_pairwise_l2(sdtw_dtype dtype, const void* X, const void* Y, int64_t B, int64_t N, int64_t M,
                              int64_t d, void* D, int* clamp_flags, void* stream)
