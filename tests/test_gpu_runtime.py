@@ -38,6 +38,68 @@ def test_torch_compile_matches_eager(cuda):
     torch.testing.assert_close(compiled, eager, rtol=1e-6, atol=1e-6)
 
 
+@pytest.mark.parametrize("distance", ["l2_squared", "l1", "cosine"])
+def test_torch_compile_module_fwd_bwd_matches_eager(cuda, distance):
+    """Every module path (fused squared L2, L1, cosine) traces under torch.compile through the FakeTensor
+    kernels, forward and backward, and matches eager."""
+    torch.manual_seed(5)
+    X = torch.randn(3, 20, 8, device=cuda)
+    Y = torch.randn(3, 16, 8, device=cuda)
+    m = T.SoftDTW(gamma=0.4, distance=distance)
+
+    def f(x, y):
+        return m(x, y).sum()
+
+    Xe = X.clone().requires_grad_(True)
+    Xc = X.clone().requires_grad_(True)
+    eager = f(Xe, Y)
+    eager.backward()
+    compiled = torch.compile(f)(Xc, Y)
+    compiled.backward()
+    torch.testing.assert_close(compiled, eager, rtol=1e-6, atol=1e-6)
+    torch.testing.assert_close(Xc.grad, Xe.grad, rtol=1e-6, atol=1e-6)
+
+
+@pytest.mark.parametrize("path", [0, 3])
+def test_cuda_graph_module_step_replay(cuda, path):
+    """A whole module step (cost matrix, forward, backward, gradient) captured in a CUDA graph and replayed on
+    new inputs equals the eager step; path 3 forces the warp-per-pair wavefront kernels, and the fp64 d = 4
+    inputs take the narrow cost and gradient kernels."""
+    lib = _ext.capi()
+    lib.sdtw_debug_force_path(path)
+    try:
+        torch.manual_seed(6)
+        X = torch.randn(64, 40, 4, device=cuda, dtype=torch.float64, requires_grad=True)
+        Y = torch.randn(64, 36, 4, device=cuda, dtype=torch.float64)
+        m = T.SoftDTW(gamma=0.7)
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            for _ in range(2):  # warm-up outside capture
+                X.grad = None
+                m(X, Y).sum().backward()
+        torch.cuda.current_stream().wait_stream(s)
+        g = torch.cuda.CUDAGraph()
+        X.grad = None
+        with torch.cuda.graph(g):
+            loss = m(X, Y).sum()
+            loss.backward()
+        for _ in range(2):
+            with torch.no_grad():
+                X.copy_(torch.randn_like(X))
+                Y.copy_(torch.randn_like(Y))
+            g.replay()
+            torch.cuda.synchronize()
+            Xr = X.detach().clone().requires_grad_(True)
+            ref = m(Xr, Y).sum()
+            ref.backward()
+            torch.testing.assert_close(loss, ref, rtol=1e-12, atol=1e-12)
+            torch.testing.assert_close(X.grad, Xr.grad, rtol=1e-12, atol=1e-12)
+        del g
+    finally:
+        lib.sdtw_debug_force_path(0)
+
+
 def test_cuda_graph_capture_and_replay(cuda):
     torch.manual_seed(1)
     D = torch.rand(8, 100, 90, device=cuda)
