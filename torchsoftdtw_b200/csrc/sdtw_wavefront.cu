@@ -224,8 +224,15 @@ __device__ void fwd_strip(const FwdArgs<T>& a, T* ring, T* top, int64_t b, int s
     __syncwarp();
 }
 
+// Warps per CTA of the strip-ticket forward (independent warps, as in the backward): fp64 6, the most
+// whose rings fit one SM (4-warp CTAs fit once: 4 warps per SM); fp32 4, two CTAs per SM.
 template <typename T>
-__global__ void __launch_bounds__(kWarpsPerCta * 32) sdtw_fwd_kernel(FwdArgs<T> a)
+struct FwdWarps {
+    static constexpr int value = sizeof(T) == 8 ? 6 : kWarpsPerCta;
+};
+
+template <typename T>
+__global__ void __launch_bounds__(FwdWarps<T>::value * 32) sdtw_fwd_kernel(FwdArgs<T> a)
 {
     extern __shared__ __align__(16) unsigned char smem[];
     const int lane = threadIdx.x & 31;
@@ -453,8 +460,22 @@ __device__ void bwd_strip(const BwdArgs<T>& a, T* ring, T* bndring, T* sendring,
     __syncwarp();
 }
 
+// Warps per CTA of the strip-ticket backward (its warps share nothing but the ticket counter). fp64: 6,
+// the most whose rings fit one SM's 227 KB (4-warp CTAs fit once: 4 warps per SM); the fp64 backward of
+// 65536 x 64 x 64 pairs takes 10.3 ms instead of 14.8. fp32: 4, three CTAs per SM (12 warps); one
+// 13-warp CTA per SM measured slower on the headline workload (288 us against 279).
+template <typename T>
+struct BwdWarps {
+    static constexpr int value = sizeof(T) == 8 ? 6 : kWarpsPerCta;
+};
+template <typename T>
+constexpr int bwd_warps()
+{
+    return BwdWarps<T>::value;
+}
+
 template <typename T, int MC>
-__global__ void __launch_bounds__(kWarpsPerCta * 32) sdtw_bwd_kernel(BwdArgs<T> a)
+__global__ void __launch_bounds__(BwdWarps<T>::value * 32) sdtw_bwd_kernel(BwdArgs<T> a)
 {
     extern __shared__ __align__(16) unsigned char smem[];
     const int lane = threadIdx.x & 31;
@@ -515,12 +536,12 @@ DeviceInfo g_dev[128];
 template <typename T>
 constexpr size_t fwd_smem_bytes()
 {
-    return static_cast<size_t>(kWarpsPerCta) * (32 * kRing + kSide) * sizeof(T);
+    return static_cast<size_t>(FwdWarps<T>::value) * (32 * kRing + kSide) * sizeof(T);
 }
 template <typename T>
 constexpr size_t bwd_smem_bytes()
 {
-    return static_cast<size_t>(kWarpsPerCta) * (33 * kRing + 2 * kSide) * sizeof(T);
+    return static_cast<size_t>(bwd_warps<T>()) * (33 * kRing + 2 * kSide) * sizeof(T);
 }
 
 template <typename T>
@@ -535,10 +556,10 @@ cudaError_t init_kernel_attrs(int& occ_f, int& occ_b)
     e = cudaFuncSetAttribute(sdtw_bwd_kernel<T, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(bwd_smem_bytes<T>()));
     if (e != cudaSuccess) return e;
-    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ_f, sdtw_fwd_kernel<T>, kWarpsPerCta * 32,
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ_f, sdtw_fwd_kernel<T>, FwdWarps<T>::value * 32,
                                                       fwd_smem_bytes<T>());
     if (e != cudaSuccess) return e;
-    return cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ_b, sdtw_bwd_kernel<T, 0>, kWarpsPerCta * 32,
+    return cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ_b, sdtw_bwd_kernel<T, 0>, bwd_warps<T>() * 32,
                                                          bwd_smem_bytes<T>());
 }
 
@@ -696,10 +717,11 @@ sdtw_status launch_forward(const void* D, int64_t B, int64_t N, int64_t M, const
     a.inject_skip = g_inject_skip;
     a.vec = (M % (16 / sizeof(T)) == 0) && (reinterpret_cast<uintptr_t>(D) % 16 == 0);
     const int occ = di->occ_fwd[sizeof(T) == 8 ? 1 : 0];
-    const int64_t ctas_needed = (B * S + kWarpsPerCta - 1) / kWarpsPerCta;
+    constexpr int FW = FwdWarps<T>::value;
+    const int64_t ctas_needed = (B * S + FW - 1) / FW;
     const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(ctas_needed, int64_t(di->sms) * std::max(occ, 1))));
     count_launch();
-    sdtw_fwd_kernel<T><<<grid, kWarpsPerCta * 32, fwd_smem_bytes<T>(), stream>>>(a);
+    sdtw_fwd_kernel<T><<<grid, FW * 32, fwd_smem_bytes<T>(), stream>>>(a);
     return from_cuda(cudaGetLastError());
 }
 
@@ -737,13 +759,14 @@ sdtw_status launch_backward(const void* R, int64_t B, int64_t N, int64_t M, cons
     a.sy = make_sync(ws, err);
     a.inject_skip = g_inject_skip;
     const int occ = di->occ_bwd[sizeof(T) == 8 ? 1 : 0];
-    const int64_t ctas_needed = (B * S + kWarpsPerCta - 1) / kWarpsPerCta;
+    constexpr int BW = bwd_warps<T>();
+    const int64_t ctas_needed = (B * S + BW - 1) / BW;
     const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(ctas_needed, int64_t(di->sms) * std::max(occ, 1))));
     count_launch();
     if (M == kPairSpecialM)
-        sdtw_bwd_kernel<T, kPairSpecialM><<<grid, kWarpsPerCta * 32, bwd_smem_bytes<T>(), stream>>>(a);
+        sdtw_bwd_kernel<T, kPairSpecialM><<<grid, BW * 32, bwd_smem_bytes<T>(), stream>>>(a);
     else
-        sdtw_bwd_kernel<T, 0><<<grid, kWarpsPerCta * 32, bwd_smem_bytes<T>(), stream>>>(a);
+        sdtw_bwd_kernel<T, 0><<<grid, BW * 32, bwd_smem_bytes<T>(), stream>>>(a);
     return from_cuda(cudaGetLastError());
 }
 
