@@ -223,6 +223,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile", action="store_true", help="run for profilers: no e2e, roofline or baseline")
     ap.add_argument("--batch", type=int, default=None, help="pairs per GPU (default: the workload's B)")
+    ap.add_argument("--loss-allreduce", action="store_true",
+                    help="N > 1: also time the step followed by the global loss sum (NCCL all-reduce of one scalar)")
     args = ap.parse_args()
     rank, world, local = dist_env()
     w = WORKLOADS[args.workload]
@@ -309,6 +311,34 @@ def main():
         "vs_baseline": None, "dtype": dtype_name(w), "data": "synthetic (seeded N(0,1) per rank; no dataset)",
         "config": config_of(w, world), "gpu_launches": int(launches),
     }
+    if world > 1 and args.loss_allreduce:
+        # The same steps, each followed by the global loss sum (sharding.all_reduce_loss: one fp32 scalar,
+        # all_reduce(SUM) over NCCL); the end event follows the collective on the step's stream.
+        from torchsoftdtw_b200 import sharding
+
+        def step_global():
+            return sharding.all_reduce_loss(step())
+
+        for _ in range(2):
+            step_global()
+        torch.cuda.synchronize()
+        barrier()
+        torch.cuda.synchronize()
+        starts2 = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+        ends2 = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+        for k in range(steps):
+            flush.fill_(float(k))
+            starts2[k].record()
+            step_global()
+            ends2[k].record()
+        torch.cuda.synchronize()
+        barrier()
+        ms2 = torch.tensor([sum(a.elapsed_time(b) for a, b in zip(starts2, ends2))], dtype=torch.float64,
+                           device=dev)
+        dist.all_reduce(ms2, op=dist.ReduceOp.MAX)
+        ms2_max = float(ms2.item())
+        result["with_loss_allreduce"] = {"value": total_cells * steps / (ms2_max / 1e3), "unit": "cells/s",
+                                         "ms_per_step": ms2_max / steps}
     if args.profile:
         if rank == 0:
             print(json.dumps(result), flush=True)

@@ -1,8 +1,9 @@
 // L1 and cosine cost matrices and their gradients for the module path (reference
 // src/torchsoftdtw/distances.py:21-50 and their autograd), behind the C ABI of include/sdtw_b200.h.
 //
-// The L1 kernels run on CUDA cores (64 x 64 outputs per CTA, 256 threads, 4 x 4 per thread, feature or
-// sequence chunks of 16 staged in shared memory): the L1 cost is not a contraction. The cosine cost and
+// The L1 kernels run on CUDA cores, because the L1 cost is not a contraction. The cost kernel tiles 128 x 64
+// cells per CTA and 8 x 4 per thread; the gradient kernel tiles 64 x 64 outputs and 4 x 4 per thread.
+// Both stage feature or sequence chunks of 16 in shared memory. The cosine cost and
 // grad_X are contractions and run in fp32 on the tcgen05 kernels of sdtw_tcgen05.cu (cost: the epilogue
 // forms 1 - acc / (n(x) n(y)); grad_X: B operand Y / n(Y), with the inverse norms of Y from
 // row_inv_norm_kernel in the caller's workspace); fp64, unsupported shapes and grad_Y use the CUDA-core
