@@ -641,10 +641,11 @@ template <typename T>
 int choose_pair_warps(const DeviceInfo& di, bool backward, int64_t B, int64_t N, int64_t M)
 {
     if (g_force_path == 1) return 0;
-    // Measured on B200 (B = 256, N = M = 512, fp32): the pair-resident forward takes 233 us against the
-    // strip-ticket forward's 303 us; the backward is on par (322 us against 319 us), so by default only
-    // the forward switches.
-    if (g_force_path != 2 && (B < di.sms || backward)) return 0;
+    // Measured on B200, fp32, forward op (pair-resident / strip-ticket): 256 x 512 x 512 0.230 / 0.313 ms,
+    // 512 x 256 x 256 0.148 / 0.172, 512 x 192 x 192 0.109 / 0.118, 1024 x 160 x 160 0.150 / 0.137,
+    // 65536 x 64 x 64 2.08 / 1.30. The backward is faster on the strip-ticket kernel at every shape
+    // (0.280 / 0.365 at 256 x 512 x 512). So only the forward switches, for pairs of at least 6 strips.
+    if (g_force_path != 2 && (B < di.sms || backward || strips_of(N) < 6)) return 0;
     if (B > 0x7fffffff || !pair_keys_fit(N, M)) return 0;
     // Enough CTAs per SM for the whole batch to be resident at once (up to 8), each as wide as its
     // share of the SM's shared memory and registers allows.
@@ -657,16 +658,20 @@ int choose_pair_warps(const DeviceInfo& di, bool backward, int64_t B, int64_t N,
     return W > 0 ? W : pair_warps<T>(backward, N, M, g_pair_warps, static_cast<size_t>(di.max_smem));
 }
 
-// Warp-per-pair kernels for large batches of short pairs (at most 4 strips): one warp per pair and no
-// shared-memory rings, so an SM holds as many warps as its registers allow. Measured on B200 (B = 65536,
-// N = M = 64, fp64): see the kernels' file. Forced with path 3 whenever the row buffers fit.
+// Warp-per-pair kernels for large fp64 batches of short pairs (at most 4 strips): one warp per pair and no
+// shared-memory rings, so an SM holds as many warps as its registers allow. Measured on B200, forward /
+// backward op in ms:
+//   fp64 65536 x 64 x 64: warp-per-pair 4.62 / 4.55, strip-ticket 11.1 / 10.2, pair-resident 7.61 / 15.0
+//   fp64 2048 x 128 x 128: 0.60 / 0.68, 1.29 / 1.08, 0.92 / 2.06
+//   fp32 65536 x 64 x 64: 2.43 / 2.31, strip-ticket 1.30 / 1.44 (fp32 stays on the strip-ticket kernels)
+// Forced with path 3 whenever the row buffers fit.
 template <typename T>
 bool use_warp_kernels(const DeviceInfo& di, int64_t B, int64_t N, int64_t M)
 {
     const bool fits = warp_fwd_smem_bytes<T>(M) <= 48 * 1024 && warp_bwd_smem_bytes<T>(M) <= 48 * 1024;
     if (!fits || g_force_path == 1 || g_force_path == 2) return false;
     if (g_force_path == 3) return true;
-    return strips_of(N) <= 4 && B >= 8 * static_cast<int64_t>(di.sms);
+    return sizeof(T) == 8 && strips_of(N) <= 4 && B >= 8 * static_cast<int64_t>(di.sms);
 }
 
 template <typename T>
