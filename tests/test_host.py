@@ -103,6 +103,18 @@ def test_c_abi_rejects_bad_arguments_before_launching(lib):
     assert lib.sdtw_grad_l2(0, null, null, null, null, null, null, -2, 1, 1, 1, null, null, null) == -1
     # empty batch: nothing to do
     assert lib.sdtw_forward(0, null, 0, 4, 4, null, null, 0, 1.0, -1, null, null, null, 0, null, null) == 0
+    # L1 / cosine entry points: unknown kind, eps <= 0, negative sizes, bad dtype, missing operands
+    assert lib.sdtw_pairwise_dist(0, 3, p, p, 1, 4, 4, 2, 1e-8, p, null) == -1
+    assert lib.sdtw_pairwise_dist(0, 2, p, p, 1, 4, 4, 2, 0.0, p, null) == -1
+    assert lib.sdtw_pairwise_dist(0, 1, p, p, 1, -4, 4, 2, 1e-8, p, null) == -1
+    assert lib.sdtw_pairwise_dist(5, 1, p, p, 1, 4, 4, 2, 1e-8, p, null) == -2
+    assert lib.sdtw_pairwise_dist(0, 1, p, p, 1, 4, 4, 2, 1e-8, null, null) == -1  # no D
+    assert lib.sdtw_pairwise_dist(0, 1, null, null, 0, 4, 4, 2, 1e-8, null, null) == 0  # empty batch
+    assert lib.sdtw_grad_dist(0, 2, p, p, null, p, p, 1, 4, 4, 2, 1e-8, null, p, null, null) == -1  # cosine needs D
+    assert lib.sdtw_grad_dist(0, 1, p, p, null, p, null, 1, 4, 4, 2, 1e-8, null, p, null, null) == -1  # no g
+    assert lib.sdtw_grad_dist(0, 1, p, p, null, p, p, 1, 4, 4, 2, 1e-8, null, null, null, null) == 0  # no outputs
+    assert lib.sdtw_grad_dist_workspace_bytes(256, 512, 0) >= 256 * 512 * 4
+    assert lib.sdtw_grad_dist_workspace_bytes(256, 512, 1) >= 256 * 512 * 8
 
 
 def test_workspace_sizes(lib):
