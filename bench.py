@@ -37,6 +37,8 @@ if ROOT not in sys.path:
 
 from torchsoftdtw_b200.workloads import WORKLOADS, make_inputs  # noqa: E402  (pure torch, no native load)
 
+DATA_KIND = {"normal": "N(0,1)", "uniform": "U[-1,1]", "randwalk": "random walks", "sine": "noisy sines"}
+
 L2_FLUSH_BYTES = 256 << 20
 
 
@@ -308,7 +310,7 @@ def main():
     result = {
         "metric": metric_name(w), "value": value, "unit": "cells/s", "n_gpus": world, "steps": steps,
         "warmup": args.warmup, "ms_per_step": ms_max / steps, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": dtype_name(w), "data": "synthetic (seeded N(0,1) per rank; no dataset)",
+        "vs_baseline": None, "dtype": dtype_name(w), "data": f"synthetic (seeded per rank, {DATA_KIND[w.kind]}; no dataset)",
         "config": config_of(w, world), "gpu_launches": int(launches),
     }
     if world > 1 and args.loss_allreduce:
