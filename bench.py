@@ -1,26 +1,35 @@
-"""Benchmark: Soft-DTW DP cells/s, forward + backward, on the headline workload (B=256 pairs per GPU,
-N=M=512, d=64, fp32, gamma=0.1, no band): ``SoftDTW(gamma=0.1)(X, Y).sum().backward()`` with X requiring
-grad — the cost matrix, the forward wavefront, the backward wavefront and the grad_X contraction.
+"""Benchmark: Soft-DTW DP cells/s, forward + backward, on the headline workload (a global batch of B=256
+pairs, N=M=512, d=64, fp32, gamma=0.1, no band): ``SoftDTW(gamma=0.1)(X, Y).sum().backward()`` with X
+requiring grad.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload NAME]
 
-One process per GPU (torchrun for N > 1). Each rank processes its own seeded batch of B pairs (weak
-scaling: per-GPU work is fixed; no collective on the data path). Prints ONE JSON line on rank 0.
+One process per GPU (torchrun for N > 1). The seeded global batch is cut into contiguous slices, one per
+rank (strong scaling: B/N pairs per GPU, no collective on the data path). Prints ONE JSON line on rank 0.
 
-* value       cells processed by all ranks / max over ranks of the summed per-step device time
+* value       cells of the global batch / max over ranks of the summed per-step device time
               (CUDA events around each step; L2 flushed between steps, outside the timed events)
+* fwd         the same for the forward alone (cost matrix, forward wavefront, costs)
+* step_roofline  value against the whole step's bound: min(HBM bandwidth / algorithmic bytes per cell,
+              MUFU rate / transcendentals per cell), for fwd+bwd and for fwd
+* weak        (N > 1) every rank runs a full batch of B pairs of its own: weak scaling, secondary
 * e2e         the same metric through the public API with inputs in pinned host memory: H2D copy of
-              X and Y, the step, D2H read of the loss, all inside the timed region
+              X and Y, the step, D2H read of the loss, all inside the timed region; with the box's
+              measured pinned H2D bandwidth and the copy-bound rate it implies
 * roofline    the dominant kernel (by device time per step), timed alone through the C ABI with CUDA
               events on its stream; algorithmic bytes per DP cell / duration vs measured HBM bandwidth
 * cpu_baseline  the reference's own CPU operator (compiled from its source, oracle/_ref) driven by the
-              reference's module glue, on a bounded sample of the same workload, all host threads
-* --impl reference: that same CPU path as the reference arm (rank 0 only)
+              reference's module glue (restated in oracle/oracle.py), on a bounded sample of the same
+              workload, all host threads
+* --impl reference: that same CPU path as the reference arm (rank 0 only). That arm never imports
+              torchsoftdtw_b200: the inputs come from workloads.py loaded as a file, the cells are
+              counted by the oracle.
 """
 
 from __future__ import annotations
 
 import argparse
+import importlib.util
 import json
 import os
 import statistics
@@ -35,7 +44,20 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 if ROOT not in sys.path:
     sys.path.insert(0, ROOT)
 
-from torchsoftdtw_b200.workloads import WORKLOADS, make_inputs  # noqa: E402  (pure torch, no native load)
+
+def _load_workloads():
+    """torchsoftdtw_b200/workloads.py loaded as a plain file: the seeded inputs are pure torch, and loading
+    the file does not run the package's __init__ (which loads the native libraries)."""
+    path = os.path.join(ROOT, "torchsoftdtw_b200", "workloads.py")
+    spec = importlib.util.spec_from_file_location("sdtw_bench_workloads", path)
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules[spec.name] = mod
+    spec.loader.exec_module(mod)
+    return mod
+
+
+_WL = _load_workloads()
+WORKLOADS, make_inputs = _WL.WORKLOADS, _WL.make_inputs
 
 DATA_KIND = {"normal": "N(0,1)", "uniform": "U[-1,1]", "randwalk": "random walks", "sine": "noisy sines"}
 
@@ -119,78 +141,48 @@ class ClockSampler:
 
 
 # ---------------------------------------------------------------------------------------------------
-# The reference's CPU path (timed baseline and reference arm)
+# The reference's CPU path (timed baseline and reference arm). Only the oracle is loaded here: the
+# reference's compiled CPU operator (oracle/_ref) under its module glue, restated in oracle/oracle.py.
 # ---------------------------------------------------------------------------------------------------
-class _RefAutograd(torch.autograd.Function):
-    """The reference's SoftDTWAutograd glue (softdtw.py:33-48) over its compiled CPU operator."""
-
-    ops = None
-
-    @staticmethod
-    def forward(ctx, D, lx, ly, gamma, bw):
-        costs, R = _RefAutograd.ops.forward(D, lx, ly, gamma, bw)
-        ctx.save_for_backward(D, R, lx, ly)
-        ctx.gamma, ctx.bw = gamma, bw
-        return costs
-
-    @staticmethod
-    def backward(ctx, g):
-        D, R, lx, ly = ctx.saved_tensors
-        E = _RefAutograd.ops.backward(D, R, lx, ly, ctx.gamma, ctx.bw)
-        return g.unsqueeze(-1).unsqueeze(-1) * E, None, None, None, None
-
-
-def reference_cpu_step(X, Y, lx, ly, w):
-    from torchsoftdtw_b200.distances import pairwise_l2_squared  # same expression as the reference's
-
-    Xr = X.detach().requires_grad_(True)
-    D = pairwise_l2_squared(Xr, Y)
-    costs = _RefAutograd.apply(D, lx, ly, w.gamma, w.bandwidth)
-    if w.normalize:
-        costs = costs / (lx + ly - 1).to(costs.dtype)
-    costs.sum().backward()
-    return Xr.grad
-
-
 def cpu_reference_measure(w, sample_pairs: int, steps: int, warmup: int, min_seconds: float = 0.0):
     """Cells/s of the reference CPU path on `sample_pairs` pairs of the workload, all host threads."""
     from oracle import oracle as O
-    from torchsoftdtw_b200.workloads import count_cells
 
     if not O.ref_available():
         O.build()
-    _RefAutograd.ops = O.load_ref()
+    O.load_ref()
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
     X, Y, lx, ly, _ = make_inputs(w.name, seed=1000, batch=sample_pairs)
-    cells = count_cells(lx, ly, w.bandwidth)
+    cells = O.count_cells(lx.numpy(), ly.numpy(), w.bandwidth)
     for _ in range(warmup):
-        reference_cpu_step(X, Y, lx, ly, w)
+        O.reference_module_step(X, Y, lx, ly, w.gamma, w.bandwidth, w.normalize)
     times = []
     t_total = 0.0
     while len(times) < steps or t_total < min_seconds:
         t0 = time.perf_counter()
-        reference_cpu_step(X, Y, lx, ly, w)
+        O.reference_module_step(X, Y, lx, ly, w.gamma, w.bandwidth, w.normalize)
         dt = time.perf_counter() - t0
         times.append(dt)
         t_total += dt
     mean = sum(times) / len(times)
     return {"value": cells / mean, "unit": "cells/s", "cores": threads, "kind": "reference",
             "sample": f"{sample_pairs} pairs of the {w.name} workload ({cells} cells) per step, "
-                      f"{len(times)} steps, module fwd+bwd (pairwise_l2_squared + reference CPU op + autograd)",
+                      f"{len(times)} steps, module fwd+bwd (the reference's pairwise_l2_squared + its CPU op + "
+                      f"torch autograd)",
             "s_per_step": mean}
 
 
-def run_reference_arm(args, w, rank):
+def run_reference_arm(args, w, rank, world):
     if rank != 0:
         return
     sample = args.cpu_sample
     r = cpu_reference_measure(w, sample, max(args.steps, 1), max(args.warmup, 1))
     line = {
         "impl": "reference", "metric": metric_name(w), "value": r["value"], "unit": "cells/s",
-        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": r["s_per_step"] * 1e3,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": dtype_name(w), "data": "synthetic",
-        "config": config_of(w, args.gpus),
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": r["s_per_step"] * 1e3,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": dtype_name(w),
+        "data": "synthetic", "config": config_of(w, world),
         "cpu_baseline": {k: r[k] for k in ("value", "unit", "cores", "kind", "sample")},
         "e2e": {"value": r["value"], "unit": "cells/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -207,10 +199,50 @@ def dtype_name(w):
 
 
 def config_of(w, world):
-    return {"workload": w.name, "pairs_per_gpu": w.B, "global_batch": w.B * world, "N": w.N, "M": w.M, "d": w.d,
-            "gamma": w.gamma, "bandwidth": w.bandwidth, "normalize": w.normalize,
-            "parallelism": f"batch-shard x{world}", "step": "SoftDTW(X,Y).sum().backward(), grad_X only",
+    return {"workload": w.name, "global_batch": w.B, "pairs_per_gpu": f"{w.B}/{world}", "N": w.N, "M": w.M,
+            "d": w.d, "gamma": w.gamma, "bandwidth": w.bandwidth, "normalize": w.normalize,
+            "parallelism": f"batch-shard x{world} (contiguous slices of one seeded global batch)",
+            "step": "SoftDTW(X,Y).sum().backward(), grad_X only",
             "l2": "flushed between timed steps (256 MiB write, outside the timed events)"}
+
+
+# Transcendental (MUFU) operations per DP cell of the north_star roofline: forward 2 exp + 1 log,
+# backward 3 exp. SMs x 16 MUFU results per clock x the SM clock is the MUFU rate.
+MUFU_PER_CELL = {"fwd": 3, "fwd+bwd": 6}
+
+
+def step_roofline(w, value: float, kind: str, sms: int):
+    """value (cells/s) against min(HBM / algorithmic bytes per cell, MUFU rate / MUFU ops per cell) of the
+    whole step, D and E kept on chip: R written once (and read once by the backward), X and Y read by
+    each pass, grad_X written."""
+    es = 8 if w.dtype == torch.float64 else 4
+    hbm, src = peaks()
+    nm = float(w.N * w.M)
+    if kind == "fwd":
+        bpc = es + (w.N + w.M) * w.d * es / nm
+    else:
+        bpc = 2 * es + (2 * (w.N + w.M) + w.N) * w.d * es / nm
+    hbm_cells = hbm * 1e9 / bpc
+    out = {"bytes_per_cell": bpc, "hbm_gbs": hbm, "hbm_bound_cells_per_s": hbm_cells, "peak_source": src}
+    peak = hbm_cells
+    if w.dtype == torch.float32:
+        mhz = sm_max_mhz()
+        mufu = sms * 16 * mhz * 1e6
+        out.update({"mufu_per_cell": MUFU_PER_CELL[kind], "mufu_per_s": mufu,
+                    "mufu_bound_cells_per_s": mufu / MUFU_PER_CELL[kind]})
+        peak = min(peak, mufu / MUFU_PER_CELL[kind])
+    out["bound"] = "hbm" if peak == hbm_cells else "mufu"
+    out["peak_cells_per_s"] = peak
+    out["frac"] = value / peak
+    return out
+
+
+def sm_max_mhz() -> float:
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            return float(json.load(f).get("sm_max_mhz", 1965.0))
+    return 1965.0
 
 
 def main():
@@ -223,8 +255,9 @@ def main():
     ap.add_argument("--cpu-sample", type=int, default=None,
                     help="pairs per CPU-baseline step (default: one per host thread, at least 16)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--profile", action="store_true", help="run for profilers: no e2e, roofline or baseline")
-    ap.add_argument("--batch", type=int, default=None, help="pairs per GPU (default: the workload's B)")
+    ap.add_argument("--profile", action="store_true", help="run for profilers: timed fwd+bwd steps only")
+    ap.add_argument("--batch", type=int, default=None, help="global batch (default: the workload's B)")
+    ap.add_argument("--no-weak", action="store_true", help="N > 1: skip the secondary weak-scaling timing")
     ap.add_argument("--loss-allreduce", action="store_true",
                     help="N > 1: also time the step followed by the global loss sum (NCCL all-reduce of one scalar)")
     args = ap.parse_args()
@@ -238,7 +271,7 @@ def main():
         w = dataclasses.replace(w, B=args.batch)
 
     if args.impl == "reference":
-        run_reference_arm(args, w, rank)
+        run_reference_arm(args, w, rank, world)
         return
 
     import torch.distributed as dist
@@ -250,15 +283,21 @@ def main():
 
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
     import torchsoftdtw_b200 as T
-    from torchsoftdtw_b200 import _ext
+    from torchsoftdtw_b200 import _ext, sharding
     from torchsoftdtw_b200.workloads import count_cells
 
-    X, Y, lx, ly, _ = make_inputs(w.name, seed=rank, batch=w.B)
+    # One seeded global batch (the same on every rank); this rank keeps its contiguous slice.
+    Xg, Yg, lxg, lyg, _ = make_inputs(w.name, seed=0, batch=w.B)
+    b0, b1 = sharding.shard_bounds(w.B, world, rank)
+    X, Y, lx, ly = Xg[b0:b1].contiguous(), Yg[b0:b1].contiguous(), lxg[b0:b1], lyg[b0:b1]
+    cells_global = count_cells(lxg, lyg, w.bandwidth)
     cells_rank = count_cells(lx, ly, w.bandwidth)
     Xd, Yd, lxd, lyd = X.to(dev), Y.to(dev), lx.to(dev), ly.to(dev)
     Xd.requires_grad_(True)
+    Xnd = Xd.detach()
     module = T.SoftDTW(gamma=w.gamma, bandwidth=w.bandwidth, normalize=w.normalize)
     flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
+    capi = _ext.capi()
 
     def step():
         Xd.grad = None
@@ -266,103 +305,133 @@ def main():
         loss.backward()
         return loss
 
+    def fwd_step():
+        return module(Xnd, Yd, lxd, lyd)
+
     def barrier():
         if world > 1:
             dist.barrier(device_ids=[local])
 
-    for _ in range(max(args.warmup, 1)):
-        step()
-    torch.cuda.synchronize()
-    T.check_errors(dev)
+    def max_over_ranks(v: float) -> float:
+        t = torch.tensor([v], dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def timed(fn, steps: int, warmup: int) -> tuple[float, int]:
+        """Summed CUDA-event time (ms) of `steps` calls of fn after `warmup` untimed ones, L2 flushed before
+        each call outside the events, max over ranks; and this library's kernel launches in the timed calls."""
+        for _ in range(max(warmup, 1)):
+            fn()
+        torch.cuda.synchronize()
+        starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+        ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+        barrier()
+        torch.cuda.synchronize()
+        l0 = capi.sdtw_debug_kernel_launches()
+        for k in range(steps):
+            flush.fill_(float(k))
+            starts[k].record()
+            fn()
+            ends[k].record()
+        torch.cuda.synchronize()
+        launches = capi.sdtw_debug_kernel_launches() - l0
+        barrier()
+        return max_over_ranks(sum(s.elapsed_time(e) for s, e in zip(starts, ends))), int(launches)
 
     sampler = None if args.profile else ClockSampler(local)
-    steps = args.steps
-    starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
-    ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
     if sampler:
         time.sleep(0.3)
         sampler.mark()
-    barrier()
-    torch.cuda.synchronize()
-    capi = _ext.capi()
-    launches0 = capi.sdtw_debug_kernel_launches()
-    for k in range(steps):
-        flush.fill_(float(k))
-        starts[k].record()
-        step()
-        ends[k].record()
-    torch.cuda.synchronize()
-    launches = capi.sdtw_debug_kernel_launches() - launches0
-    barrier()
-    if sampler:
-        sampler.mark()
-    ms_rank = sum(s.elapsed_time(e) for s, e in zip(starts, ends))
+    steps = args.steps
+    ms_max, launches = timed(step, steps, args.warmup)
     T.check_errors(dev)
-    ms_t = torch.tensor([ms_rank], dtype=torch.float64, device=dev)
-    cells_t = torch.tensor([float(cells_rank)], dtype=torch.float64, device=dev)
-    if world > 1:
-        dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
-        dist.all_reduce(cells_t, op=dist.ReduceOp.SUM)
-    ms_max = float(ms_t.item())
-    total_cells = float(cells_t.item())
-    value = total_cells * steps / (ms_max / 1e3)
-
+    value = cells_global * steps / (ms_max / 1e3)
     result = {
         "metric": metric_name(w), "value": value, "unit": "cells/s", "n_gpus": world, "steps": steps,
-        "warmup": args.warmup, "ms_per_step": ms_max / steps, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": dtype_name(w), "data": f"synthetic (seeded per rank, {DATA_KIND[w.kind]}; no dataset)",
-        "config": config_of(w, world), "gpu_launches": int(launches),
+        "warmup": args.warmup, "ms_per_step": ms_max / steps, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": dtype_name(w),
+        "data": f"synthetic (one seeded global batch, {DATA_KIND[w.kind]}; no dataset)",
+        "config": config_of(w, world), "gpu_launches": launches,
     }
-    if world > 1 and args.loss_allreduce:
-        # The same steps, each followed by the global loss sum (sharding.all_reduce_loss: one fp32 scalar,
-        # all_reduce(SUM) over NCCL); the end event follows the collective on the step's stream.
-        from torchsoftdtw_b200 import sharding
-
-        def step_global():
-            return sharding.all_reduce_loss(step())
-
-        for _ in range(2):
-            step_global()
-        torch.cuda.synchronize()
-        barrier()
-        torch.cuda.synchronize()
-        starts2 = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
-        ends2 = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
-        for k in range(steps):
-            flush.fill_(float(k))
-            starts2[k].record()
-            step_global()
-            ends2[k].record()
-        torch.cuda.synchronize()
-        barrier()
-        ms2 = torch.tensor([sum(a.elapsed_time(b) for a, b in zip(starts2, ends2))], dtype=torch.float64,
-                           device=dev)
-        dist.all_reduce(ms2, op=dist.ReduceOp.MAX)
-        ms2_max = float(ms2.item())
-        result["with_loss_allreduce"] = {"value": total_cells * steps / (ms2_max / 1e3), "unit": "cells/s",
-                                         "ms_per_step": ms2_max / steps}
     if args.profile:
         if rank == 0:
             print(json.dumps(result), flush=True)
         if world > 1:
             dist.destroy_process_group()
         return
+    if sampler:
+        sampler.mark()
+
+    # ---- forward alone (cost matrix + forward wavefront + costs) ---------------------------------------
+    ms_fwd, launches_fwd = timed(fwd_step, steps, args.warmup)
+    T.check_errors(dev)
+    value_fwd = cells_global * steps / (ms_fwd / 1e3)
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    result["fwd"] = {"value": value_fwd, "unit": "cells/s", "ms_per_step": ms_fwd / steps,
+                     "gpu_launches": launches_fwd, "step_roofline": step_roofline(w, value_fwd, "fwd", sms)}
+    result["step_roofline"] = step_roofline(w, value, "fwd+bwd", sms)
+
+    if world > 1 and args.loss_allreduce:
+        # The same steps, each followed by the global loss sum (sharding.all_reduce_loss: one fp32 scalar,
+        # all_reduce(SUM) over NCCL); the end event follows the collective on the step's stream.
+        def step_global():
+            return sharding.all_reduce_loss(step())
+
+        ms2, _ = timed(step_global, steps, 2)
+        result["with_loss_allreduce"] = {"value": cells_global * steps / (ms2 / 1e3), "unit": "cells/s",
+                                         "ms_per_step": ms2 / steps}
+
+    if world > 1 and not args.no_weak:
+        # Secondary: weak scaling, every rank a full batch of B pairs of its own (seed = rank).
+        Xw, Yw, lxw, lyw, _ = make_inputs(w.name, seed=rank, batch=w.B)
+        cw = float(count_cells(lxw, lyw, w.bandwidth))
+        Xwd, Ywd, lxwd, lywd = Xw.to(dev).requires_grad_(True), Yw.to(dev), lxw.to(dev), lyw.to(dev)
+
+        def step_weak():
+            Xwd.grad = None
+            module(Xwd, Ywd, lxwd, lywd).sum().backward()
+
+        weak_steps = max(5, steps // 4)
+        ms_w, _ = timed(step_weak, weak_steps, 2)
+        cw_t = torch.tensor([cw], dtype=torch.float64, device=dev)
+        dist.all_reduce(cw_t, op=dist.ReduceOp.SUM)
+        result["weak"] = {"value": float(cw_t.item()) * weak_steps / (ms_w / 1e3), "unit": "cells/s",
+                          "ms_per_step": ms_w / weak_steps, "pairs_per_gpu": w.B, "global_batch": w.B * world,
+                          "steps": weak_steps}
+        del Xwd, Ywd
 
     # ---- e2e through the public API with host buffers ----------------------------------------------
-    # Every step copies its X and Y from pinned host memory (H2D) and reads its loss back (D2H) inside the
-    # timed region. The copies run on a second stream into two alternating device buffers, so the copy of
-    # step k+1 overlaps the compute of step k (an input pipeline); step k waits for its own copy, and the
-    # copy into a buffer waits for the step that last used it.
+    # Every step copies its X and Y slices from pinned host memory (H2D) and reads its loss back (D2H)
+    # inside the timed region. The copies run on a second stream into two alternating device buffers, so
+    # the copy of step k+1 overlaps the compute of step k (an input pipeline); step k waits for its own
+    # copy, and the copy into a buffer waits for the step that last used it.
     Xh = X.pin_memory()
     Yh = Y.pin_memory()
     loss_h = torch.empty((), dtype=torch.float32).pin_memory()
     e2e_steps = max(10, steps // 4)
     copy_stream = torch.cuda.Stream(device=dev)
     main_stream = torch.cuda.current_stream(dev)
-    xbuf = [torch.empty_like(Xd) for _ in range(2)]
+    xbuf = [torch.empty_like(Xnd) for _ in range(2)]
     ybuf = [torch.empty_like(Yd) for _ in range(2)]
     copied = [torch.cuda.Event() for _ in range(2)]
     used = [torch.cuda.Event() for _ in range(2)]
+    h2d_bytes = Xh.numel() * Xh.element_size() + Yh.numel() * Yh.element_size()
+
+    # Pinned host -> device bandwidth of this box for these buffers (the bound of the e2e figure).
+    for _ in range(2):
+        xbuf[0].copy_(Xh, non_blocking=True)
+        ybuf[0].copy_(Yh, non_blocking=True)
+    torch.cuda.synchronize()
+    c0 = torch.cuda.Event(enable_timing=True)
+    c1 = torch.cuda.Event(enable_timing=True)
+    c0.record()
+    for _ in range(5):
+        xbuf[0].copy_(Xh, non_blocking=True)
+        ybuf[0].copy_(Yh, non_blocking=True)
+    c1.record()
+    torch.cuda.synchronize()
+    h2d_gbs = 5 * h2d_bytes / (c0.elapsed_time(c1) / 1e3) / 1e9
 
     def e2e_copy(k, after):
         j = k % 2
@@ -397,23 +466,24 @@ def main():
     e1.record(main_stream)
     torch.cuda.synchronize()
     barrier()
-    e2e_ms = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
-    if world > 1:
-        dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
-    e2e_value = total_cells * e2e_steps / (float(e2e_ms.item()) / 1e3)
-    result["e2e"] = {"value": e2e_value, "unit": "cells/s",
-                     "h2d_bytes_per_step": Xh.numel() * Xh.element_size() + Yh.numel() * Yh.element_size(),
-                     "d2h_bytes_per_step": loss_h.element_size()}
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1))
+    e2e_value = cells_global * e2e_steps / (e2e_ms / 1e3)
+    h2d_min = -max_over_ranks(-h2d_gbs)
+    copy_bound = cells_global / (h2d_bytes / (h2d_min * 1e9))
+    result["e2e"] = {"value": e2e_value, "unit": "cells/s", "h2d_bytes_per_step": h2d_bytes,
+                     "d2h_bytes_per_step": loss_h.element_size(), "ms_per_step": e2e_ms / e2e_steps,
+                     "h2d_gbs_measured": h2d_min, "copy_bound_cells_per_s": copy_bound,
+                     "frac_of_copy_bound": e2e_value / copy_bound}
 
     # ---- per-kernel device time through the C ABI (dominant kernel -> roofline) --------------------
-    kt = kernel_times(T, Xd.detach(), Yd, lxd, lyd, w, dev, flush)
+    kt = kernel_times(T, Xnd, Yd, lxd, lyd, w, dev, flush)
     clocks = sampler.summarize(sampler.stop(), sampler.marks[0]) if sampler else None
     if rank == 0:
         hbm, peak_kind = peaks()
         name, ms = max(kt.items(), key=lambda kv: kv[1])
         bytes_per_cell = ALGO_BYTES[name] * (8 if w.dtype == torch.float64 else 4)
         achieved = cells_rank * bytes_per_cell / (ms / 1e3) / 1e9
-        traffic = measured_traffic(w, name)
+        traffic = measured_traffic(w, world, name)
         result["roofline"] = {"bound": "hbm", "kernel": name, "achieved": achieved, "peak": hbm,
                               "unit": "GB/s", "frac": achieved / hbm,
                               "traffic": traffic / (ms / 1e3) / 1e9 if traffic else None,
@@ -430,11 +500,11 @@ def main():
         dist.destroy_process_group()
 
 
-def measured_traffic(w, name: str):
-    """DRAM bytes (read + write) of one launch of the C-ABI call `name` on workload `w`, as recorded from
-    an ncu capture in profiles/dram_traffic_<workload>_b<B>.txt (lines: <call> <kernel> <bytes>), or
-    None when no capture of this workload exists."""
-    path = os.path.join(ROOT, "profiles", f"dram_traffic_{w.name}_b{w.B}.txt")
+def measured_traffic(w, world: int, name: str):
+    """DRAM bytes (read + write) of one launch of the C-ABI call `name` on one rank's slice of workload `w`,
+    as recorded from an ncu capture in profiles/dram_traffic_<workload>_b<pairs per GPU>.txt (lines:
+    <call> <kernel> <bytes>), or None when no capture of that slice exists."""
+    path = os.path.join(ROOT, "profiles", f"dram_traffic_{w.name}_b{(w.B + world - 1) // world}.txt")
     if not os.path.exists(path):
         return None
     with open(path) as f:

@@ -85,10 +85,14 @@ sdtw_status sdtw_forward(sdtw_dtype dtype, const void* D, int64_t B, int64_t N, 
  * static device array of SDTW_NOALLOC_SCRATCH_BYTES (16 MiB) inside this library instead. The caller
  * still provides D, R, costs, lengths and err_word (err_word must start at zero, as for sdtw_forward);
  * nothing else needs to start at zero (the call resets its scratch on the stream before use).
- *   - Limit: problems whose sdtw_forward_workspace_bytes exceeds SDTW_NOALLOC_SCRATCH_BYTES are rejected
- *     with SDTW_ETOOLARGE before anything is enqueued (e.g. B=256, N=M=512 fp32 fits; fp64 does not).
- *   - The first call on each device looks the scratch's address up (cudaGetSymbolAddress); make it
- *     before any stream capture. Later calls only enqueue work.
+ *   - Limit: the scratch must hold the workspace of the kernel this shape runs on. The pair-resident and
+ *     warp-per-pair kernels need 256 bytes, so every shape they take fits; the strip-ticket kernels (few
+ *     long pairs) need 256 bytes plus one row of M values per 32-row strip (sdtw_forward_workspace_bytes),
+ *     and shapes beyond SDTW_NOALLOC_SCRATCH_BYTES are rejected with SDTW_ETOOLARGE before anything is
+ *     enqueued (e.g. B=16, N=M=4096 fp32 needs 32 MiB).
+ *   - Every call looks the scratch's address up on the current device (cudaGetSymbolAddress, which
+ *     allocates nothing), so a cudaDeviceReset between calls does no harm. The first call on a device can
+ *     load this library's kernels there: make it before any stream capture.
  *   - The scratch is shared by every call in the process on that device: calls that can overlap in time
  *     (different streams, or different host threads without ordering) race on it and give wrong results.
  *     Serialise them, e.g. on one stream.

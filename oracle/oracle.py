@@ -184,3 +184,64 @@ def load_ref_cuda():
         torch.ops.load_library(REF_CUDA_SO)
         _ref_cuda_loaded = True
     return torch.ops.torchsoftdtw_refcu
+
+
+# ----------------------------------------------------------------------------------------------------
+# The reference's module path on its compiled CPU operator (bench.py's CPU baseline and reference arm).
+# Nothing here imports torchsoftdtw_b200, so a process that runs only this path maps no library of the
+# product.
+# ----------------------------------------------------------------------------------------------------
+
+def ref_pairwise_l2_squared_torch(X, Y):
+    """Torch restatement of the reference's ``pairwise_l2_squared`` (``src/torchsoftdtw/distances.py:4-18``):
+    |x|^2 + |y|^2 - 2 x.y through ``bmm``, clamped at 0; differentiable by torch autograd as in the
+    reference's module."""
+    import torch
+
+    x2 = (X * X).sum(dim=-1)
+    y2 = (Y * Y).sum(dim=-1)
+    xy = torch.bmm(X, Y.transpose(1, 2))
+    return (x2.unsqueeze(2) + y2.unsqueeze(1) - 2 * xy).clamp_min(0.0)
+
+
+def _ref_autograd_class():
+    import torch
+
+    class RefSoftDTWAutograd(torch.autograd.Function):
+        """The reference's ``SoftDTWAutograd`` glue (``softdtw.py:33-48``) over its compiled CPU operator."""
+
+        @staticmethod
+        def forward(ctx, D, lx, ly, gamma, bw):
+            costs, R = load_ref().forward(D, lx, ly, gamma, bw)
+            ctx.save_for_backward(D, R, lx, ly)
+            ctx.gamma, ctx.bw = gamma, bw
+            return costs
+
+        @staticmethod
+        def backward(ctx, g):
+            D, R, lx, ly = ctx.saved_tensors
+            E = load_ref().backward(D, R, lx, ly, ctx.gamma, ctx.bw)
+            return g.unsqueeze(-1).unsqueeze(-1) * E, None, None, None, None
+
+    return RefSoftDTWAutograd
+
+
+_REF_AUTOGRAD = None
+
+
+def reference_module_step(X, Y, lx, ly, gamma: float, bandwidth: int, normalize: bool, backward: bool = True):
+    """One step of the reference module (``SoftDTW.forward``, ``softdtw.py:106-142``) on CPU tensors:
+    the distance, the compiled reference operator under torch autograd, the optional normalisation,
+    and (``backward``) grad_X of ``costs.sum()``. Returns (costs, grad_X or None)."""
+    global _REF_AUTOGRAD
+    if _REF_AUTOGRAD is None:
+        _REF_AUTOGRAD = _ref_autograd_class()
+    Xr = X.detach().requires_grad_(backward)
+    D = ref_pairwise_l2_squared_torch(Xr, Y)
+    costs = _REF_AUTOGRAD.apply(D, lx, ly, float(gamma), int(bandwidth))
+    if normalize:
+        costs = costs / (lx + ly - 1).to(costs.dtype)
+    if backward:
+        costs.sum().backward()
+        return costs.detach(), Xr.grad
+    return costs.detach(), None

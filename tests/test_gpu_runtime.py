@@ -200,10 +200,14 @@ def test_wait_timeout_is_reported_and_context_survives(cuda, path, direction):
     lib.sdtw_debug_inject_stall(0 if direction == "forward" else 3)
     try:
         if direction == "forward":
-            torch.ops.torchsoftdtw.forward(D, lx, ly, 1.0, -1)
+            c, _ = torch.ops.torchsoftdtw.forward(D, lx, ly, 1.0, -1)
         else:
             torch.ops.torchsoftdtw.backward(D, R, lx, ly, 1.0, -1)
         torch.cuda.synchronize()
+        if direction == "forward":
+            # The aborted pair never reaches its terminal cell: its cost stays at the NaN it starts as, so
+            # a caller that never reads the error word still cannot mistake it for a value.
+            assert torch.isnan(c[0]).item()
         with pytest.raises(RuntimeError, match="timed out"):
             T.check_errors(cuda)
     finally:

@@ -63,9 +63,10 @@ def forward_noalloc(lib, D, lx, ly, gamma, bw, code):
 
 
 # (B, N, M, bandwidth, dtype, ragged): the headline shape (one CTA per pair), a small banded ragged batch
-# (strips claimed from the ticket counter, boundary rows in the scratch), and fp64.
+# (strips claimed from the ticket counter, boundary rows in the scratch), fp64, and the fp64 headline
+# shape, which runs on the pair-resident kernels and needs only the scratch's header.
 CASES = [(256, 512, 512, -1, torch.float32, False), (6, 300, 200, 20, torch.float32, True),
-         (4, 100, 90, -1, torch.float64, True)]
+         (4, 100, 90, -1, torch.float64, True), (256, 512, 512, -1, torch.float64, False)]
 
 
 @pytest.mark.parametrize("B,N,M,bw,dtype,ragged", CASES)
@@ -83,7 +84,9 @@ def test_noalloc_forward_matches_workspace_forward_twice(cuda, B, N, M, bw, dtyp
 
 def test_noalloc_rejects_problems_beyond_its_scratch(cuda):
     lib = _ext.capi()
-    B, N, M = 512, 1024, 1024  # strip-ticket workspace: 512 * 32 * 1024 * 4 bytes > 16 MiB
+    # Few long pairs run on the strip-ticket kernels: 16 pairs * 128 strips * 4096 * 4 bytes of boundary
+    # rows (32 MiB) > 16 MiB.
+    B, N, M = 16, 4096, 4096
     assert lib.sdtw_forward_workspace_bytes(B, N, M, 0) > (16 << 20)
     dummy = torch.zeros(8, device=cuda)
     st = lib.sdtw_forward_noalloc(0, p(dummy), B, N, M, p(dummy), p(dummy), 0, 1.0, -1, p(dummy), p(dummy),

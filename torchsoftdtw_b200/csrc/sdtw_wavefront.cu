@@ -674,6 +674,15 @@ bool use_warp_kernels(const DeviceInfo& di, int64_t B, int64_t N, int64_t M)
     return sizeof(T) == 8 && strips_of(N) <= 4 && B >= 8 * static_cast<int64_t>(di.sms);
 }
 
+// Workspace bytes the forward kernel chosen for this shape needs: the header alone for the warp-per-pair
+// and pair-resident kernels, the header and the strip boundary rows for the strip-ticket kernels.
+template <typename T>
+size_t forward_ws_needed(const DeviceInfo& di, int64_t B, int64_t N, int64_t M)
+{
+    if (use_warp_kernels<T>(di, B, N, M) || choose_pair_warps<T>(di, false, B, N, M) > 0) return kHeader;
+    return kHeader + bnd_bytes(B, N, M, sizeof(T));
+}
+
 template <typename T>
 sdtw_status launch_forward(const void* D, int64_t B, int64_t N, int64_t M, const void* lx, const void* ly, int is32,
                            double gamma, int64_t bw, void* R, void* costs, void* ws, uint32_t* err,
@@ -681,6 +690,10 @@ sdtw_status launch_forward(const void* D, int64_t B, int64_t N, int64_t M, const
 {
     const DeviceInfo* di = nullptr;
     cudaError_t e = device_info(di);
+    if (e != cudaSuccess) return from_cuda(e);
+    // Every cost starts as NaN (all-ones bits): a pair whose strips never finish (a launch that aborted on
+    // a wait timeout) then reads as NaN even when nobody checks the error word.
+    e = cudaMemsetAsync(costs, 0xff, static_cast<size_t>(B) * sizeof(T), stream);
     if (e != cudaSuccess) return from_cuda(e);
     if (use_warp_kernels<T>(*di, B, N, M))
         return from_cuda(warp_forward<T>(static_cast<const T*>(D), static_cast<T*>(R), static_cast<T*>(costs), lx, ly,
@@ -868,35 +881,28 @@ size_t sdtw_backward_workspace_bytes(int64_t B, int64_t N, int64_t M, sdtw_dtype
 }
 
 /* Forward for callers that cannot allocate device memory (see the header): the workspace is the static
- * device array g_noalloc_scratch. The first call on a device looks its address up; later calls only
- * enqueue work. The launch resets the scratch itself (cudaMemsetAsync of the header to 0 and of the
- * boundary rows to 0xFF), so its content between calls does not matter. */
+ * device array g_noalloc_scratch. Every call looks the array's address up on the current device
+ * (cudaGetSymbolAddress allocates nothing; the first lookup on a device may load this library's module
+ * there), so the address is never stale, also after a cudaDeviceReset. The launch resets the scratch itself
+ * (cudaMemsetAsync of the header to 0 and of the boundary rows to 0xFF), so its content between calls does
+ * not matter. The size limit applies to the workspace of the kernel this shape runs on. */
 sdtw_status sdtw_forward_noalloc(sdtw_dtype dtype, const void* D, int64_t B, int64_t N, int64_t M,
                                  const void* lengths_x, const void* lengths_y, int lengths_int32, double gamma,
                                  int64_t bandwidth, void* R, void* costs, uint32_t* err_word, void* stream)
 {
-    static std::mutex mu;
-    static void* scratch[128] = {};
     if (dtype != SDTW_F32 && dtype != SDTW_F64) return SDTW_EDTYPE;
     if (!common_args_ok(B, N, M, gamma)) return SDTW_EINVAL;
     if (B == 0) return SDTW_OK;
     if (!lengths_x || !lengths_y || !R || !costs || !err_word || (N * M > 0 && !D)) return SDTW_EINVAL;
-    if (sdtw_forward_workspace_bytes(B, N, M, dtype) > SDTW_NOALLOC_SCRATCH_BYTES) return SDTW_ETOOLARGE;
-    int dev = 0;
-    cudaError_t e = cudaGetDevice(&dev);
+    const DeviceInfo* di = nullptr;
+    cudaError_t e = device_info(di);
     if (e != cudaSuccess) return from_cuda(e);
-    if (dev < 0 || dev >= 128) return SDTW_EDEVICE;
+    const size_t need = dtype == SDTW_F32 ? forward_ws_needed<float>(*di, B, N, M)
+                                          : forward_ws_needed<double>(*di, B, N, M);
+    if (need > SDTW_NOALLOC_SCRATCH_BYTES) return SDTW_ETOOLARGE;
     void* ws = nullptr;
-    {
-        std::lock_guard<std::mutex> lock(mu);
-        if (!scratch[dev]) {
-            void* p = nullptr;
-            e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-            if (e != cudaSuccess) return from_cuda(e);
-            scratch[dev] = p;
-        }
-        ws = scratch[dev];
-    }
+    e = cudaGetSymbolAddress(&ws, g_noalloc_scratch);
+    if (e != cudaSuccess) return from_cuda(e);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     if (dtype == SDTW_F32)
         return launch_forward<float>(D, B, N, M, lengths_x, lengths_y, lengths_int32, gamma, bandwidth, R, costs, ws,

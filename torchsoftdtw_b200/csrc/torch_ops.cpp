@@ -59,7 +59,11 @@ sdtw_dtype code_of(at::ScalarType st) { return st == at::kDouble ? SDTW_F64 : SD
 // Lengths as the kernels read them: int32 or int64, contiguous, on D's device.
 Tensor prep_lengths(const Tensor& l) { return l.contiguous(); }
 
-// One sticky device error word per device, owned by this library for the process lifetime.
+// One sticky device error word per device, owned by this library for the process lifetime. It is created
+// by the first op call on the device, which must not be under CUDA-graph capture: a word allocated there
+// would come from the graph's private memory pool (and its zero-fill would be a captured memset), and the
+// library would keep a pointer that dies with the graph. A capture that reaches a device without a word
+// raises instead; one eager call before the capture (a warm-up step) creates it.
 uint32_t* error_word(const Tensor& like)
 {
     static std::mutex mu;
@@ -68,6 +72,12 @@ uint32_t* error_word(const Tensor& like)
     const int dev = like.get_device();
     auto it = words.find(dev);
     if (it == words.end()) {
+        cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+        const cudaStream_t stream = at::cuda::getCurrentCUDAStream(dev).stream();
+        TORCH_CHECK(cudaStreamIsCapturing(stream, &cap) == cudaSuccess && cap == cudaStreamCaptureStatusNone,
+                    "torchsoftdtw_b200: the first op call on ", like.device(),
+                    " is under CUDA-graph capture; run one call outside the capture first (a warm-up step), "
+                    "which creates the device's error word");
         it = words.emplace(dev, at::zeros({1}, like.options().dtype(at::kInt))).first;
     }
     return reinterpret_cast<uint32_t*>(it->second.data_ptr<int>());
