@@ -520,7 +520,8 @@ def measured_traffic(w, world: int, name: str):
 #   backward : read R + write E                      = 2
 #   pairwise : write D (X, Y reads are O((N+M)d/NM)) = 1
 #   grad     : read E (D only for pairs with a clamped cell) = 1
-ALGO_BYTES = {"sdtw_forward": 2, "sdtw_backward": 2, "sdtw_pairwise_l2": 1, "sdtw_grad_l2": 1}
+ALGO_BYTES = {"sdtw_forward": 2, "sdtw_backward": 2, "sdtw_forward_tiles": 2, "sdtw_backward_tiles": 2,
+              "sdtw_pairwise_l2": 1, "sdtw_grad_l2": 1}
 
 
 def kernel_times(T, X, Y, lx, ly, w, dev, flush, reps: int = 20):
@@ -558,6 +559,16 @@ def kernel_times(T, X, Y, lx, ly, w, dev, flush, reps: int = 20):
         "sdtw_grad_l2": lambda: lib.sdtw_grad_l2(code, p(X), p(Y), p(D), p(E), p(g), p(flags), B, N, M, d, p(gX),
                                                  None, sp),
     }
+    if lib.sdtw_r_tiled(B, N, M, code):
+        # The module path hands R over as strip tiles for this shape: time the calls it makes.
+        Rt = torch.empty(lib.sdtw_r_tiles_elems(B, N, M), device=dev, dtype=X.dtype)
+        calls["sdtw_forward_tiles"] = lambda: lib.sdtw_forward_tiles(code, p(D), B, N, M, p(lx), p(ly), is32, w.gamma,
+                                                                     w.bandwidth, p(Rt), p(costs), p(ws), wsf, p(err),
+                                                                     sp)
+        calls["sdtw_backward_tiles"] = lambda: lib.sdtw_backward_tiles(code, p(Rt), B, N, M, p(lx), p(ly), is32,
+                                                                       w.gamma, w.bandwidth, p(E), p(ws), wsb, p(err),
+                                                                       sp)
+        del calls["sdtw_forward"], calls["sdtw_backward"]
     out = {}
     for name, fn in calls.items():
         st = fn()

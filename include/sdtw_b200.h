@@ -117,6 +117,30 @@ sdtw_status sdtw_backward(sdtw_dtype dtype, const void* D, const void* R, int64_
                           uint32_t* err_word, void* stream);
 
 /* ---------------------------------------------------------------------------------------------------
+ * R as strip tiles: the layout in which the module path hands R from the forward to the backward (no
+ * counterpart in the reference, whose module keeps the padded R of the op; the padded R stays the layout of
+ * sdtw_forward / sdtw_backward). Tile (b, s, k), s = 0 .. ceil(N/32)-1, k = 0 .. M/32 (integer division), is
+ * 32 x 32 elements, contiguous: row l, element x is R[32 s + l][32 k + x - l - 1] (DP indices; +inf outside
+ * the band and the lengths). Each tile row is written and read as one bulk copy, against the per-element
+ * copies of the padded layout. Only available when both directions run on the pair-resident kernels for the
+ * shape: sdtw_r_tiled(...) != 0 (a property of the shape, the dtype and the current device).
+ *   sdtw_r_tiles_elems: elements of the tile array (16-byte aligned device memory, any initial content).
+ *   sdtw_forward_tiles / sdtw_backward_tiles: sdtw_forward / sdtw_backward with R_tiles in place of R;
+ *     SDTW_EINVAL when sdtw_r_tiled is 0. Same workspace sizes. The backward takes the forward's tiles for the
+ *     same D, lengths, gamma and bandwidth.
+ * ------------------------------------------------------------------------------------------------- */
+int sdtw_r_tiled(int64_t B, int64_t N, int64_t M, sdtw_dtype dtype);
+int64_t sdtw_r_tiles_elems(int64_t B, int64_t N, int64_t M);
+sdtw_status sdtw_forward_tiles(sdtw_dtype dtype, const void* D, int64_t B, int64_t N, int64_t M,
+                               const void* lengths_x, const void* lengths_y, int lengths_int32, double gamma,
+                               int64_t bandwidth, void* R_tiles, void* costs, void* workspace,
+                               size_t workspace_bytes, uint32_t* err_word, void* stream);
+sdtw_status sdtw_backward_tiles(sdtw_dtype dtype, const void* R_tiles, int64_t B, int64_t N, int64_t M,
+                                const void* lengths_x, const void* lengths_y, int lengths_int32, double gamma,
+                                int64_t bandwidth, void* E, void* workspace, size_t workspace_bytes,
+                                uint32_t* err_word, void* stream);
+
+/* ---------------------------------------------------------------------------------------------------
  * Pairwise squared Euclidean cost: D[b,i,j] = (|x_i|^2 + |y_j|^2) - 2 x_i.y_j, clamped at 0.
  * Replaces the reference's pairwise_l2_squared (src/torchsoftdtw/distances.py:4-18) on the module path.
  * Cells where the unclamped value is negative are stored as -0.0 (sign bit set), so that the

@@ -4,7 +4,8 @@ module (golden fixtures) and the oracle's module restatement; the l1 / cosine pa
 
 Tolerances: fp64 costs rtol 1e-10, fp64 gradients rtol 1e-8 (D is summed in a different order than
 torch's bmm); fp32 costs rtol 1e-5 / atol 1e-6; fp32 gradients vs the oracle in fp64 within the literal
-tolerance or no worse than the reference's own fp32 error."""
+tolerance or at most 0.25 times the reference's own fp32 error (measured: 0.02-0.13 times,
+tests/test_gpu_error_table.py)."""
 
 import numpy as np
 import pytest
@@ -32,8 +33,12 @@ def run_module(X, Y, lx, ly, gamma, bw, normalize, dev, need=(True, True), dista
     return costs.detach().cpu().numpy(), gx, gy
 
 
+F32_GRAD_RATIO = 0.25
+
+
 def grad_contract(ours, X, Y, lx, ly, gamma, bw, normalize, which):
-    """fp32 gradient vs fp64 oracle: literal tolerance or no worse than the reference's fp32 error."""
+    """fp32 gradient vs fp64 oracle: literal tolerance or at most F32_GRAD_RATIO times the reference's fp32
+    error on the same inputs."""
     _, gx64, gy64 = O.module_forward_backward(X.astype(np.float64), Y.astype(np.float64), lx, ly, gamma, bw,
                                               normalize)
     _, gx32, gy32 = O.module_forward_backward(X.astype(np.float32), Y.astype(np.float32), lx, ly, gamma, bw,
@@ -44,7 +49,7 @@ def grad_contract(ours, X, Y, lx, ly, gamma, bw, normalize, which):
     with np.errstate(invalid="ignore"):
         err_ref = float(np.nanmax(np.abs(refe.astype(np.float64) - exact)))
     literal = 1e-6 + 1e-5 * float(np.max(np.abs(exact)))
-    assert err <= max(literal, err_ref), (which, err, err_ref, literal)
+    assert err <= max(literal, F32_GRAD_RATIO * err_ref), (which, err, err_ref, literal)
 
 
 @pytest.mark.parametrize("name", golden_names("mod_"))

@@ -289,3 +289,67 @@ def test_bad_lengths_give_nan_and_error_bit(cuda):
     with pytest.raises(RuntimeError, match="outside"):
         T.check_errors(cuda)
     T.check_errors(cuda)  # cleared
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float64])
+@pytest.mark.parametrize("B,N,M,bw,ragged", [(3, 100, 90, -1, False), (4, 257, 130, 20, True), (5, 64, 300, 3, True),
+                                             (2, 31, 33, -1, True), (3, 450, 70, 0, False), (2, 200, 512, -1, False)])
+def test_r_tiles_match_padded_r(cuda, dtype, B, N, M, bw, ragged):
+    """The module path's R tiles (sdtw_forward_tiles / sdtw_backward_tiles, pair-resident kernels) give the same
+    costs and E as the padded R, bit for bit, and every tile row holds the padded R's values."""
+    lib = _ext.capi()
+    code = 1 if dtype == torch.float64 else 0
+    g = torch.Generator().manual_seed(N * 3 + M + B)
+    D = (torch.rand(B, N, M, generator=g, dtype=torch.float64) * 2).to(dtype).to(cuda)
+    if ragged:
+        lx = torch.randint(max(1, N // 2), N + 1, (B,), generator=g)
+        ly = torch.randint(max(1, M // 2), M + 1, (B,), generator=g)
+    else:
+        lx, ly = torch.full((B,), N), torch.full((B,), M)
+    lx, ly = lx.to(cuda), ly.to(cuda)
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    p = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+    err = torch.zeros(1, device=cuda, dtype=torch.int32)
+    ws = torch.empty(max(lib.sdtw_forward_workspace_bytes(B, N, M, code), lib.sdtw_backward_workspace_bytes(B, N, M, code)),
+                     device=cuda, dtype=torch.uint8)
+    try:
+        lib.sdtw_debug_force_path(2)
+        assert lib.sdtw_r_tiled(B, N, M, code) == 1
+        S, NBt = (N + 31) // 32, (M + 31) // 32 + 1
+        assert lib.sdtw_r_tiles_elems(B, N, M) == B * S * NBt * 1024
+        Rt = torch.full((B, S, NBt, 32, 32), float("nan"), device=cuda, dtype=dtype)
+        c1 = torch.empty(B, device=cuda, dtype=dtype)
+        E1 = torch.empty(B, N, M, device=cuda, dtype=dtype)
+        st = lib.sdtw_forward_tiles(code, p(D), B, N, M, p(lx), p(ly), 0, 0.3, bw, p(Rt), p(c1), p(ws), ws.numel(),
+                                    p(err), stream)
+        assert st == 0, lib.sdtw_status_string(st)
+        st = lib.sdtw_backward_tiles(code, p(Rt), B, N, M, p(lx), p(ly), 0, 0.3, bw, p(E1), p(ws), ws.numel(), p(err),
+                                     stream)
+        assert st == 0, lib.sdtw_status_string(st)
+        c2, R2 = torch.ops.torchsoftdtw.forward(D, lx, ly, 0.3, bw)
+        E2 = torch.ops.torchsoftdtw.backward(D, R2, lx, ly, 0.3, bw)
+        torch.cuda.synchronize()
+    finally:
+        lib.sdtw_debug_force_path(0)
+    assert lib.sdtw_read_error_word(p(err), stream) == 0
+    T.check_errors(cuda)
+    assert torch.equal(c1, c2)
+    assert torch.equal(E1, E2)
+    # Tile rows against the padded R: tile (b, s, k)[l][x] = R[32 s + l][32 k + x - l - 1] (padded row +1, column +1)
+    # wherever the tile was written (NaN marks a tile the forward did not sweep).
+    Rt_c, R2_c = Rt.cpu().numpy(), R2.cpu().numpy()
+    written = 0
+    lgrid, xgrid = np.meshgrid(np.arange(32), np.arange(32), indexing="ij")
+    for b in range(B):
+        for s in range(S):
+            rows = min(32, N - 32 * s)
+            for k in range(NBt):
+                tile = Rt_c[b, s, k]
+                if np.isnan(tile).all():
+                    continue
+                written += 1
+                c = 32 * k + xgrid - lgrid - 1
+                sel = (lgrid < rows) & (c >= 0) & (c < M)
+                want = R2_c[b, 32 * s + lgrid[sel] + 1, c[sel] + 1]
+                assert np.array_equal(tile[sel], want), (b, s, k)
+    assert written > 0

@@ -59,6 +59,10 @@ SIGNATURES: dict[str, tuple] = {
     "sdtw_forward_noalloc": (_i, [_i, _p, _i64, _i64, _i64, _p, _p, _i, _d, _i64, _p, _p, _p, _p]),
     "sdtw_backward_workspace_bytes": (_sz, [_i64, _i64, _i64, _i]),
     "sdtw_backward": (_i, [_i, _p, _p, _i64, _i64, _i64, _p, _p, _i, _d, _i64, _p, _p, _sz, _p, _p]),
+    "sdtw_r_tiled": (_i, [_i64, _i64, _i64, _i]),
+    "sdtw_r_tiles_elems": (_i64, [_i64, _i64, _i64]),
+    "sdtw_forward_tiles": (_i, [_i, _p, _i64, _i64, _i64, _p, _p, _i, _d, _i64, _p, _p, _p, _sz, _p, _p]),
+    "sdtw_backward_tiles": (_i, [_i, _p, _i64, _i64, _i64, _p, _p, _i, _d, _i64, _p, _p, _sz, _p, _p]),
     "sdtw_pairwise_l2": (_i, [_i, _p, _p, _i64, _i64, _i64, _i64, _p, _p, _p]),
     "sdtw_grad_l2": (_i, [_i, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _p, _p, _p]),
     "sdtw_pairwise_dist": (_i, [_i, _i, _p, _p, _i64, _i64, _i64, _i64, _d, _p, _p]),
@@ -88,3 +92,15 @@ def capi() -> ctypes.CDLL:
             fn.argtypes = args
         _capi = lib
     return _capi
+
+
+def r_tiled(B: int, N: int, M: int, dtype: torch.dtype, device) -> bool:
+    """Whether the module path keeps R as the forward's strip tiles for this shape and dtype on ``device``
+    (include/sdtw_b200.h, sdtw_r_tiled)."""
+    if B <= 0 or N <= 0 or M <= 0 or dtype not in (torch.float32, torch.float64):
+        return False
+    dev = torch.device(device)
+    if dev.type != "cuda":
+        return False
+    with torch.cuda.device(dev):
+        return bool(capi().sdtw_r_tiled(B, N, M, 1 if dtype == torch.float64 else 0))

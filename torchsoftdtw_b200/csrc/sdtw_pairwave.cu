@@ -28,35 +28,16 @@ namespace sdtw {
 
 namespace {
 
-// ---- shared-memory acquire / release on a CTA-scope progress counter ------------------------------
-__device__ __forceinline__ int ld_acquire_cta(const int* p)
-{
-    int v;
-    asm volatile("ld.acquire.cta.shared::cta.b32 %0, [%1];" : "=r"(v) : "r"(smem_addr(p)) : "memory");
-    return v;
-}
-__device__ __forceinline__ void st_release_cta_if(int* p, int v, bool pred)
-{
-    asm volatile(
-        "{ .reg .pred q; setp.ne.u32 q, %2, 0; @q st.release.cta.shared::cta.b32 [%0], %1; }" ::"r"(smem_addr(p)),
-        "r"(v), "r"(static_cast<unsigned>(pred))
-        : "memory");
-}
-
-// ---- forward progress barriers -------------------------------------------------------------------
-// The forward publishes its strip's last row in groups of 8 steps. Group g (= step / 8) of the strip held
-// by warp w completes mbarrier g of warp w's array (count 1, arrived by lane 0 after the group's values
-// are in shared memory). Each barrier completes exactly once per non-empty strip that warp sweeps (the
-// groups the sweep does not reach are completed when the strip ends), so the consumer of the strip in
-// round r of that warp waits for parity r & 1. A round can only complete a barrier after the consumer of
-// the previous round has passed it: the strip W positions later depends, through the W-1 strips between,
-// on that consumer being 4 groups further on. An empty strip (rows past the pair's length) completes
-// nothing, and nothing waits after it. A waiting warp is suspended by mbarrier.try_wait instead of polling.
-__device__ __forceinline__ void fbar_init(uint32_t bar) { asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(bar) : "memory"); }
-__device__ __forceinline__ void fbar_arrive(uint32_t bar)
-{
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
-}
+// ---- progress barriers between strips -----------------------------------------------------------
+// A strip publishes its boundary row (forward: its last row of R; backward: the contributions its first row
+// pushes into the row above) in groups of 8 steps, and group g (= step / 8) of the strip held by warp w
+// completes mbarrier g of warp w's array once the group's values are in shared memory. Each barrier
+// completes exactly once per non-empty strip that warp sweeps (the groups the sweep does not reach are
+// completed when the strip ends), so the consumer of the strip in round r of that warp waits for parity
+// r & 1. A round can only complete a barrier after the consumer of the previous round has passed it: the
+// strip W positions later depends, through the W-1 strips between, on that consumer being 4 groups further
+// on. An empty strip (rows past the pair's length) completes nothing, and nothing waits after it. A waiting
+// warp is suspended by mbarrier.try_wait instead of polling.
 __device__ __forceinline__ bool fbar_try_wait(uint32_t bar, uint32_t parity)
 {
     uint32_t ok;
@@ -87,55 +68,32 @@ __device__ __forceinline__ bool fbar_wait(uint32_t bar, uint32_t parity, const S
         if (__shfl_sync(kFull, stop, 0)) return false;
     }
 }
-// Progress barriers per warp for rows of M columns: groups 0 .. 4 * (blocks + 1) - 1.
+// Progress barriers per warp for rows of M columns: groups 0 .. 4 * (blocks + 1) - 1 (both directions).
 inline __host__ __device__ int fwd_groups(int64_t M) { return 4 * (static_cast<int>((M + 30) / 32) + 2); }
-
-// Warp-collective bounded wait until *prog >= need. `seen` caches the last value read (all lanes read
-// the same word, so it is warp-uniform). Keys count columns, so need - seen is the number of steps the
-// producer still has to take: the warp sleeps for about that many steps (~100 ns each, at most 2 us)
-// between polls instead of spinning, which leaves the issue slots to the warps that compute. Returns
-// false if the launch aborted or the wait ran out.
-__device__ __forceinline__ bool wait_key(const int* prog, int need, int& seen, const Sync& sy, int lane)
-{
-    if (seen >= need) return true;
-    seen = ld_acquire_cta(prog);
-    if (seen >= need) return true;
-    const uint64_t t0 = global_ns();
-    unsigned spins = 0;
-    while (true) {
-        const int deficit = need - seen;
-        __nanosleep(deficit >= 20 ? 2000u : 64u + 96u * static_cast<unsigned>(deficit));
-        seen = ld_acquire_cta(prog);
-        if (seen >= need) return true;
-        if ((++spins & 15u) == 0) {
-            int stop = 0;
-            if (lane == 0) {
-                if (aborted(sy)) {
-                    stop = 1;
-                } else if (global_ns() - t0 > sy.timeout_ns) {
-                    raise_error(sy, kErrTimeout);
-                    stop = 1;
-                }
-            }
-            if (__shfl_sync(kFull, stop, 0)) return false;
-        }
-    }
-}
 
 inline __host__ __device__ int buf_len(int64_t M) { return static_cast<int>((M + 128 + 3) / 4 * 4); }
 
-// Ring slot of block `blk` (blk >= -1) in the backward's three-slot ring.
-__device__ __forceinline__ int slot3(int blk) { return (blk + 3) % 3; }
 
 }  // namespace
 
 // ==================================================================================================
 // Forward
 // ==================================================================================================
+// Forward ring row stride in elements: 2 slots of 32 positions + pad. 68 floats / 66 doubles are 272 / 528
+// bytes, 16-byte multiples whose word stride is 4 (mod 32), so the per-lane 16-byte accesses of a quarter
+// warp (8 lanes, 8 rows) fall into 8 distinct 16-byte bank groups, and a whole row read or written one lane
+// per position is conflict-free.
+template <typename T>
+struct FwdRing {
+    static constexpr int S = sizeof(T) == 4 ? 68 : 66;
+};
+
 template <typename T>
 struct PairFwdArgs {
     const T* D;
-    T* R;
+    T* R;   // padded R (B, N+2, M+2), or null when Rt is given
+    T* Rt;  // R as strip tiles (B, S, NBt, 32, 32), or null (see pair_forward)
+    int NBt;
     T* costs;
     Lengths len;
     int64_t B, N, M, bw;
@@ -145,24 +103,25 @@ struct PairFwdArgs {
     int64_t inject;  // b * S + s: that strip never publishes its boundary row (failure-path test); -1 = none
 };
 
-// D rows r0..r0+31, skewed slot of block `blk` (positions 32*blk + lane) <- global, asynchronously.
-// Rows at or beyond `nrows` and columns outside [0, M) are zero-filled.
+// D rows r0..r0+31, skewed slot of block `blk` (positions 32*blk + lane) <- global, asynchronously. Ring row
+// r holds column c at position c + r + 1. Rows at or beyond `nrows` and columns outside [0, M) are zero-filled.
 template <typename T>
 __device__ __forceinline__ void fwd_pair_load(const T* Db, int64_t M, T* ring, int blk, int nrows, int lane)
 {
+    constexpr int S = FwdRing<T>::S;
     T* dst = ring + (blk & 1) * 32 + lane;
-    const int c0 = 32 * blk + lane;  // column read by row 0; row r reads column c0 - r
-    if (32 * blk - 31 >= 0 && 32 * blk + 31 < M && nrows == 32) {
+    const int c0 = 32 * blk + lane - 1;  // column read by row 0; row r reads column c0 - r
+    if (32 * blk - 32 >= 0 && 32 * blk + 30 < M && nrows == 32) {
         const T* src = Db + c0;
         const int64_t step = M - 1;  // a compile-time constant in the kernels specialized on M
 #pragma unroll
         for (int r = 0; r < 32; ++r)
-            cp_async_scalar<sizeof(T)>(dst + r * kFwdStride, src + r * step, static_cast<int>(sizeof(T)));
+            cp_async_scalar<sizeof(T)>(dst + r * S, src + r * step, static_cast<int>(sizeof(T)));
     } else {
         for (int r = 0; r < 32; ++r) {
             const int c = c0 - r;
             const bool in = r < nrows && c >= 0 && c < M;
-            cp_async_scalar<sizeof(T)>(dst + r * kFwdStride, in ? Db + static_cast<int64_t>(r) * M + c : Db,
+            cp_async_scalar<sizeof(T)>(dst + r * S, in ? Db + static_cast<int64_t>(r) * M + c : Db,
                                        in ? static_cast<int>(sizeof(T)) : 0);
         }
     }
@@ -173,56 +132,140 @@ template <typename T>
 __device__ __forceinline__ void fwd_pair_store(T* Rrow, int64_t pitch, int64_t M, const T* ring, int blk, int nmat,
                                                int lane)
 {
+    constexpr int S = FwdRing<T>::S;
     const T* src = ring + (blk & 1) * 32 + lane;
-    const int c0 = 32 * blk + lane;
-    if (32 * blk - 31 >= 0 && 32 * blk + 31 < M && nmat == 32) {
+    const int c0 = 32 * blk + lane - 1;  // column of row 0; row r: c0 - r
+    if (32 * blk - 32 >= 0 && 32 * blk + 30 < M && nmat == 32) {
         T* dst = Rrow + c0 + 1;
         const int64_t step = pitch - 1;
 #pragma unroll
-        for (int r = 0; r < 32; ++r) dst[r * step] = src[r * kFwdStride];
+        for (int r = 0; r < 32; ++r) dst[r * step] = src[r * S];
     } else {
         for (int r = 0; r < nmat; ++r) {
             const int c = c0 - r;
-            if (c >= 0 && c < M) Rrow[r * pitch + c + 1] = src[r * kFwdStride];
+            if (c >= 0 && c < M) Rrow[r * pitch + c + 1] = src[r * S];
         }
     }
 }
 
-// 8 forward steps tau0 .. tau0+7 of one warp. `cell` is this lane's ring row at position tau0, `top`
-// the row above (boundary row) at column tau0.
+// 8 consecutive elements <-> shared memory, 16-byte accesses (p 16-byte aligned).
+__device__ __forceinline__ void lds8(float (&v)[8], const float* p)
+{
+    const float4 x = reinterpret_cast<const float4*>(p)[0], y = reinterpret_cast<const float4*>(p)[1];
+    v[0] = x.x, v[1] = x.y, v[2] = x.z, v[3] = x.w, v[4] = y.x, v[5] = y.y, v[6] = y.z, v[7] = y.w;
+}
+__device__ __forceinline__ void lds8(double (&v)[8], const double* p)
+{
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const double2 x = reinterpret_cast<const double2*>(p)[i];
+        v[2 * i] = x.x, v[2 * i + 1] = x.y;
+    }
+}
+__device__ __forceinline__ void sts8(float* p, const float (&v)[8])
+{
+    reinterpret_cast<float4*>(p)[0] = make_float4(v[0], v[1], v[2], v[3]);
+    reinterpret_cast<float4*>(p)[1] = make_float4(v[4], v[5], v[6], v[7]);
+}
+__device__ __forceinline__ void sts8(double* p, const double (&v)[8])
+{
+#pragma unroll
+    for (int i = 0; i < 4; ++i) reinterpret_cast<double2*>(p)[i] = make_double2(v[2 * i], v[2 * i + 1]);
+}
+
+// Arrive (count `n`) on a forward progress barrier when `pred`.
+__device__ __forceinline__ void fbar_arrive_n_if(uint32_t bar, uint32_t n, bool pred)
+{
+    asm volatile("{ .reg .pred q; setp.ne.u32 q, %2, 0; @q mbarrier.arrive.shared::cta.b64 _, [%0], %1; }" ::"r"(bar),
+                 "r"(n), "r"(static_cast<unsigned>(pred))
+                 : "memory");
+}
+// Lanes that publish a group of the boundary row: each arrives once, so a barrier phase completes after all
+// of them stored their value (each arrive releases its own store; no second warp barrier is needed).
+constexpr int kPubLanes = 8;
+
+// Out-of-line part of the bounded wait (the common case, a phase already complete, is one try_wait).
+__device__ __noinline__ bool fbar_wait_slow(uint32_t bar, uint32_t parity, Sync sy, int lane)
+{
+    return fbar_wait(bar, parity, sy, lane);
+}
+__device__ __forceinline__ bool fbar_wait_fast(uint32_t bar, uint32_t parity, const Sync& sy, int lane)
+{
+    if (__all_sync(kFull, fbar_try_wait(bar, parity))) return true;
+    return fbar_wait_slow(bar, parity, sy, lane);
+}
+
+// 8 forward steps tau0 .. tau0+7 of one warp. `cell` is this lane's ring row at position tau0 (read and
+// written with 16-byte accesses), `top` the row above (boundary row) at column tau0.
 template <typename T, bool MASKED>
 __device__ __forceinline__ void fwd_pair_steps8(T* cell, const T* top, int tau0, int A, int Z, T k, T gl,
                                                 int src_lane, bool lane0, T& outp, T& upp)
 {
     const T INF = Num<T>::inf();
+    T dv[8], tv[8];
+    lds8(dv, cell);
+    lds8(tv, top);
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
-        const T d = cell[j];
-        const T tv = top[j];
         const T upw = __shfl_sync(kFull, outp, src_lane);
-        const T up = lane0 ? tv : upw;
-        T r = fwd_cell<T>(d, upp, up, outp, k, gl);
+        const T up = lane0 ? tv[j] : upw;
+        T r = fwd_cell<T>(dv[j], upp, up, outp, k, gl);
         if (MASKED) {
             const int tau = tau0 + j;
             r = (tau >= A && tau <= Z) ? r : INF;
         }
-        cell[j] = r;
+        dv[j] = r;
         upp = up;
         outp = r;
     }
+    sts8(cell, dv);
+}
+
+// The 32 steps of block `tau0 / 32`, as four groups of 8: wait for the strip above (group g of this strip
+// reads columns up to 8g + 7 of the row above, complete with the group g + 4 of the strip above), sweep,
+// publish the 8 values of the last row that the group finished. Returns false if the launch aborted.
+template <typename T, bool MASKED>
+__device__ __forceinline__ bool fwd_pair_block(T* cell, const T* top, const T* last, T* bout, int tau0, int A, int Z,
+                                               T k, T gl, bool wait_in, uint32_t bars_in, uint32_t par_in, int glast,
+                                               bool publish, bool has_consumer, uint32_t bars_out, const Sync& sy,
+                                               int src_lane, int lane, T& outp, T& upp)
+{
+    const bool lane0 = lane == 0;
+    const bool pub_lane = lane < kPubLanes;
+    const int g0 = tau0 / 8;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        if (wait_in && !fbar_wait_fast(bars_in + 8 * min(g0 + q + 4, glast), par_in, sy, lane)) return false;
+        fwd_pair_steps8<T, MASKED>(cell + 8 * q, top + 8 * q, tau0 + 8 * q, A, Z, k, gl, src_lane, lane0, outp, upp);
+        if (publish) {
+            // Columns tau0 + 8q - 31 .. tau0 + 8q - 24 of the last row, written by lane 31 above.
+            __syncwarp();
+            const T v = last[8 * q + (lane & (kPubLanes - 1))];
+            if (pub_lane && has_consumer) bout[tau0 + 8 * q + lane - 31 + kBufPad] = v;
+            fbar_arrive_n_if(bars_out + 8 * (g0 + q), 1, pub_lane);
+        }
+    }
+    return true;
 }
 
 // One strip of the forward. Returns false if the launch aborted. MC > 0: the kernel is specialized on
 // M == MC, so every row offset in the ring's loads and stores is a compile-time constant.
+//
+// Lane l processes column c at step tau = c + l + 1 (ring position tau), one step later than the skew of the
+// strip-ticket kernels: a block's slot then holds, for row l, exactly the columns 32*blk + x - l - 1 that the
+// backward's ring row l + 1 needs at its positions 32*blk + x, so that R can travel between the two as whole
+// 32 x 32 tiles (PairFwdArgs::Rt). The boundary rows are indexed by column + kBufPad + 1.
 template <typename T, int MC>
 __device__ bool fwd_pair_strip(const PairFwdArgs<T>& a, T* ring, const T* bin, uint32_t bars_in, uint32_t par_in,
                                T* bout, uint32_t bars_out, int64_t b, int s, int lane)
 {
+    constexpr int RS = FwdRing<T>::S;
     const T INF = Num<T>::inf();
     const int64_t N = a.N, M = MC > 0 ? MC : a.M, pitch = M + 2;
+    const bool tiles = a.Rt != nullptr;
     const int r0 = 32 * s;
     const int nmat = static_cast<int>(N - r0 < 32 ? N - r0 : 32);
-    T* Rrow = a.R + b * (N + 2) * pitch + static_cast<int64_t>(r0 + 1) * pitch;
+    T* Rrow = tiles ? nullptr : a.R + b * (N + 2) * pitch + static_cast<int64_t>(r0 + 1) * pitch;
     Strip st;
     if (!make_strip(st, a.len, b, s, N, M, a.bw, lane)) {
         if (s == 0 && lane == 0) {
@@ -233,18 +276,22 @@ __device__ bool fwd_pair_strip(const PairFwdArgs<T>& a, T* ring, const T* bin, u
                 a.costs[b] = (st.nx == 0 && st.ny == 0) ? T(0) : INF;
             }
         }
-        for (int r = 0; r < nmat; ++r)
-            for (int c = lane; c < M + 2; c += 32) Rrow[r * pitch + c] = INF;
+        if (!tiles)
+            for (int r = 0; r < nmat; ++r)
+                for (int c = lane; c < M + 2; c += 32) Rrow[r * pitch + c] = INF;
         // No barrier arrivals: every later strip of this pair is empty too, so nothing waits on this
         // warp's barriers again (arriving here could lap the phase the strip below the previous round
         // is still waiting for).
         return true;
     }
-    const int k0 = st.c_begin >> 5;
-    const int k1 = (st.c_end + 31) >> 5;
+    // Valid steps of this lane and of the whole warp, in this kernel's step numbering.
+    const int A = st.A + 1, Z = st.Z + 1, Amax = st.Amax + 1, Zmin = st.Zmin + 1;
+    const int k0 = (st.c_begin + 1) >> 5;
+    const int k1 = (st.c_end + 32) >> 5;
     const bool skip = b * a.S + s == a.inject;
     const bool has_consumer = st.rows == 32 && r0 + 32 < st.nx && !skip;
     const T* Db = a.D + (b * N + r0) * M;
+    T* tile0 = tiles ? a.Rt + ((b * a.S + s) * static_cast<int64_t>(a.NBt) * 32 + lane) * 32 : nullptr;
 
     cp_async_wait<0>();
     __syncwarp();
@@ -253,62 +300,60 @@ __device__ bool fwd_pair_strip(const PairFwdArgs<T>& a, T* ring, const T* bin, u
     if (k0 + 1 <= k1) fwd_pair_load<T>(Db, M, ring, k0 + 1, st.rows, lane);
     cp_async_commit();
 
-    // Columns of each row outside the swept range [32*k0 - r, 32*k1 + 31 - r], and the border: +inf.
-    for (int r = 0; r < nmat; ++r) {
-        T* row = Rrow + r * pitch;
-        int pe = 32 * k0 - r;
-        pe = pe < 0 ? 0 : pe;
-        int ss = 32 * k1 + 32 - r;
-        ss = ss > M ? static_cast<int>(M) : ss;
-        for (int c = lane; c <= pe; c += 32) row[c] = INF;
-        for (int c = ss + 1 + lane; c < M + 2; c += 32) row[c] = INF;
+    if (!tiles) {
+        // Padded columns of each row outside the swept range (columns 32*k0 - r - 1 .. 32*k1 + 30 - r, padded
+        // index + 1), and the border: +inf.
+        for (int r = 0; r < nmat; ++r) {
+            T* row = Rrow + r * pitch;
+            int pe = 32 * k0 - r - 1;
+            pe = pe < 0 ? 0 : pe;
+            int ss = 32 * k1 + 32 - r;
+            ss = ss > M + 1 ? static_cast<int>(M + 1) : ss;
+            for (int c = lane; c <= pe; c += 32) row[c] = INF;
+            for (int c = ss + lane; c < M + 2; c += 32) row[c] = INF;
+        }
     }
 
     // Terminal cell (nx-1, ny-1): lane lstar at step tstar.
     const int lstar = static_cast<int>(st.nx - 1 - r0);
-    const int tstar = static_cast<int>(st.ny - 1) + lstar;
+    const int tstar = static_cast<int>(st.ny - 1) + lstar + 1;
     const int bstar = (lstar >= 0 && lstar < 32) ? (tstar >> 5) : INT_MIN;
 
-    // Group g of the strip above publishes its last row through column 8g - 24, so the columns up to
-    // 8g + 7 that group g of this strip reads are complete with its group g + 4 (or, past its sweep, with
-    // the barriers completed when it ends).
     const int glast = a.G - 1;
-    if (s > 0 && !fbar_wait(bars_in + 8 * min(4 * k0 + 4, glast), par_in, a.sy, lane)) return false;
-    T upp = lane == 0 ? bin[32 * k0 - 1 + kBufPad] : INF;  // lane 0's diagonal predecessor
+    const bool wait_in = s > 0;
+    if (wait_in && !fbar_wait(bars_in + 8 * min(4 * k0 + 4, glast), par_in, a.sy, lane)) return false;
+    T upp = lane == 0 ? bin[32 * k0 - 1 + kBufPad] : INF;  // lane 0's diagonal predecessor (column 32*k0 - 2)
     T outp = INF;
     const int src_lane = (lane + 31) & 31;
-    const bool lane0 = lane == 0;
 
 #pragma unroll 1
     for (int blk = k0; blk <= k1; ++blk) {
         cp_async_wait<1>();
         __syncwarp();
         const int tau0 = 32 * blk;
-        T* cell = ring + lane * kFwdStride + (blk & 1) * 32;
+        T* cell = ring + lane * RS + (blk & 1) * 32;
         const T* top = bin + tau0 + kBufPad;
-        const T* last = ring + 31 * kFwdStride + (blk & 1) * 32;  // the strip's last row, positions tau0 ..
-        const bool full = tau0 >= st.Amax && tau0 + 31 <= st.Zmin;
-#pragma unroll 1
-        for (int q = 0; q < 4; ++q) {
-            const int t8 = tau0 + 8 * q;
-            if (s > 0 && !fbar_wait(bars_in + 8 * min(t8 / 8 + 4, glast), par_in, a.sy, lane)) return false;
-            if (full)
-                fwd_pair_steps8<T, false>(cell + 8 * q, top + 8 * q, t8, st.A, st.Z, a.k, a.gl, src_lane, lane0,
-                                          outp, upp);
-            else
-                fwd_pair_steps8<T, true>(cell + 8 * q, top + 8 * q, t8, st.A, st.Z, a.k, a.gl, src_lane, lane0,
-                                         outp, upp);
-            if (!skip) {
-                // Publish the last row's 8 new values (columns t8 - 31 .. t8 - 24) from the ring.
-                __syncwarp();
-                if (has_consumer && lane < 8) bout[t8 + lane - 31 + kBufPad] = last[8 * q + lane];
-                __syncwarp();
-                if (lane == 0) fbar_arrive(bars_out + 8 * (t8 / 8));
-            }
+        const T* last = ring + 31 * RS + (blk & 1) * 32;  // the strip's last row, positions tau0 ..
+        const bool ok = (tau0 >= Amax && tau0 + 31 <= Zmin)
+                            ? fwd_pair_block<T, false>(cell, top, last, bout, tau0, A, Z, a.k, a.gl, wait_in, bars_in,
+                                                       par_in, glast, !skip, has_consumer, bars_out, a.sy, src_lane,
+                                                       lane, outp, upp)
+                            : fwd_pair_block<T, true>(cell, top, last, bout, tau0, A, Z, a.k, a.gl, wait_in, bars_in,
+                                                      par_in, glast, !skip, has_consumer, bars_out, a.sy, src_lane,
+                                                      lane, outp, upp);
+        if (!ok) return false;
+        if (tiles) {
+            // Row `lane` of the block's slot -> tile (b, s, blk), one bulk copy per lane (the lane's own writes,
+            // ordered before the copy by the proxy fence).
+            fence_proxy_async_smem();
+            bulk_s2g(tile0 + static_cast<int64_t>(blk) * 1024, cell, 32 * sizeof(T));
+            bulk_commit();
+        } else {
+            __syncwarp();
+            fwd_pair_store<T>(Rrow, pitch, M, ring, blk, nmat, lane);
         }
-        __syncwarp();
-        fwd_pair_store<T>(Rrow, pitch, M, ring, blk, nmat, lane);
         if (blk == bstar && lane == lstar) a.costs[b] = cell[tstar - tau0];
+        if (tiles) bulk_wait_read<0>();  // the slot is refilled next
         __syncwarp();
         if (blk + 2 <= k1) fwd_pair_load<T>(Db, M, ring, blk + 2, st.rows, lane);
         cp_async_commit();
@@ -318,9 +363,10 @@ __device__ bool fwd_pair_strip(const PairFwdArgs<T>& a, T* ring, const T* bin, u
         if (has_consumer)
             for (int c = 32 * k1 + 1 + lane; c + kBufPad < a.BL; c += 32) bout[c + kBufPad] = INF;
         __syncwarp();
-        // Complete the barriers of the groups this sweep did not reach (every barrier once per strip).
+        // Complete the barriers of the groups this sweep did not reach (every barrier once per strip; each
+        // phase expects kPubLanes arrivals).
         for (int g = lane; g < a.G; g += 32)
-            if (g < 4 * k0 || g > 4 * k1 + 3) fbar_arrive(bars_out + 8 * g);
+            if (g < 4 * k0 || g > 4 * k1 + 3) fbar_arrive_n_if(bars_out + 8 * g, kPubLanes, true);
     }
     return true;
 }
@@ -329,11 +375,12 @@ template <typename T, int MC>
 __global__ void __launch_bounds__(SDTW_PAIR_THREADS, SDTW_PAIR_MIN_CTAS) sdtw_fwd_pair_kernel(PairFwdArgs<T> a)
 {
     extern __shared__ __align__(16) unsigned char smem[];
+    constexpr int RS = FwdRing<T>::S;
     const int lane = threadIdx.x & 31;
     const int warp = threadIdx.x >> 5;
     const int W = a.W;
     T* rings = reinterpret_cast<T*>(smem);
-    T* bufs = rings + static_cast<size_t>(W) * 32 * kFwdStride;
+    T* bufs = rings + static_cast<size_t>(W) * 32 * RS;
     T* crow = bufs + static_cast<size_t>(W) * a.BL;
     T* scratch = crow + a.BL;  // 32 elements per warp
     const uint32_t bars = (smem_addr(scratch + static_cast<size_t>(W) * 32) + 7u) & ~7u;  // [W][G] mbarriers
@@ -341,18 +388,21 @@ __global__ void __launch_bounds__(SDTW_PAIR_THREADS, SDTW_PAIR_MIN_CTAS) sdtw_fw
     const T INF = Num<T>::inf();
     // Zero the rings and boundary rows (stale shared memory must not feed NaN patterns to masked
     // cells); the row above strip 0 is +inf with R[-1][-1] = 0.
-    for (int e = threadIdx.x; e < W * (32 * kFwdStride + a.BL); e += blockDim.x) rings[e] = T(0);
-    for (int e = threadIdx.x; e < a.BL; e += blockDim.x) crow[e] = e == kBufPad - 1 ? T(0) : INF;
-    for (int e = threadIdx.x; e < W * a.G; e += blockDim.x) fbar_init(bars + 8 * e);
+    for (int e = threadIdx.x; e < W * (32 * RS + a.BL); e += blockDim.x) rings[e] = T(0);
+    for (int e = threadIdx.x; e < a.BL; e += blockDim.x) crow[e] = e == kBufPad ? T(0) : INF;  // column -1: 0
+    for (int e = threadIdx.x; e < W * a.G; e += blockDim.x)
+        asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bars + 8 * e), "r"(kPubLanes) : "memory");
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     // Padded rows 0 and N+1 of R (softdtw.cpp:114-121: +inf with R[b,0,0] = 0).
-    T* Rb = a.R + b * (a.N + 2) * (a.M + 2);
-    for (int64_t e = threadIdx.x; e < a.M + 2; e += blockDim.x) {
-        Rb[e] = e == 0 ? T(0) : INF;
-        Rb[(a.N + 1) * (a.M + 2) + e] = INF;
+    if (a.Rt == nullptr) {
+        T* Rb = a.R + b * (a.N + 2) * (a.M + 2);
+        for (int64_t e = threadIdx.x; e < a.M + 2; e += blockDim.x) {
+            Rb[e] = e == 0 ? T(0) : INF;
+            Rb[(a.N + 1) * (a.M + 2) + e] = INF;
+        }
     }
     __syncthreads();
-    T* ring = rings + static_cast<size_t>(warp) * 32 * kFwdStride;
+    T* ring = rings + static_cast<size_t>(warp) * 32 * RS;
     for (int s = warp; s < a.S; s += W) {
         const int wp = (s + W - 1) % W;
         const T* bin = s > 0 ? bufs + static_cast<size_t>(wp) * a.BL : crow;
@@ -362,18 +412,32 @@ __global__ void __launch_bounds__(SDTW_PAIR_THREADS, SDTW_PAIR_MIN_CTAS) sdtw_fw
             break;
     }
     cp_async_wait<0>();
+    if (a.Rt != nullptr) bulk_wait_all<0>();  // every tile written before the CTA ends
 }
 
 // ==================================================================================================
 // Backward (scatter form, see sdtw_wavefront.cu)
 // ==================================================================================================
+// Backward ring of a warp: 33 rows (ring row p = padded R row r0 + p = DP row r0 - 1 + p) x 2 slots of 32
+// positions, row p holding DP column c at position c + p (the forward's skew). At step tau, lane l (DP row
+// i = r0 + l, column c = tau - l) reads R[i-1][c-1] and R[i-1][c] at positions tau - 1 and tau of ring row l,
+// and R[i][c-1] at position tau of ring row l + 1, and writes E[i][c] in place of the last (R[i][c-1] is not
+// read again: the cells that need it, (i, c) itself and the row below, have already run). A group of 8 steps
+// therefore reads and writes aligned 16-byte vectors. Strides as in FwdRing (2 slots + pad).
+template <typename T>
+struct BwdRing {
+    static constexpr int S = sizeof(T) == 4 ? 68 : 66;
+};
+
 template <typename T>
 struct PairBwdArgs {
-    const T* R;
+    const T* R;   // padded R (B, N+2, M+2), or null when Rt is given
+    const T* Rt;  // R as the forward's strip tiles (B, S, NBt, 32, 32), or null
+    int NBt;
     T* E;
     Lengths len;
     int64_t B, N, M, bw;
-    int S, W, BL, P;
+    int S, W, BL, G;  // strips, warps, boundary row length, progress barriers per warp
     T k;
     Sync sy;
     int64_t inject;
@@ -383,74 +447,123 @@ struct PairBwdArgs {
 template <typename T>
 __device__ __forceinline__ void bwd_pair_load(const T* Rb, int64_t N, int64_t M, T* ring, int blk, int r0, int lane)
 {
+    constexpr int S = BwdRing<T>::S;
     const int64_t pitch = M + 2;
-    T* dst = ring + slot3(blk) * 32 + lane;
+    T* dst = ring + (blk & 1) * 32 + lane;
     const int c0 = 32 * blk + lane;  // column read by ring row 0; ring row p reads column c0 - p
     if (32 * blk - 31 >= 0 && 32 * blk + 32 <= M + 1 && r0 + 32 <= N + 1) {
         const T* src = Rb + static_cast<int64_t>(r0) * pitch + c0 + 1;
         const int64_t step = pitch - 1;
 #pragma unroll 11
         for (int p = 0; p < 33; ++p) {
-            cp_async_scalar<sizeof(T)>(dst + p * kBwdStride, src, static_cast<int>(sizeof(T)));
+            cp_async_scalar<sizeof(T)>(dst + p * S, src, static_cast<int>(sizeof(T)));
             src += step;
         }
     } else {
         for (int p = 0; p < 33; ++p) {
             const int pc = c0 - p + 1;  // padded column
             const bool in = r0 + p <= N + 1 && pc >= 0 && pc <= M + 1;
-            cp_async_scalar<sizeof(T)>(dst + p * kBwdStride,
-                                       in ? Rb + static_cast<int64_t>(r0 + p) * pitch + pc : Rb,
+            cp_async_scalar<sizeof(T)>(dst + p * S, in ? Rb + static_cast<int64_t>(r0 + p) * pitch + pc : Rb,
                                        in ? static_cast<int>(sizeof(T)) : 0);
         }
     }
 }
 
-// E of slot `blk` -> global (Erow = E row of DP row r0). Positions outside [lo_pos, hi_pos] were never
-// written by the sweep: their cells lie outside the band and get 0.
+// Per-warp bookkeeping of the two slot barriers of the tiled backward: loads issued into each slot, and the
+// parity of the latest one (the phase a reader of the slot waits for).
+struct SlotPhases {
+    uint32_t n[2];
+    uint32_t par[2];
+};
+
+// Slot of block `blk` <- R tiles written by the forward: ring rows 1..32 from tile (s, blk), ring row 0 from
+// row 31 of tile (s-1, blk+1) (the forward's skew puts both at the positions this ring expects). Tiles outside
+// the forward's swept blocks ([kf0, kf1] for strip s, [kp0, kp1] for strip s-1) were never written: their
+// cells are outside the band or the lengths, +inf, and are filled here instead (the row above strip 0 is R's
+// border row, +inf with R[-1][-1] = 0). The copies complete the slot's mbarrier `bar`.
 template <typename T>
-__device__ __forceinline__ void bwd_pair_store(T* Erow, int64_t M, const T* ring, int blk, int lo_pos, int hi_pos,
-                                               int nmat, int lane)
+__device__ __forceinline__ void bwd_tile_load(const PairBwdArgs<T>& a, T* ring, int blk, int64_t b, int s, int kf0,
+                                              int kf1, int kp0, int kp1, uint32_t bar, SlotPhases& ph, int lane)
 {
-    const T* src = ring + kBwdStride + slot3(blk) * 32 + lane;  // ring row p = r + 1 holds DP row r0 + r
-    const int pos = 32 * blk + lane;
-    const int c0 = pos - 1;  // column of row 0; row r: c0 - r
-    if (32 * blk - 32 >= 0 && 32 * blk + 30 < M && nmat == 32 && 32 * blk >= lo_pos && 32 * blk + 31 <= hi_pos) {
+    constexpr int RS = BwdRing<T>::S;
+    const T INF = Num<T>::inf();
+    T* slot = ring + (blk & 1) * 32;
+    const bool own = blk >= kf0 && blk <= kf1;
+    const bool above = s > 0 && blk + 1 >= kp0 && blk + 1 <= kp1;
+    const int p = blk & 1;
+    ph.par[p] = ph.n[p] & 1u;
+    ++ph.n[p];
+    fence_proxy_async_smem();  // this slot's earlier generic reads and writes come before the copies
+    __syncwarp();
+    if (lane == 0)
+        mbar_arrive_expect_tx(bar, static_cast<uint32_t>(((own ? 32 : 0) + (above ? 1 : 0)) * 32 * sizeof(T)));
+    __syncwarp();
+    T* row = slot + (lane + 1) * RS;
+    if (own) {
+        bulk_g2s(row, a.Rt + (((b * a.S + s) * static_cast<int64_t>(a.NBt) + blk) * 32 + lane) * 32,
+                 32 * sizeof(T), bar);
+    } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) row[i] = INF;
+    }
+    if (above) {
+        if (lane == 0)
+            bulk_g2s(slot, a.Rt + (((b * a.S + s - 1) * static_cast<int64_t>(a.NBt) + blk + 1) * 32 + 31) * 32,
+                     32 * sizeof(T), bar);
+    } else {
+        slot[lane] = (s == 0 && blk == -1 && lane == 31) ? T(0) : INF;
+    }
+}
+
+// Bounded wait for the latest load into the slot of block `blk` (tiled backward).
+__device__ __forceinline__ bool slot_wait(uint32_t bars_slot, int blk, const SlotPhases& ph, const Sync& sy, int lane)
+{
+    const int p = blk & 1;
+    const bool ok = fbar_wait_fast(bars_slot + 8 * p, ph.par[p], sy, lane);
+    __syncwarp();
+    return ok;
+}
+
+// E of slot `blk` -> global (Erow = E row of DP row r0): ring row r + 1 holds E[r0 + r][c] at position c + r.
+// Every position of the slot was written by the block's sweep (zeros where a step was outside the band).
+template <typename T>
+__device__ __forceinline__ void bwd_pair_store(T* Erow, int64_t M, const T* ring, int blk, int nmat, int lane)
+{
+    constexpr int S = BwdRing<T>::S;
+    const T* src = ring + S + (blk & 1) * 32 + lane;
+    const int c0 = 32 * blk + lane;  // column of row 0; row r: c0 - r
+    if (32 * blk - 31 >= 0 && 32 * blk + 31 < M && nmat == 32) {
         T* dst = Erow + c0;
         const int64_t step = M - 1;
 #pragma unroll 8
         for (int r = 0; r < 32; ++r) {
-            *dst = src[r * kBwdStride];
+            *dst = src[r * S];
             dst += step;
         }
     } else {
-        const bool written = pos >= lo_pos && pos <= hi_pos;
         for (int r = 0; r < nmat; ++r) {
             const int c = c0 - r;
-            if (c >= 0 && c < M) Erow[r * M + c] = written ? src[r * kBwdStride] : T(0);
+            if (c >= 0 && c < M) Erow[r * M + c] = src[r * S];
         }
     }
 }
 
-// Backward steps tau = tau0 + u for u = UHI down to ULO. `A` is this lane's ring row (the row above its
-// own) at the block's slot; position tau-1 of it is R[i-1][c-1], position tau of the next ring row is
-// R[i][c-1], and E[i][c] is written at position tau+1 of the next ring row. The first position of the
-// block (u = 0 reads tau-1 = 32*blk - 1) and the last (u = 31 writes 32*blk + 32) lie in neighbouring
-// slots: `edge_rd` / `edge_e` point there.
-template <typename T, bool MASKED, int UHI, int ULO>
-__device__ __forceinline__ void bwd_pair_steps(T* A, const T* edge_rd, T* edge_e, const T* bin, T* bout, int tau0,
-                                               int Av, int Zv, T k, T seed, int src_lane, bool lane31, T& upc,
-                                               T& sendv, T& pend, T& acc)
+// 8 backward steps tau = t8+7 .. t8 of one warp. A: ring row l at positions t8 .. t8+7, am1: position t8-1;
+// Bv: ring row l+1 at positions t8 .. t8+7 (R in, E out); bvv: lane 31's contributions from the strip below
+// (columns t8-31 .. t8-24); sv: the values lane 0 pushes into the row above (columns t8 .. t8+7).
+template <typename T, bool MASKED>
+__device__ __forceinline__ void bwd_pair_steps8(const T (&A)[8], T am1, T (&Bv)[8], const T (&bvv)[8], T (&sv)[8],
+                                                int t8, int Av, int Zv, T k, T seed, int src_lane, bool lane31,
+                                                T& sendv, T& pend, T& acc)
 {
     const T big = Num<T>::big();
-    T* A1 = A + kBwdStride;
 #pragma unroll
-    for (int u = UHI; u >= ULO; --u) {
-        const T rd = (u == 0) ? *edge_rd : A[u - 1];
-        const T rl = A1[u];
-        const T ru = upc;
+    for (int j = 7; j >= 0; --j) {
+        const T rd = j > 0 ? A[j > 0 ? j - 1 : 0] : am1;  // R[i-1][c-1]
+        const T ru = A[j];                                // R[i-1][c]
+        const T rl = Bv[j];                               // R[i][c-1]
         const T recvw = __shfl_sync(kFull, sendv, src_lane);
-        const T bv = bin[u];
-        const T recv = lane31 ? bv : recvw;
+        const T recv = lane31 ? bvv[j] : recvw;
         const T Es = acc + recv;
         const T m = Num<T>::mn(Num<T>::mn(rd, ru), rl);
         const T mc = Num<T>::mn(m, big);
@@ -460,7 +573,7 @@ __device__ __forceinline__ void bwd_pair_steps(T* A, const T* edge_rd, T* edge_e
         T q = Es * Num<T>::rcp_((ed + eu) + el);
         T Eo = Es;
         if (MASKED) {
-            const int tau = tau0 + u;
+            const int tau = t8 + j;
             const bool valid = tau >= Av && tau <= Zv;
             q = valid ? q : T(0);
             acc = valid ? q * el : seed;
@@ -470,48 +583,72 @@ __device__ __forceinline__ void bwd_pair_steps(T* A, const T* edge_rd, T* edge_e
         }
         sendv = fma(q, eu, pend);
         pend = q * ed;
-        if (u == 31)
-            *edge_e = Eo;
-        else
-            A1[u + 1] = Eo;
-        bout[u] = sendv;  // lane 0: the boundary row; other lanes: a scratch area
-        upc = rd;
+        Bv[j] = Eo;
+        sv[j] = sendv;
     }
 }
 
+// The 32 steps of block tau0 / 32 as four groups of 8, top group first. Before group g (steps 8g .. 8g+7)
+// the strip below must have completed its group g - 4: lane 31 reads the contributions into columns
+// 8g - 31 .. 8g - 24, pushed by the strip below at its steps 8g - 31 .. 8g - 24 (groups g - 4 and g - 3; the
+// strip below sweeps downwards, so g - 3 completes first). `bcar` carries the contribution at column
+// 8g - 24, loaded with the group above. Returns false if the launch aborted.
 template <typename T, bool MASKED>
-__device__ __forceinline__ void bwd_pair_block(T* A, const T* edge_rd, T* edge_e, const T* bin, T* bout, int tau0,
-                                               const Strip& st, T k, T seed, int src_lane, bool lane31, T& upc,
-                                               T& sendv, T& pend, T& acc, int q)
+__device__ __forceinline__ bool bwd_pair_block(T* ring, const T* bin, T* bout, int tau0, const Strip& st, T k, T seed,
+                                               bool wait_in, uint32_t bars_in, uint32_t par_in, bool publish,
+                                               uint32_t bars_out, bool slot_below_pending, bool tiles,
+                                               uint32_t bars_slot, const SlotPhases& ph, const Sync& sy,
+                                               int src_lane, int lane, T& sendv, T& pend, T& acc, T& bcar)
 {
-    // q selects the 8-step group; the block's first and last steps are run by the caller.
-    switch (q) {
-        case 3:
-            bwd_pair_steps<T, MASKED, 30, 24>(A, edge_rd, edge_e, bin, bout, tau0, st.A, st.Z, k, seed,
-                                              src_lane, lane31, upc, sendv, pend, acc);
-            break;
-        case 2:
-            bwd_pair_steps<T, MASKED, 23, 16>(A, edge_rd, edge_e, bin, bout, tau0, st.A, st.Z, k, seed,
-                                              src_lane, lane31, upc, sendv, pend, acc);
-            break;
-        case 1:
-            bwd_pair_steps<T, MASKED, 15, 8>(A, edge_rd, edge_e, bin, bout, tau0, st.A, st.Z, k, seed,
-                                             src_lane, lane31, upc, sendv, pend, acc);
-            break;
-        default:
-            bwd_pair_steps<T, MASKED, 7, 1>(A, edge_rd, edge_e, bin, bout, tau0, st.A, st.Z, k, seed,
-                                            src_lane, lane31, upc, sendv, pend, acc);
-            break;
+    constexpr int RS = BwdRing<T>::S;
+    const bool lane31 = lane == 31;
+    T* rowA = ring + lane * RS + (tau0 & 32);  // ring row l, positions tau0 .. (slot of this block)
+    T* rowB = rowA + RS;                       // ring row l + 1
+    const int g0 = tau0 / 8;
+#pragma unroll
+    for (int q = 3; q >= 0; --q) {
+        const int t8 = tau0 + 8 * q;
+        if (wait_in && !fbar_wait_fast(bars_in + 8 * max(g0 + q - 4, 0), par_in, sy, lane)) return false;
+        if (q == 0 && slot_below_pending) {  // position tau0 - 1 lies in the slot of the block below
+            if (tiles) {
+                if (!slot_wait(bars_slot, tau0 / 32 - 1, ph, sy, lane)) return false;
+            } else {
+                cp_async_wait<0>();
+                __syncwarp();
+            }
+        }
+        T A[8], Bv[8], bvv[8], sv[8];
+        lds8(A, rowA + 8 * q);
+        // Position t8 - 1 of ring row l: the slot of the block below for the group q = 0.
+        const T am1 = q > 0 ? rowA[8 * q - 1] : ring[lane * RS + ((tau0 - 1) & 63)];
+        lds8(Bv, rowB + 8 * q);
+        {
+            T v[8];
+            lds8(v, bin + t8 - 32 + kBufPad);
+#pragma unroll
+            for (int j = 0; j < 7; ++j) bvv[j] = v[j + 1];
+            bvv[7] = bcar;
+            bcar = v[0];
+        }
+        bwd_pair_steps8<T, MASKED>(A, am1, Bv, bvv, sv, t8, st.A, st.Z, k, seed, src_lane, lane31, sendv, pend, acc);
+        __syncwarp();  // every lane has read ring row l+1 [t8, t8+8) (its A) before lane l overwrites it
+        sts8(rowB + 8 * q, Bv);
+        if (publish) {
+            if (lane == 0) sts8(bout + t8 + kBufPad, sv);
+            fbar_arrive_n_if(bars_out + 8 * (g0 + q), 1, lane == 0);
+        }
     }
+    return true;
 }
 
 // One strip of the backward; `t` is its position in sweep order (strip S-1-t). Returns false if the
 // launch aborted.
-template <typename T>
-__device__ bool bwd_pair_strip(const PairBwdArgs<T>& a, T* ring, const T* bin, const int* pin, const T* zrow,
-                               T* bout, int* pout, T* scratch, int64_t b, int s, int t, int lane)
+template <typename T, int MC>
+__device__ bool bwd_pair_strip(const PairBwdArgs<T>& a, T* ring, const T* bin, uint32_t bars_in, uint32_t par_in,
+                               const T* zrow, T* bout, uint32_t bars_out, uint32_t bars_slot, SlotPhases& ph,
+                               int64_t b, int s, int lane)
 {
-    const int64_t N = a.N, M = a.M;
+    const int64_t N = a.N, M = MC > 0 ? MC : a.M;
     const int r0 = 32 * s;
     const int nmat = static_cast<int>(N - r0 < 32 ? N - r0 : 32);
     T* Erow = a.E + (b * N + r0) * M;
@@ -520,6 +657,11 @@ __device__ bool bwd_pair_strip(const PairBwdArgs<T>& a, T* ring, const T* bin, c
         if (st.bad && s == 0 && lane == 0) atomicOr(a.sy.err, kErrBadLength);
         for (int r = 0; r < nmat; ++r)
             for (int c = lane; c < M; c += 32) Erow[r * M + c] = T(0);
+        // Empty strips (rows past the pair's length) come first in the bottom-up order, and their warps sweep
+        // non-empty strips in later rounds: complete every barrier once here too, so that a warp's barrier
+        // phases keep counting its rounds (nothing waits on these arrivals: the strip above an empty strip
+        // has no producer).
+        for (int g = lane; g < a.G; g += 32) fbar_arrive_n_if(bars_out + 8 * g, 1, true);
         return true;
     }
     const int k0 = st.c_begin >> 5;
@@ -527,130 +669,146 @@ __device__ bool bwd_pair_strip(const PairBwdArgs<T>& a, T* ring, const T* bin, c
     const int kmin = (32 * k0 - 1) >> 5;  // arithmetic shift: -1 when k0 == 0
     const bool has_producer = r0 + 32 < st.nx;
     const bool skip = b * a.S + s == a.inject;
-    const bool has_consumer = s > 0 && !skip;
+    const bool publish = s > 0 && !skip;
     if (!has_producer) bin = zrow;
     const T seed = (r0 + lane == st.nx - 1) ? T(1) : T(0);
-    const T* Rb = a.R + b * (N + 2) * (M + 2);
+    const bool tiles = a.Rt != nullptr;
+    const T* Rb = tiles ? nullptr : a.R + b * (N + 2) * (M + 2);
+    // Blocks of the forward's tiles of this strip and of the strip above (the forward's skew is one step later).
+    const int kf0 = (st.c_begin + 1) >> 5, kf1 = (st.c_end + 32) >> 5;
+    int kp0 = 0, kp1 = -1;
+    if (tiles && s > 0) {
+        int64_t lo, hi, lo2, hi2;
+        band_row_range(r0 - 32, st.nx, st.ny, a.bw, lo, hi);
+        band_row_range(r0 - 1, st.nx, st.ny, a.bw, lo2, hi2);
+        kp0 = static_cast<int>((lo + 1) >> 5);
+        kp1 = static_cast<int>((hi2 + 32) >> 5);
+    }
 
-    cp_async_wait<0>();
-    __syncwarp();
-    bwd_pair_load<T>(Rb, N, M, ring, k1, r0, lane);
-    cp_async_commit();
-    if (k1 - 1 >= kmin) bwd_pair_load<T>(Rb, N, M, ring, k1 - 1, r0, lane);
-    cp_async_commit();
+    if (tiles) {
+        bwd_tile_load<T>(a, ring, k1, b, s, kf0, kf1, kp0, kp1, bars_slot + 8 * (k1 & 1), ph, lane);
+        if (k1 - 1 >= kmin)
+            bwd_tile_load<T>(a, ring, k1 - 1, b, s, kf0, kf1, kp0, kp1, bars_slot + 8 * ((k1 - 1) & 1), ph, lane);
+    } else {
+        cp_async_wait<0>();
+        __syncwarp();
+        bwd_pair_load<T>(Rb, N, M, ring, k1, r0, lane);
+        cp_async_commit();
+        if (k1 - 1 >= kmin) bwd_pair_load<T>(Rb, N, M, ring, k1 - 1, r0, lane);
+        cp_async_commit();
+    }
 
-    // Columns of each row outside the stored range [32*k0 - r - 1, 32*k1 + 62 - r]: zero.
+    // Columns of each row outside the stored range [32*k0 - r, 32*k1 + 31 - r]: zero.
     for (int r = 0; r < nmat; ++r) {
         T* row = Erow + r * M;
-        int pe = 32 * k0 - r - 1;
+        int pe = 32 * k0 - r;
         pe = pe < 0 ? 0 : (pe > M ? static_cast<int>(M) : pe);
-        int ss = 32 * k1 + 63 - r;
+        int ss = 32 * k1 + 32 - r;
         ss = ss > M ? static_cast<int>(M) : ss;
         for (int c = lane; c < pe; c += 32) row[c] = T(0);
         for (int c = ss + lane; c < M; c += 32) row[c] = T(0);
     }
 
-    const int P = a.P;
-    const int H = static_cast<int>(M) + 63;
-    const int key_in = (t - 1) * P + H;  // the strip below has pushed into every column >= c: key_in - c
-    const int key_out = t * P + H;
-    const int lo_pos = 32 * k0 + 1;
-    const int hi_pos = 32 * k1 + 32;
-    int seen = INT_MIN;
-    T upc = T(0), sendv = T(0), pend = T(0), acc = seed;
+    T sendv = T(0), pend = T(0), acc = seed;
+    // The carry of the top group g = 4*k1 + 3 (lane 31's contribution at column 8g - 24 = 32*k1) comes from the
+    // strip below's group 4*k1, complete once the group's own wait (on group g - 4) returns.
+    T bcar = T(0);
+    bool first = true;
     const int src_lane = (lane + 1) & 31;
-    const bool lane31 = lane == 31;
-    const bool put_out = has_consumer && lane == 0;
 
 #pragma unroll 1
     for (int blk = k1; blk >= k0; --blk) {
-        cp_async_wait<1>();
-        __syncwarp();
+        if (tiles) {
+            if (!slot_wait(bars_slot, blk, ph, a.sy, lane)) return false;
+        } else {
+            cp_async_wait<1>();
+            __syncwarp();
+        }
         const int tau0 = 32 * blk;
-        T* A = ring + lane * kBwdStride + slot3(blk) * 32;
-        if (blk == k1) upc = A[31];  // R[i-1][c] of the first step
-        const T* edge_rd = ring + lane * kBwdStride + slot3(blk - 1) * 32 + 31;
-        T* edge_e = ring + (lane + 1) * kBwdStride + slot3(blk + 1) * 32;
-        const T* bi = bin + tau0 - 31 + kBufPad;
-        T* bo = put_out ? bout + tau0 + kBufPad : scratch;
-        const bool full = tau0 >= st.Amax && tau0 + 31 <= st.Zmin;
-#pragma unroll 1
-        for (int q = 3; q >= 0; --q) {
-            const int t8 = tau0 + 8 * q;
-            if (has_producer && !wait_key(pin, key_in - (t8 - 31), seen, a.sy, lane)) return false;
-            if (q == 3) {
-                if (full)
-                    bwd_pair_steps<T, false, 31, 31>(A, edge_rd, edge_e, bi, bo, tau0, st.A, st.Z, a.k, seed,
-                                                     src_lane, lane31, upc, sendv, pend, acc);
-                else
-                    bwd_pair_steps<T, true, 31, 31>(A, edge_rd, edge_e, bi, bo, tau0, st.A, st.Z, a.k, seed,
-                                                    src_lane, lane31, upc, sendv, pend, acc);
-                // Slot blk+1 is now final: write its E back and refill it with slot blk-2.
-                __syncwarp();
-                bwd_pair_store<T>(Erow, M, ring, blk + 1, lo_pos, hi_pos, nmat, lane);
-                __syncwarp();
-                if (blk - 2 >= kmin) bwd_pair_load<T>(Rb, N, M, ring, blk - 2, r0, lane);
-                cp_async_commit();
-            }
-            if (full)
-                bwd_pair_block<T, false>(A, edge_rd, edge_e, bi, bo, tau0, st, a.k, seed, src_lane,
-                                         lane31, upc, sendv, pend, acc, q);
-            else
-                bwd_pair_block<T, true>(A, edge_rd, edge_e, bi, bo, tau0, st, a.k, seed, src_lane,
-                                        lane31, upc, sendv, pend, acc, q);
-            if (q == 0) {
-                cp_async_wait<1>();  // slot blk-1 (read by the last step)
-                __syncwarp();
-                if (full)
-                    bwd_pair_steps<T, false, 0, 0>(A, edge_rd, edge_e, bi, bo, tau0, st.A, st.Z, a.k, seed,
-                                                   src_lane, lane31, upc, sendv, pend, acc);
-                else
-                    bwd_pair_steps<T, true, 0, 0>(A, edge_rd, edge_e, bi, bo, tau0, st.A, st.Z, a.k, seed,
-                                                  src_lane, lane31, upc, sendv, pend, acc);
-            }
-            st_release_cta_if(pout, key_out - t8, put_out);
+        if (first) {
+            if (has_producer && !fbar_wait_fast(bars_in + 8 * max(4 * k1 + 3 - 4, 0), par_in, a.sy, lane))
+                return false;
+            bcar = bin[32 * k1 + kBufPad];
+            first = false;
+        }
+        const bool below = blk - 1 >= kmin;
+        const bool ok = (tau0 >= st.Amax && tau0 + 31 <= st.Zmin)
+                            ? bwd_pair_block<T, false>(ring, bin, bout, tau0, st, a.k, seed, has_producer, bars_in,
+                                                       par_in, publish, bars_out, below, tiles, bars_slot, ph, a.sy,
+                                                       src_lane, lane, sendv, pend, acc, bcar)
+                            : bwd_pair_block<T, true>(ring, bin, bout, tau0, st, a.k, seed, has_producer, bars_in,
+                                                      par_in, publish, bars_out, below, tiles, bars_slot, ph, a.sy,
+                                                      src_lane, lane, sendv, pend, acc, bcar);
+        if (!ok) return false;
+        __syncwarp();
+        bwd_pair_store<T>(Erow, M, ring, blk, nmat, lane);
+        __syncwarp();
+        if (tiles) {
+            if (blk - 2 >= kmin)
+                bwd_tile_load<T>(a, ring, blk - 2, b, s, kf0, kf1, kp0, kp1, bars_slot + 8 * (blk & 1), ph, lane);
+        } else {
+            if (blk - 2 >= kmin) bwd_pair_load<T>(Rb, N, M, ring, blk - 2, r0, lane);
+            cp_async_commit();
         }
     }
-    cp_async_wait<0>();
+    if (!tiles) cp_async_wait<0>();
     __syncwarp();
-    bwd_pair_store<T>(Erow, M, ring, k0, lo_pos, hi_pos, nmat, lane);
-    if (has_consumer) {
-        // Lane 0's last diagonal push (into column 32*k0 - 1) and zeros below the sweep.
+    if (publish) {
+        // Lane 0's last diagonal push (into column 32*k0 - 1) and zeros below the sweep; then complete the
+        // barriers of the groups below the sweep (every barrier once per strip).
         if (lane == 0) bout[32 * k0 - 1 + kBufPad] = pend;
         for (int c = -kBufPad + lane; c <= 32 * k0 - 2; c += 32) bout[c + kBufPad] = T(0);
-        __threadfence_block();
         __syncwarp();
-        st_release_cta_if(pout, t * P + P - 1, lane == 0);
+        for (int g = lane; g < 4 * k0; g += 32) fbar_arrive_n_if(bars_out + 8 * g, 1, true);
     }
     __syncwarp();
     return true;
 }
 
-template <typename T>
+template <typename T, int MC>
 __global__ void __launch_bounds__(SDTW_PAIR_THREADS, SDTW_PAIR_MIN_CTAS) sdtw_bwd_pair_kernel(PairBwdArgs<T> a)
 {
     extern __shared__ __align__(16) unsigned char smem[];
+    constexpr int RS = BwdRing<T>::S;
     const int lane = threadIdx.x & 31;
     const int warp = threadIdx.x >> 5;
     const int W = a.W;
     T* rings = reinterpret_cast<T*>(smem);
-    T* bufs = rings + static_cast<size_t>(W) * 33 * kBwdStride;
+    T* bufs = rings + static_cast<size_t>(W) * 33 * RS;
     T* zrow = bufs + static_cast<size_t>(W) * a.BL;
-    T* scratch = zrow + a.BL;  // 32 elements per warp
-    int* prog = reinterpret_cast<int*>(scratch + static_cast<size_t>(W) * 32);
+    const uint32_t bars = (smem_addr(zrow + a.BL) + 7u) & ~7u;  // [W][G] progress mbarriers, then [W][2] slot ones
+    const uint32_t slot_bars = bars + 8 * W * a.G;
     const int64_t b = blockIdx.x;
-    for (int e = threadIdx.x; e < W * (33 * kBwdStride + a.BL) + a.BL; e += blockDim.x) rings[e] = T(0);
-    if (threadIdx.x < W) prog[threadIdx.x] = -1;
+    for (int e = threadIdx.x; e < W * (33 * RS + a.BL) + a.BL; e += blockDim.x) rings[e] = T(0);
+    for (int e = threadIdx.x; e < W * (a.G + 2); e += blockDim.x)
+        asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bars + 8 * e), "r"(1) : "memory");
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     __syncthreads();
-    T* ring = rings + static_cast<size_t>(warp) * 33 * kBwdStride;
+    T* ring = rings + static_cast<size_t>(warp) * 33 * RS;
+    SlotPhases ph = {{0u, 0u}, {0u, 0u}};
+    bool ok = true;
     for (int t = warp; t < a.S; t += W) {
         const int wp = (t + W - 1) % W;
-        if (!bwd_pair_strip<T>(a, ring, bufs + static_cast<size_t>(wp) * a.BL, prog + wp, zrow,
-                               bufs + static_cast<size_t>(warp) * a.BL, prog + warp,
-                               scratch + static_cast<size_t>(warp) * 32, b, a.S - 1 - t, t, lane))
+        const uint32_t par_in = static_cast<uint32_t>(((t - 1) / W) & 1);  // round of the strip below in its warp
+        if (!bwd_pair_strip<T, MC>(a, ring, bufs + static_cast<size_t>(wp) * a.BL, bars + 8 * wp * a.G, par_in, zrow,
+                                   bufs + static_cast<size_t>(warp) * a.BL, bars + 8 * warp * a.G,
+                                   slot_bars + 16 * warp, ph, b, a.S - 1 - t, lane)) {
+            ok = false;
             break;
+        }
     }
     cp_async_wait<0>();
+    if (a.Rt != nullptr && !ok) {
+        // A strip that stopped early (the launch aborted) may have bulk loads in flight into this warp's ring:
+        // they land before the CTA ends (each wait bounded by the library's wait limit, ignoring the abort).
+        for (int p = 0; p < 2; ++p) {
+            if (ph.n[p] == 0) continue;
+            const uint32_t bar = slot_bars + 16 * warp + 8 * p;
+            const uint64_t t0 = global_ns();
+            while (!__all_sync(kFull, fbar_try_wait(bar, ph.par[p])) && global_ns() - t0 <= a.sy.timeout_ns) {
+            }
+        }
+    }
 }
 
 // ==================================================================================================
@@ -659,14 +817,14 @@ __global__ void __launch_bounds__(SDTW_PAIR_THREADS, SDTW_PAIR_MIN_CTAS) sdtw_bw
 template <typename T>
 size_t pair_fwd_smem_bytes(int W, int64_t M)
 {
-    return (static_cast<size_t>(W) * (32 * kFwdStride + 32) + static_cast<size_t>(W + 1) * buf_len(M)) * sizeof(T) +
+    return (static_cast<size_t>(W) * (32 * FwdRing<T>::S + 32) + static_cast<size_t>(W + 1) * buf_len(M)) * sizeof(T) +
            8 + static_cast<size_t>(W) * fwd_groups(M) * 8;
 }
 template <typename T>
 size_t pair_bwd_smem_bytes(int W, int64_t M)
 {
-    return (static_cast<size_t>(W) * (33 * kBwdStride + 32) + static_cast<size_t>(W + 1) * buf_len(M)) * sizeof(T) +
-           static_cast<size_t>(W) * sizeof(int);
+    return (static_cast<size_t>(W) * 33 * BwdRing<T>::S + static_cast<size_t>(W + 1) * buf_len(M)) * sizeof(T) + 8 +
+           static_cast<size_t>(W) * (fwd_groups(M) + 2) * 8;
 }
 
 template <typename T>
@@ -676,7 +834,10 @@ cudaError_t pair_init_attrs(int max_smem)
     if (e != cudaSuccess) return e;
     e = cudaFuncSetAttribute(sdtw_fwd_pair_kernel<T, kPairSpecialM>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
     if (e != cudaSuccess) return e;
-    return cudaFuncSetAttribute(sdtw_bwd_pair_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
+    e = cudaFuncSetAttribute(sdtw_bwd_pair_kernel<T, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
+    if (e != cudaSuccess) return e;
+    return cudaFuncSetAttribute(sdtw_bwd_pair_kernel<T, kPairSpecialM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                max_smem);
 }
 template cudaError_t pair_init_attrs<float>(int);
 template cudaError_t pair_init_attrs<double>(int);
@@ -684,10 +845,14 @@ template cudaError_t pair_init_attrs<double>(int);
 template <typename T>
 cudaError_t pair_regs(bool backward, int& regs)
 {
-    cudaFuncAttributes fa;
-    const cudaError_t e = backward ? cudaFuncGetAttributes(&fa, sdtw_bwd_pair_kernel<T>)
-                                   : cudaFuncGetAttributes(&fa, sdtw_fwd_pair_kernel<T, 0>);
-    regs = e == cudaSuccess ? fa.numRegs : 0;
+    // The largest count over the kernel's instantiations (the one specialized on M can need more).
+    cudaFuncAttributes fa, fb;
+    cudaError_t e = backward ? cudaFuncGetAttributes(&fa, sdtw_bwd_pair_kernel<T, 0>)
+                             : cudaFuncGetAttributes(&fa, sdtw_fwd_pair_kernel<T, 0>);
+    if (e == cudaSuccess)
+        e = backward ? cudaFuncGetAttributes(&fb, sdtw_bwd_pair_kernel<T, kPairSpecialM>)
+                     : cudaFuncGetAttributes(&fb, sdtw_fwd_pair_kernel<T, kPairSpecialM>);
+    regs = e == cudaSuccess ? (fa.numRegs > fb.numRegs ? fa.numRegs : fb.numRegs) : 0;
     return e;
 }
 template cudaError_t pair_regs<float>(bool, int&);
@@ -702,7 +867,12 @@ int pair_warps(bool backward, int64_t N, int64_t M, int cap, size_t budget)
     if (W > kPairMaxWarps) W = kPairMaxWarps;
     while (W >= 1) {
         const size_t bytes = backward ? pair_bwd_smem_bytes<T>(W, M) : pair_fwd_smem_bytes<T>(W, M);
-        if (bytes <= budget) return W;
+        if (bytes <= budget) {
+            // As few warps as give the same number of rounds over the strips (16 strips on 9 warps take 2 rounds
+            // like 8 warps, with an idle warp in the second): fewer registers and less shared memory per CTA.
+            const int64_t rounds = (S + W - 1) / W;
+            return static_cast<int>((S + rounds - 1) / rounds);
+        }
         --W;
     }
     return 0;
@@ -717,12 +887,15 @@ bool pair_keys_fit(int64_t N, int64_t M)
 }
 
 template <typename T>
-cudaError_t pair_forward(const T* D, T* R, T* costs, const void* lx, const void* ly, int is32, int64_t B, int64_t N,
-                         int64_t M, int64_t bw, double gamma, int W, Sync sy, int64_t inject, cudaStream_t stream)
+cudaError_t pair_forward(const T* D, T* R, T* Rt, T* costs, const void* lx, const void* ly, int is32, int64_t B,
+                         int64_t N, int64_t M, int64_t bw, double gamma, int W, Sync sy, int64_t inject,
+                         cudaStream_t stream)
 {
     PairFwdArgs<T> a;
     a.D = D;
     a.R = R;
+    a.Rt = Rt;
+    a.NBt = pair_tile_blocks(M);
     a.costs = costs;
     a.len = Lengths{lx, ly, is32};
     a.B = B;
@@ -744,17 +917,21 @@ cudaError_t pair_forward(const T* D, T* R, T* costs, const void* lx, const void*
         sdtw_fwd_pair_kernel<T, 0><<<static_cast<unsigned>(B), W * 32, pair_fwd_smem_bytes<T>(W, M), stream>>>(a);
     return cudaGetLastError();
 }
-template cudaError_t pair_forward<float>(const float*, float*, float*, const void*, const void*, int, int64_t, int64_t,
-                                         int64_t, int64_t, double, int, Sync, int64_t, cudaStream_t);
-template cudaError_t pair_forward<double>(const double*, double*, double*, const void*, const void*, int, int64_t,
-                                          int64_t, int64_t, int64_t, double, int, Sync, int64_t, cudaStream_t);
+template cudaError_t pair_forward<float>(const float*, float*, float*, float*, const void*, const void*, int, int64_t,
+                                         int64_t, int64_t, int64_t, double, int, Sync, int64_t, cudaStream_t);
+template cudaError_t pair_forward<double>(const double*, double*, double*, double*, const void*, const void*, int,
+                                          int64_t, int64_t, int64_t, int64_t, double, int, Sync, int64_t,
+                                          cudaStream_t);
 
 template <typename T>
-cudaError_t pair_backward(const T* R, T* E, const void* lx, const void* ly, int is32, int64_t B, int64_t N, int64_t M,
-                          int64_t bw, double gamma, int W, Sync sy, int64_t inject, cudaStream_t stream)
+cudaError_t pair_backward(const T* R, const T* Rt, T* E, const void* lx, const void* ly, int is32, int64_t B,
+                          int64_t N, int64_t M, int64_t bw, double gamma, int W, Sync sy, int64_t inject,
+                          cudaStream_t stream)
 {
     PairBwdArgs<T> a;
     a.R = R;
+    a.Rt = Rt;
+    a.NBt = pair_tile_blocks(M);
     a.E = E;
     a.len = Lengths{lx, ly, is32};
     a.B = B;
@@ -764,17 +941,21 @@ cudaError_t pair_backward(const T* R, T* E, const void* lx, const void* ly, int 
     a.S = static_cast<int>(N > 0 ? (N + 31) / 32 : 1);
     a.W = W;
     a.BL = buf_len(M);
-    a.P = static_cast<int>(M + 128);
+    a.G = fwd_groups(M);
     a.k = static_cast<T>(1.4426950408889634 / gamma);
     a.sy = sy;
     a.inject = inject;
     count_launch();
-    sdtw_bwd_pair_kernel<T><<<static_cast<unsigned>(B), W * 32, pair_bwd_smem_bytes<T>(W, M), stream>>>(a);
+    if (M == kPairSpecialM)
+        sdtw_bwd_pair_kernel<T, kPairSpecialM><<<static_cast<unsigned>(B), W * 32, pair_bwd_smem_bytes<T>(W, M), stream>>>(a);
+    else
+        sdtw_bwd_pair_kernel<T, 0><<<static_cast<unsigned>(B), W * 32, pair_bwd_smem_bytes<T>(W, M), stream>>>(a);
     return cudaGetLastError();
 }
-template cudaError_t pair_backward<float>(const float*, float*, const void*, const void*, int, int64_t, int64_t,
-                                          int64_t, int64_t, double, int, Sync, int64_t, cudaStream_t);
-template cudaError_t pair_backward<double>(const double*, double*, const void*, const void*, int, int64_t, int64_t,
-                                           int64_t, int64_t, double, int, Sync, int64_t, cudaStream_t);
+template cudaError_t pair_backward<float>(const float*, const float*, float*, const void*, const void*, int, int64_t,
+                                          int64_t, int64_t, int64_t, double, int, Sync, int64_t, cudaStream_t);
+template cudaError_t pair_backward<double>(const double*, const double*, double*, const void*, const void*, int,
+                                           int64_t, int64_t, int64_t, int64_t, double, int, Sync, int64_t,
+                                           cudaStream_t);
 
 }  // namespace sdtw

@@ -20,8 +20,6 @@ namespace sdtw {
 #define SDTW_PAIR_MIN_CTAS 1
 #endif
 constexpr int kPairMaxWarps = SDTW_PAIR_THREADS / 32;  // warps per CTA at most
-constexpr int kFwdStride = 65;     // forward ring row: 2 slots of 32 positions + 1 (odd: conflict-free)
-constexpr int kBwdStride = 97;     // backward ring row: 3 slots + 1
 constexpr int kBufPad = 64;        // boundary rows are indexed by column + kBufPad
 // Row length M for which the wavefront kernels are also compiled with M as a compile-time constant
 // (immediate row offsets in the ring loads and stores); other lengths run the generic instantiation.
@@ -48,11 +46,20 @@ int pair_warps(bool backward, int64_t N, int64_t M, int cap, size_t budget);
 // Progress keys stay below 2^30 for these sizes.
 bool pair_keys_fit(int64_t N, int64_t M);
 
+// R as strip tiles (the module path's layout between the pair-resident forward and backward): tile (b, s, k)
+// is 32 x 32 elements, row l holding R[32 s + l][32 k + x - l - 1] at x = 0..31 (+inf outside the band and the
+// lengths); tiles of blocks a strip does not sweep are never written. Blocks per strip: pair_tile_blocks(M).
+inline int pair_tile_blocks(int64_t M) { return static_cast<int>((M + 31) / 32) + 1; }
+
+// Forward: writes the padded R (B, N+2, M+2) when Rt is null, else the tiles Rt (R unused).
 template <typename T>
-cudaError_t pair_forward(const T* D, T* R, T* costs, const void* lx, const void* ly, int is32, int64_t B, int64_t N,
-                         int64_t M, int64_t bw, double gamma, int W, Sync sy, int64_t inject, cudaStream_t stream);
+cudaError_t pair_forward(const T* D, T* R, T* Rt, T* costs, const void* lx, const void* ly, int is32, int64_t B,
+                         int64_t N, int64_t M, int64_t bw, double gamma, int W, Sync sy, int64_t inject,
+                         cudaStream_t stream);
+// Backward: reads the padded R when Rt is null, else the tiles Rt written by pair_forward (R unused).
 template <typename T>
-cudaError_t pair_backward(const T* R, T* E, const void* lx, const void* ly, int is32, int64_t B, int64_t N, int64_t M,
-                          int64_t bw, double gamma, int W, Sync sy, int64_t inject, cudaStream_t stream);
+cudaError_t pair_backward(const T* R, const T* Rt, T* E, const void* lx, const void* ly, int is32, int64_t B,
+                          int64_t N, int64_t M, int64_t bw, double gamma, int W, Sync sy, int64_t inject,
+                          cudaStream_t stream);
 
 }  // namespace sdtw

@@ -643,9 +643,9 @@ int choose_pair_warps(const DeviceInfo& di, bool backward, int64_t B, int64_t N,
     if (g_force_path == 1) return 0;
     // Measured on B200, fp32, forward op (pair-resident / strip-ticket): 256 x 512 x 512 0.230 / 0.313 ms,
     // 512 x 256 x 256 0.148 / 0.172, 512 x 192 x 192 0.109 / 0.118, 1024 x 160 x 160 0.150 / 0.137,
-    // 65536 x 64 x 64 2.08 / 1.30. The backward is faster on the strip-ticket kernel at every shape
-    // (0.280 / 0.365 at 256 x 512 x 512). So only the forward switches, for pairs of at least 6 strips.
-    if (g_force_path != 2 && (B < di.sms || backward || strips_of(N) < 6)) return 0;
+    // 65536 x 64 x 64 2.08 / 1.30; backward op at 256 x 512 x 512: 0.243 / 0.272 ms. Both directions switch
+    // together (the module path then hands R over as tiles), for pairs of at least 6 strips.
+    if (g_force_path != 2 && (B < di.sms || strips_of(N) < 6)) return 0;
     if (B > 0x7fffffff || !pair_keys_fit(N, M)) return 0;
     // Enough CTAs per SM for the whole batch to be resident at once (up to 8), each as wide as its
     // share of the SM's shared memory and registers allows.
@@ -683,10 +683,20 @@ size_t forward_ws_needed(const DeviceInfo& di, int64_t B, int64_t N, int64_t M)
     return kHeader + bnd_bytes(B, N, M, sizeof(T));
 }
 
+// True when both directions run on the pair-resident kernels for this shape (the module path then keeps R
+// as the forward's strip tiles).
+template <typename T>
+bool uses_tiles(const DeviceInfo& di, int64_t B, int64_t N, int64_t M)
+{
+    if (use_warp_kernels<T>(di, B, N, M)) return false;
+    return choose_pair_warps<T>(di, false, B, N, M) > 0 && choose_pair_warps<T>(di, true, B, N, M) > 0;
+}
+
+// Rt non-null: the forward writes R as strip tiles (only when uses_tiles; R unused), else the padded R.
 template <typename T>
 sdtw_status launch_forward(const void* D, int64_t B, int64_t N, int64_t M, const void* lx, const void* ly, int is32,
                            double gamma, int64_t bw, void* R, void* costs, void* ws, uint32_t* err,
-                           cudaStream_t stream)
+                           cudaStream_t stream, void* Rt = nullptr)
 {
     const DeviceInfo* di = nullptr;
     cudaError_t e = device_info(di);
@@ -695,6 +705,7 @@ sdtw_status launch_forward(const void* D, int64_t B, int64_t N, int64_t M, const
     // a wait timeout) then reads as NaN even when nobody checks the error word.
     e = cudaMemsetAsync(costs, 0xff, static_cast<size_t>(B) * sizeof(T), stream);
     if (e != cudaSuccess) return from_cuda(e);
+    if (Rt != nullptr && !uses_tiles<T>(*di, B, N, M)) return SDTW_EINVAL;
     if (use_warp_kernels<T>(*di, B, N, M))
         return from_cuda(warp_forward<T>(static_cast<const T*>(D), static_cast<T*>(R), static_cast<T*>(costs), lx, ly,
                                          is32, B, N, M, clamp_bw(bw, N, M), gamma, err, stream));
@@ -702,10 +713,11 @@ sdtw_status launch_forward(const void* D, int64_t B, int64_t N, int64_t M, const
     e = cudaMemsetAsync(ws, 0, kHeader, stream);
     if (e != cudaSuccess) return from_cuda(e);
     const int W = choose_pair_warps<T>(*di, false, B, N, M);
+    if (Rt != nullptr && W == 0) return SDTW_EINVAL;  // tiles exist only between the pair-resident kernels
     if (W > 0)
-        return from_cuda(pair_forward<T>(static_cast<const T*>(D), static_cast<T*>(R), static_cast<T*>(costs), lx, ly,
-                                         is32, B, N, M, clamp_bw(bw, N, M), gamma, W, make_sync(ws, err),
-                                         g_inject_skip, stream));
+        return from_cuda(pair_forward<T>(static_cast<const T*>(D), static_cast<T*>(R), static_cast<T*>(Rt),
+                                         static_cast<T*>(costs), lx, ly, is32, B, N, M, clamp_bw(bw, N, M), gamma, W,
+                                         make_sync(ws, err), g_inject_skip, stream));
     e = cudaMemsetAsync(static_cast<char*>(ws) + kHeader, 0xff, bnd_bytes(B, N, M, sizeof(T)), stream);
     if (e != cudaSuccess) return from_cuda(e);
     const int64_t slab = (N + 2) * (M + 2);
@@ -745,11 +757,13 @@ sdtw_status launch_forward(const void* D, int64_t B, int64_t N, int64_t M, const
 
 template <typename T>
 sdtw_status launch_backward(const void* R, int64_t B, int64_t N, int64_t M, const void* lx, const void* ly, int is32,
-                            double gamma, int64_t bw, void* E, void* ws, uint32_t* err, cudaStream_t stream)
+                            double gamma, int64_t bw, void* E, void* ws, uint32_t* err, cudaStream_t stream,
+                            const void* Rt = nullptr)
 {
     const DeviceInfo* di = nullptr;
     cudaError_t e = device_info(di);
     if (e != cudaSuccess) return from_cuda(e);
+    if (Rt != nullptr && !uses_tiles<T>(*di, B, N, M)) return SDTW_EINVAL;
     if (use_warp_kernels<T>(*di, B, N, M))
         return from_cuda(warp_backward<T>(static_cast<const T*>(R), static_cast<T*>(E), lx, ly, is32, B, N, M,
                                           clamp_bw(bw, N, M), gamma, err, stream));
@@ -757,8 +771,10 @@ sdtw_status launch_backward(const void* R, int64_t B, int64_t N, int64_t M, cons
     e = cudaMemsetAsync(ws, 0, kHeader, stream);
     if (e != cudaSuccess) return from_cuda(e);
     const int W = choose_pair_warps<T>(*di, true, B, N, M);
+    if (Rt != nullptr && W == 0) return SDTW_EINVAL;
     if (W > 0)
-        return from_cuda(pair_backward<T>(static_cast<const T*>(R), static_cast<T*>(E), lx, ly, is32, B, N, M,
+        return from_cuda(pair_backward<T>(static_cast<const T*>(R), static_cast<const T*>(Rt), static_cast<T*>(E), lx,
+                                          ly, is32, B, N, M,
                                           clamp_bw(bw, N, M), gamma, W, make_sync(ws, err), g_inject_skip, stream));
     e = cudaMemsetAsync(static_cast<char*>(ws) + kHeader, 0xff, bnd_bytes(B, N, M, sizeof(T)), stream);
     if (e != cudaSuccess) return from_cuda(e);
@@ -926,6 +942,60 @@ sdtw_status sdtw_forward(sdtw_dtype dtype, const void* D, int64_t B, int64_t N, 
                                      workspace, err_word, s);
     return launch_forward<double>(D, B, N, M, lengths_x, lengths_y, lengths_int32, gamma, bandwidth, R, costs,
                                   workspace, err_word, s);
+}
+
+int sdtw_r_tiled(int64_t B, int64_t N, int64_t M, sdtw_dtype dtype)
+{
+    if (B <= 0 || N <= 0 || M <= 0 || (dtype != SDTW_F32 && dtype != SDTW_F64)) return 0;
+    const DeviceInfo* di = nullptr;
+    if (device_info(di) != cudaSuccess) return 0;
+    return dtype == SDTW_F32 ? uses_tiles<float>(*di, B, N, M) : uses_tiles<double>(*di, B, N, M);
+}
+
+int64_t sdtw_r_tiles_elems(int64_t B, int64_t N, int64_t M)
+{
+    if (B < 0 || N < 0 || M < 0) return 0;
+    return B * strips_of(N) * static_cast<int64_t>(pair_tile_blocks(M)) * 1024;
+}
+
+sdtw_status sdtw_forward_tiles(sdtw_dtype dtype, const void* D, int64_t B, int64_t N, int64_t M, const void* lengths_x,
+                               const void* lengths_y, int lengths_int32, double gamma, int64_t bandwidth,
+                               void* R_tiles, void* costs, void* workspace, size_t workspace_bytes,
+                               uint32_t* err_word, void* stream)
+{
+    if (dtype != SDTW_F32 && dtype != SDTW_F64) return SDTW_EDTYPE;
+    if (!common_args_ok(B, N, M, gamma)) return SDTW_EINVAL;
+    if (B == 0) return SDTW_OK;
+    if (!sdtw_r_tiled(B, N, M, dtype)) return SDTW_EINVAL;
+    if (!lengths_x || !lengths_y || !R_tiles || !costs || !err_word || !D) return SDTW_EINVAL;
+    if (reinterpret_cast<uintptr_t>(R_tiles) % 16 != 0) return SDTW_EINVAL;
+    if (!workspace || workspace_bytes < sdtw_forward_workspace_bytes(B, N, M, dtype)) return SDTW_EWORKSPACE;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (dtype == SDTW_F32)
+        return launch_forward<float>(D, B, N, M, lengths_x, lengths_y, lengths_int32, gamma, bandwidth, nullptr,
+                                     costs, workspace, err_word, s, R_tiles);
+    return launch_forward<double>(D, B, N, M, lengths_x, lengths_y, lengths_int32, gamma, bandwidth, nullptr, costs,
+                                  workspace, err_word, s, R_tiles);
+}
+
+sdtw_status sdtw_backward_tiles(sdtw_dtype dtype, const void* R_tiles, int64_t B, int64_t N, int64_t M,
+                                const void* lengths_x, const void* lengths_y, int lengths_int32, double gamma,
+                                int64_t bandwidth, void* E, void* workspace, size_t workspace_bytes,
+                                uint32_t* err_word, void* stream)
+{
+    if (dtype != SDTW_F32 && dtype != SDTW_F64) return SDTW_EDTYPE;
+    if (!common_args_ok(B, N, M, gamma)) return SDTW_EINVAL;
+    if (B == 0) return SDTW_OK;
+    if (!sdtw_r_tiled(B, N, M, dtype)) return SDTW_EINVAL;
+    if (!lengths_x || !lengths_y || !R_tiles || !E || !err_word) return SDTW_EINVAL;
+    if (reinterpret_cast<uintptr_t>(R_tiles) % 16 != 0) return SDTW_EINVAL;
+    if (!workspace || workspace_bytes < sdtw_backward_workspace_bytes(B, N, M, dtype)) return SDTW_EWORKSPACE;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (dtype == SDTW_F32)
+        return launch_backward<float>(nullptr, B, N, M, lengths_x, lengths_y, lengths_int32, gamma, bandwidth, E,
+                                      workspace, err_word, s, R_tiles);
+    return launch_backward<double>(nullptr, B, N, M, lengths_x, lengths_y, lengths_int32, gamma, bandwidth, E,
+                                   workspace, err_word, s, R_tiles);
 }
 
 sdtw_status sdtw_backward(sdtw_dtype dtype, const void* D, const void* R, int64_t B, int64_t N, int64_t M,

@@ -219,8 +219,51 @@ void xy_checks(const Tensor& X, const Tensor& Y, const Tensor& lengths_x, const 
     same_device(X, lengths_y, "lengths_y");
 }
 
-// Returns (costs, R, D, clamp_flags): D is the clamped cost matrix with the clamp recorded in its sign
-// bit; clamp_flags (B,) int32 marks the pairs that have a clamped cell.
+// The module path's R: the forward's strip tiles (B, S, NBt, 32, 32) when both wavefront directions run on
+// the pair-resident kernels for this shape (sdtw_r_tiled), else the padded R (B, N+2, M+2) of the op. The
+// backward tells the two apart by the number of dimensions.
+std::tuple<Tensor, Tensor> run_forward_module(const Tensor& Dacc, const Tensor& lx, const Tensor& ly, double gamma,
+                                              int64_t bandwidth)
+{
+    const int64_t B = Dacc.size(0), N = Dacc.size(1), M = Dacc.size(2);
+    const auto st = Dacc.scalar_type();
+    if (B == 0 || N == 0 || M == 0 || !sdtw_r_tiled(B, N, M, code_of(st))) return run_forward(Dacc, lx, ly, gamma, bandwidth);
+    auto opts = Dacc.options();
+    const int64_t S = (N + 31) / 32, NBt = sdtw_r_tiles_elems(1, 32, M) / 1024;
+    Tensor Rt = at::empty({B, S, NBt, 32, 32}, opts);
+    Tensor costs = at::empty({B}, opts);
+    const size_t wsb = sdtw_forward_workspace_bytes(B, N, M, code_of(st));
+    Tensor ws = at::empty({static_cast<int64_t>(wsb)}, opts.dtype(at::kByte));
+    cudaStream_t stream = at::cuda::getCurrentCUDAStream(Dacc.get_device()).stream();
+    check_status(sdtw_forward_tiles(code_of(st), Dacc.data_ptr(), B, N, M, lx.data_ptr(), ly.data_ptr(),
+                                    lx.scalar_type() == at::kInt, gamma, bandwidth, Rt.data_ptr(), costs.data_ptr(),
+                                    ws.data_ptr(), wsb, error_word(Dacc), stream),
+                 "forward");
+    maybe_sync_check(Dacc, stream);
+    return {costs, Rt};
+}
+
+Tensor run_backward_module(const Tensor& Racc, const Tensor& lx, const Tensor& ly, double gamma, int64_t bandwidth,
+                           int64_t N, int64_t M)
+{
+    if (Racc.dim() != 5) return run_backward(Racc, lx, ly, gamma, bandwidth, N, M);
+    const int64_t B = Racc.size(0);
+    const auto st = Racc.scalar_type();
+    auto opts = Racc.options();
+    Tensor E = at::empty({B, N, M}, opts);
+    const size_t wsb = sdtw_backward_workspace_bytes(B, N, M, code_of(st));
+    Tensor ws = at::empty({static_cast<int64_t>(wsb)}, opts.dtype(at::kByte));
+    cudaStream_t stream = at::cuda::getCurrentCUDAStream(Racc.get_device()).stream();
+    check_status(sdtw_backward_tiles(code_of(st), Racc.data_ptr(), B, N, M, lx.data_ptr(), ly.data_ptr(),
+                                     lx.scalar_type() == at::kInt, gamma, bandwidth, E.data_ptr(), ws.data_ptr(), wsb,
+                                     error_word(Racc), stream),
+                 "backward");
+    maybe_sync_check(Racc, stream);
+    return E;
+}
+
+// Returns (costs, R, D, clamp_flags): R as run_forward_module returns it; D is the clamped cost matrix with
+// the clamp recorded in its sign bit; clamp_flags (B,) int32 marks the pairs that have a clamped cell.
 std::tuple<Tensor, Tensor, Tensor, Tensor> l2_forward_cuda(const Tensor& X, const Tensor& Y,
                                                            const Tensor& lengths_x, const Tensor& lengths_y,
                                                            double gamma, int64_t bandwidth)
@@ -236,7 +279,7 @@ std::tuple<Tensor, Tensor, Tensor, Tensor> l2_forward_cuda(const Tensor& X, cons
     check_status(sdtw_pairwise_l2(code_of(acc), Xc.data_ptr(), Yc.data_ptr(), B, N, M, d, D.data_ptr(),
                                   flags.data_ptr<int>(), stream),
                  "pairwise_l2");
-    auto [costs, R] = run_forward(D, prep_lengths(lengths_x), prep_lengths(lengths_y), gamma, bandwidth);
+    auto [costs, R] = run_forward_module(D, prep_lengths(lengths_x), prep_lengths(lengths_y), gamma, bandwidth);
     return {costs, R, D, flags};
 }
 
@@ -252,9 +295,12 @@ std::tuple<Tensor, Tensor> l2_backward_cuda(const Tensor& X, const Tensor& Y, co
     const Tensor Xc = X.to(acc).contiguous(), Yc = Y.to(acc).contiguous();
     const int64_t B = Xc.size(0), N = Xc.size(1), M = Yc.size(1), d = Xc.size(2);
     TORCH_CHECK(D.sizes() == at::IntArrayRef({B, N, M}) && D.scalar_type() == acc, "D has the wrong shape or dtype");
-    TORCH_CHECK(R.sizes() == at::IntArrayRef({B, N + 2, M + 2}) && R.scalar_type() == acc,
+    const bool tiled = R.dim() == 5 &&
+                       R.sizes() == at::IntArrayRef({B, (N + 31) / 32, sdtw_r_tiles_elems(1, 32, M) / 1024, 32, 32});
+    TORCH_CHECK((tiled || R.sizes() == at::IntArrayRef({B, N + 2, M + 2})) && R.scalar_type() == acc,
                 "R has the wrong shape or dtype");
-    Tensor E = run_backward(R.contiguous(), prep_lengths(lengths_x), prep_lengths(lengths_y), gamma, bandwidth, N, M);
+    Tensor E = run_backward_module(R.contiguous(), prep_lengths(lengths_x), prep_lengths(lengths_y), gamma, bandwidth,
+                                   N, M);
     const Tensor g = grad_costs.to(acc).contiguous();
     // Gradients that are not requested come back as empty tensors.
     Tensor gX = need_x ? at::empty({B, N, d}, Xc.options()) : at::empty({0}, X.options());

@@ -52,8 +52,14 @@ def _l2_forward_fake(X, Y, lengths_x, lengths_y, gamma, bandwidth):
     B, N, _ = X.shape
     M = Y.shape[1]
     acc_dt = _acc_dtype(X.dtype)
-    return (X.new_empty((B,), dtype=acc_dt), X.new_empty((B, N + 2, M + 2), dtype=acc_dt),
-            X.new_empty((B, N, M), dtype=acc_dt), X.new_empty((B,), dtype=torch.int32))
+    # R is the forward's strip tiles when the pair-resident kernels run both directions (a property of the
+    # shape, the dtype and the device, asked of the library), else the padded R.
+    if _ext.r_tiled(int(B), int(N), int(M), acc_dt, X.device):
+        R = X.new_empty((B, (N + 31) // 32, (M + 31) // 32 + 1, 32, 32), dtype=acc_dt)
+    else:
+        R = X.new_empty((B, N + 2, M + 2), dtype=acc_dt)
+    return (X.new_empty((B,), dtype=acc_dt), R, X.new_empty((B, N, M), dtype=acc_dt),
+            X.new_empty((B,), dtype=torch.int32))
 
 
 @torch.library.register_fake("torchsoftdtw_b200::l2_backward")
