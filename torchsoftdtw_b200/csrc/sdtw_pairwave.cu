@@ -221,10 +221,10 @@ __device__ __forceinline__ void fwd_pair_steps8(T* cell, const T* top, int tau0,
     sts8(cell, dv);
 }
 
-// The 32 steps of block `tau0 / 32`, as four groups of 8: wait for the strip above (group g of this strip
+// Groups Q0 .. Q1 of the 32 steps of block `tau0 / 32` (four groups of 8): wait for the strip above (group g of this strip
 // reads columns up to 8g + 7 of the row above, complete with the group g + 4 of the strip above), sweep,
 // publish the 8 values of the last row that the group finished. Returns false if the launch aborted.
-template <typename T, bool MASKED>
+template <typename T, bool MASKED, int Q0, int Q1>
 __device__ __forceinline__ bool fwd_pair_block(T* cell, const T* top, const T* last, T* bout, int tau0, int A, int Z,
                                                T k, T gl, bool wait_in, uint32_t bars_in, uint32_t par_in, int glast,
                                                bool publish, bool has_consumer, uint32_t bars_out, const Sync& sy,
@@ -234,7 +234,7 @@ __device__ __forceinline__ bool fwd_pair_block(T* cell, const T* top, const T* l
     const bool pub_lane = lane < kPubLanes;
     const int g0 = tau0 / 8;
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
+    for (int q = Q0; q <= Q1; ++q) {
         if (wait_in && !fbar_wait_fast(bars_in + 8 * min(g0 + q + 4, glast), par_in, sy, lane)) return false;
         fwd_pair_steps8<T, MASKED>(cell + 8 * q, top + 8 * q, tau0 + 8 * q, A, Z, k, gl, src_lane, lane0, outp, upp);
         if (publish) {
@@ -294,10 +294,9 @@ __device__ bool fwd_pair_strip(const PairFwdArgs<T>& a, T* ring, const T* bin, u
     T* tile0 = tiles ? a.Rt + ((b * a.S + s) * static_cast<int64_t>(a.NBt) * 32 + lane) * 32 : nullptr;
 
     cp_async_wait<0>();
+    if (tiles) bulk_wait_read<0>();
     __syncwarp();
     fwd_pair_load<T>(Db, M, ring, k0, st.rows, lane);
-    cp_async_commit();
-    if (k0 + 1 <= k1) fwd_pair_load<T>(Db, M, ring, k0 + 1, st.rows, lane);
     cp_async_commit();
 
     if (!tiles) {
@@ -326,21 +325,37 @@ __device__ bool fwd_pair_strip(const PairFwdArgs<T>& a, T* ring, const T* bin, u
     T outp = INF;
     const int src_lane = (lane + 31) & 31;
 
+    // D of the first block is in flight; the loop prefetches D of block blk + 1 after the first group of block
+    // blk, into the slot of block blk - 1, whose R was written back at the end of that block (its bulk copy has
+    // had a group's time to read the slot).
 #pragma unroll 1
     for (int blk = k0; blk <= k1; ++blk) {
-        cp_async_wait<1>();
+        cp_async_wait<0>();
         __syncwarp();
         const int tau0 = 32 * blk;
         T* cell = ring + lane * RS + (blk & 1) * 32;
         const T* top = bin + tau0 + kBufPad;
         const T* last = ring + 31 * RS + (blk & 1) * 32;  // the strip's last row, positions tau0 ..
-        const bool ok = (tau0 >= Amax && tau0 + 31 <= Zmin)
-                            ? fwd_pair_block<T, false>(cell, top, last, bout, tau0, A, Z, a.k, a.gl, wait_in, bars_in,
+        const bool full = tau0 >= Amax && tau0 + 31 <= Zmin;
+        bool ok = full ? fwd_pair_block<T, false, 0, 0>(cell, top, last, bout, tau0, A, Z, a.k, a.gl, wait_in, bars_in,
+                                                        par_in, glast, !skip, has_consumer, bars_out, a.sy, src_lane,
+                                                        lane, outp, upp)
+                       : fwd_pair_block<T, true, 0, 0>(cell, top, last, bout, tau0, A, Z, a.k, a.gl, wait_in, bars_in,
                                                        par_in, glast, !skip, has_consumer, bars_out, a.sy, src_lane,
-                                                       lane, outp, upp)
-                            : fwd_pair_block<T, true>(cell, top, last, bout, tau0, A, Z, a.k, a.gl, wait_in, bars_in,
-                                                      par_in, glast, !skip, has_consumer, bars_out, a.sy, src_lane,
-                                                      lane, outp, upp);
+                                                       lane, outp, upp);
+        if (!ok) return false;
+        if (blk + 1 <= k1) {
+            if (tiles) bulk_wait_read<0>();
+            __syncwarp();
+            fwd_pair_load<T>(Db, M, ring, blk + 1, st.rows, lane);
+        }
+        cp_async_commit();
+        ok = full ? fwd_pair_block<T, false, 1, 3>(cell, top, last, bout, tau0, A, Z, a.k, a.gl, wait_in, bars_in,
+                                                   par_in, glast, !skip, has_consumer, bars_out, a.sy, src_lane, lane,
+                                                   outp, upp)
+                  : fwd_pair_block<T, true, 1, 3>(cell, top, last, bout, tau0, A, Z, a.k, a.gl, wait_in, bars_in,
+                                                  par_in, glast, !skip, has_consumer, bars_out, a.sy, src_lane, lane,
+                                                  outp, upp);
         if (!ok) return false;
         if (tiles) {
             // Row `lane` of the block's slot -> tile (b, s, blk), one bulk copy per lane (the lane's own writes,
@@ -353,11 +368,8 @@ __device__ bool fwd_pair_strip(const PairFwdArgs<T>& a, T* ring, const T* bin, u
             fwd_pair_store<T>(Rrow, pitch, M, ring, blk, nmat, lane);
         }
         if (blk == bstar && lane == lstar) a.costs[b] = cell[tstar - tau0];
-        if (tiles) bulk_wait_read<0>();  // the slot is refilled next
-        __syncwarp();
-        if (blk + 2 <= k1) fwd_pair_load<T>(Db, M, ring, blk + 2, st.rows, lane);
-        cp_async_commit();
     }
+    if (tiles) bulk_wait_read<0>();  // the ring is reused by the warp's next strip
     if (!skip) {
         // The strip below may read columns past this sweep as its row above: they are out of band (+inf).
         if (has_consumer)
