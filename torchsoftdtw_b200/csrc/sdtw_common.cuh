@@ -214,46 +214,6 @@ __device__ __forceinline__ void st_relaxed(double* p, double v)
 __device__ __forceinline__ bool is_absent(float v) { return __float_as_uint(v) == 0xffffffffu; }
 __device__ __forceinline__ bool is_absent(double v) { return __double_as_longlong(v) == -1ll; }
 
-// --------------------------------------------------------------------------------------------------
-// Bulk copies between global and shared memory (the TMA engine, no tensor map): 16-byte aligned
-// addresses, sizes a multiple of 16 bytes.
-// --------------------------------------------------------------------------------------------------
-// Generic-proxy shared-memory writes (or reads) of this thread, ordered before its later bulk copies.
-__device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
-// shared -> global, in this thread's current bulk group.
-__device__ __forceinline__ void bulk_s2g(void* gdst, const void* ssrc, uint32_t bytes)
-{
-    asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(gdst), "r"(smem_addr(ssrc)),
-                 "r"(bytes)
-                 : "memory");
-}
-__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
-// Until at most N of this thread's bulk groups are still reading their shared-memory source.
-template <int N>
-__device__ __forceinline__ void bulk_wait_read()
-{
-    asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
-}
-// Until at most N of this thread's bulk groups are incomplete (their global writes done).
-template <int N>
-__device__ __forceinline__ void bulk_wait_all()
-{
-    asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory");
-}
-// global -> shared, completing `bytes` of the transaction count of the mbarrier at shared address `bar`.
-__device__ __forceinline__ void bulk_g2s(void* sdst, const void* gsrc, uint32_t bytes, uint32_t bar)
-{
-    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                     smem_addr(sdst)),
-                 "l"(gsrc), "r"(bytes), "r"(bar)
-                 : "memory");
-}
-// One arrival on the mbarrier at `bar`, raising its expected transaction count by `bytes`.
-__device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes)
-{
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
-}
-
 __device__ __forceinline__ uint64_t global_ns()
 {
     uint64_t t;

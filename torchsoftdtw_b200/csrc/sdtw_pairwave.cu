@@ -197,6 +197,25 @@ __device__ __forceinline__ bool fbar_wait_fast(uint32_t bar, uint32_t parity, co
 
 // 8 forward steps tau0 .. tau0+7 of one warp. `cell` is this lane's ring row at position tau0 (read and
 // written with 16-byte accesses), `top` the row above (boundary row) at column tau0.
+// Finished slot of block `blk` -> its 32 x 32 tile (module path): 16-byte pieces, each store instruction writing
+// whole 128-byte tile rows (4 rows of floats, 2 of doubles), read from the ring row by row.
+template <typename T>
+__device__ __forceinline__ void fwd_tile_store(T* tile, const T* ring, int blk, int lane)
+{
+    constexpr int RS = FwdRing<T>::S;
+    constexpr int EPP = 16 / sizeof(T);  // elements per piece
+    constexpr int CPR = 32 / EPP;        // pieces per row
+    constexpr int RPI = 32 / CPR;        // rows per store instruction
+    const int r = lane / CPR, c = (lane % CPR) * EPP;
+    const T* src = ring + r * RS + (blk & 1) * 32 + c;
+    T* dst = tile + r * 32 + c;
+#pragma unroll
+    for (int i = 0; i < 32; i += RPI) {
+        const uint4 v = *reinterpret_cast<const uint4*>(src + i * RS);
+        *reinterpret_cast<uint4*>(dst + i * 32) = v;
+    }
+}
+
 template <typename T, bool MASKED>
 __device__ __forceinline__ void fwd_pair_steps8(T* cell, const T* top, int tau0, int A, int Z, T k, T gl,
                                                 int src_lane, bool lane0, T& outp, T& upp)
@@ -291,10 +310,9 @@ __device__ bool fwd_pair_strip(const PairFwdArgs<T>& a, T* ring, const T* bin, u
     const bool skip = b * a.S + s == a.inject;
     const bool has_consumer = st.rows == 32 && r0 + 32 < st.nx && !skip;
     const T* Db = a.D + (b * N + r0) * M;
-    T* tile0 = tiles ? a.Rt + ((b * a.S + s) * static_cast<int64_t>(a.NBt) * 32 + lane) * 32 : nullptr;
+    T* tile0 = tiles ? a.Rt + (b * a.S + s) * static_cast<int64_t>(a.NBt) * 1024 : nullptr;
 
     cp_async_wait<0>();
-    if (tiles) bulk_wait_read<0>();
     __syncwarp();
     fwd_pair_load<T>(Db, M, ring, k0, st.rows, lane);
     cp_async_commit();
@@ -326,8 +344,7 @@ __device__ bool fwd_pair_strip(const PairFwdArgs<T>& a, T* ring, const T* bin, u
     const int src_lane = (lane + 31) & 31;
 
     // D of the first block is in flight; the loop prefetches D of block blk + 1 after the first group of block
-    // blk, into the slot of block blk - 1, whose R was written back at the end of that block (its bulk copy has
-    // had a group's time to read the slot).
+    // blk, into the slot of block blk - 1 (whose R was written back at the end of that block).
 #pragma unroll 1
     for (int blk = k0; blk <= k1; ++blk) {
         cp_async_wait<0>();
@@ -345,7 +362,6 @@ __device__ bool fwd_pair_strip(const PairFwdArgs<T>& a, T* ring, const T* bin, u
                                                        lane, outp, upp);
         if (!ok) return false;
         if (blk + 1 <= k1) {
-            if (tiles) bulk_wait_read<0>();
             __syncwarp();
             fwd_pair_load<T>(Db, M, ring, blk + 1, st.rows, lane);
         }
@@ -357,19 +373,13 @@ __device__ bool fwd_pair_strip(const PairFwdArgs<T>& a, T* ring, const T* bin, u
                                                   par_in, glast, !skip, has_consumer, bars_out, a.sy, src_lane, lane,
                                                   outp, upp);
         if (!ok) return false;
-        if (tiles) {
-            // Row `lane` of the block's slot -> tile (b, s, blk), one bulk copy per lane (the lane's own writes,
-            // ordered before the copy by the proxy fence).
-            fence_proxy_async_smem();
-            bulk_s2g(tile0 + static_cast<int64_t>(blk) * 1024, cell, 32 * sizeof(T));
-            bulk_commit();
-        } else {
-            __syncwarp();
+        __syncwarp();
+        if (tiles)
+            fwd_tile_store<T>(tile0 + static_cast<int64_t>(blk) * 1024, ring, blk, lane);
+        else
             fwd_pair_store<T>(Rrow, pitch, M, ring, blk, nmat, lane);
-        }
         if (blk == bstar && lane == lstar) a.costs[b] = cell[tstar - tau0];
     }
-    if (tiles) bulk_wait_read<0>();  // the ring is reused by the warp's next strip
     if (!skip) {
         // The strip below may read columns past this sweep as its row above: they are out of band (+inf).
         if (has_consumer)
@@ -424,7 +434,6 @@ __global__ void __launch_bounds__(SDTW_PAIR_THREADS, SDTW_PAIR_MIN_CTAS) sdtw_fw
             break;
     }
     cp_async_wait<0>();
-    if (a.Rt != nullptr) bulk_wait_all<0>();  // every tile written before the CTA ends
 }
 
 // ==================================================================================================
@@ -481,59 +490,35 @@ __device__ __forceinline__ void bwd_pair_load(const T* Rb, int64_t N, int64_t M,
     }
 }
 
-// Per-warp bookkeeping of the two slot barriers of the tiled backward: loads issued into each slot, and the
-// parity of the latest one (the phase a reader of the slot waits for).
-struct SlotPhases {
-    uint32_t n[2];
-    uint32_t par[2];
-};
-
-// Slot of block `blk` <- R tiles written by the forward: ring rows 1..32 from tile (s, blk), ring row 0 from
-// row 31 of tile (s-1, blk+1) (the forward's skew puts both at the positions this ring expects). Tiles outside
-// the forward's swept blocks ([kf0, kf1] for strip s, [kp0, kp1] for strip s-1) were never written: their
-// cells are outside the band or the lengths, +inf, and are filled here instead (the row above strip 0 is R's
-// border row, +inf with R[-1][-1] = 0). The copies complete the slot's mbarrier `bar`.
+// Slot of block `blk` <- R tiles written by the forward, asynchronously (cp.async, 16-byte pieces): ring rows
+// 1..32 from tile (s, blk), each lane copying its own row, and ring row 0 from row 31 of tile (s-1, blk+1)
+// (the forward's skew puts both at the positions this ring expects). Tiles outside the forward's swept blocks
+// ([kf0, kf1] for strip s, [kp0, kp1] for strip s-1) were never written: their cells are outside the band or
+// the lengths, +inf, and are filled here instead (the row above strip 0 is R's border row, +inf with
+// R[-1][-1] = 0).
 template <typename T>
 __device__ __forceinline__ void bwd_tile_load(const PairBwdArgs<T>& a, T* ring, int blk, int64_t b, int s, int kf0,
-                                              int kf1, int kp0, int kp1, uint32_t bar, SlotPhases& ph, int lane)
+                                              int kf1, int kp0, int kp1, int lane)
 {
     constexpr int RS = BwdRing<T>::S;
+    constexpr int EPP = 16 / sizeof(T);  // elements per 16-byte piece
     const T INF = Num<T>::inf();
     T* slot = ring + (blk & 1) * 32;
-    const bool own = blk >= kf0 && blk <= kf1;
-    const bool above = s > 0 && blk + 1 >= kp0 && blk + 1 <= kp1;
-    const int p = blk & 1;
-    ph.par[p] = ph.n[p] & 1u;
-    ++ph.n[p];
-    fence_proxy_async_smem();  // this slot's earlier generic reads and writes come before the copies
-    __syncwarp();
-    if (lane == 0)
-        mbar_arrive_expect_tx(bar, static_cast<uint32_t>(((own ? 32 : 0) + (above ? 1 : 0)) * 32 * sizeof(T)));
-    __syncwarp();
     T* row = slot + (lane + 1) * RS;
-    if (own) {
-        bulk_g2s(row, a.Rt + (((b * a.S + s) * static_cast<int64_t>(a.NBt) + blk) * 32 + lane) * 32,
-                 32 * sizeof(T), bar);
+    if (blk >= kf0 && blk <= kf1) {
+        const T* src = a.Rt + (((b * a.S + s) * static_cast<int64_t>(a.NBt) + blk) * 32 + lane) * 32;
+#pragma unroll
+        for (int i = 0; i < 32; i += EPP) cp_async_16(row + i, src + i, 16);
     } else {
 #pragma unroll
         for (int i = 0; i < 32; ++i) row[i] = INF;
     }
-    if (above) {
-        if (lane == 0)
-            bulk_g2s(slot, a.Rt + (((b * a.S + s - 1) * static_cast<int64_t>(a.NBt) + blk + 1) * 32 + 31) * 32,
-                     32 * sizeof(T), bar);
+    if (s > 0 && blk + 1 >= kp0 && blk + 1 <= kp1) {
+        const T* src = a.Rt + (((b * a.S + s - 1) * static_cast<int64_t>(a.NBt) + blk + 1) * 32 + 31) * 32;
+        if (lane < 32 / EPP) cp_async_16(slot + lane * EPP, src + lane * EPP, 16);
     } else {
         slot[lane] = (s == 0 && blk == -1 && lane == 31) ? T(0) : INF;
     }
-}
-
-// Bounded wait for the latest load into the slot of block `blk` (tiled backward).
-__device__ __forceinline__ bool slot_wait(uint32_t bars_slot, int blk, const SlotPhases& ph, const Sync& sy, int lane)
-{
-    const int p = blk & 1;
-    const bool ok = fbar_wait_fast(bars_slot + 8 * p, ph.par[p], sy, lane);
-    __syncwarp();
-    return ok;
 }
 
 // E of slot `blk` -> global (Erow = E row of DP row r0): ring row r + 1 holds E[r0 + r][c] at position c + r.
@@ -608,8 +593,7 @@ __device__ __forceinline__ void bwd_pair_steps8(const T (&A)[8], T am1, T (&Bv)[
 template <typename T, bool MASKED>
 __device__ __forceinline__ bool bwd_pair_block(T* ring, const T* bin, T* bout, int tau0, const Strip& st, T k, T seed,
                                                bool wait_in, uint32_t bars_in, uint32_t par_in, bool publish,
-                                               uint32_t bars_out, bool slot_below_pending, bool tiles,
-                                               uint32_t bars_slot, const SlotPhases& ph, const Sync& sy,
+                                               uint32_t bars_out, bool slot_below_pending, const Sync& sy,
                                                int src_lane, int lane, T& sendv, T& pend, T& acc, T& bcar)
 {
     constexpr int RS = BwdRing<T>::S;
@@ -622,12 +606,8 @@ __device__ __forceinline__ bool bwd_pair_block(T* ring, const T* bin, T* bout, i
         const int t8 = tau0 + 8 * q;
         if (wait_in && !fbar_wait_fast(bars_in + 8 * max(g0 + q - 4, 0), par_in, sy, lane)) return false;
         if (q == 0 && slot_below_pending) {  // position tau0 - 1 lies in the slot of the block below
-            if (tiles) {
-                if (!slot_wait(bars_slot, tau0 / 32 - 1, ph, sy, lane)) return false;
-            } else {
-                cp_async_wait<0>();
-                __syncwarp();
-            }
+            cp_async_wait<0>();
+            __syncwarp();
         }
         T A[8], Bv[8], bvv[8], sv[8];
         lds8(A, rowA + 8 * q);
@@ -657,8 +637,7 @@ __device__ __forceinline__ bool bwd_pair_block(T* ring, const T* bin, T* bout, i
 // launch aborted.
 template <typename T, int MC>
 __device__ bool bwd_pair_strip(const PairBwdArgs<T>& a, T* ring, const T* bin, uint32_t bars_in, uint32_t par_in,
-                               const T* zrow, T* bout, uint32_t bars_out, uint32_t bars_slot, SlotPhases& ph,
-                               int64_t b, int s, int lane)
+                               const T* zrow, T* bout, uint32_t bars_out, int64_t b, int s, int lane)
 {
     const int64_t N = a.N, M = MC > 0 ? MC : a.M;
     const int r0 = 32 * s;
@@ -697,18 +676,20 @@ __device__ bool bwd_pair_strip(const PairBwdArgs<T>& a, T* ring, const T* bin, u
         kp1 = static_cast<int>((hi2 + 32) >> 5);
     }
 
-    if (tiles) {
-        bwd_tile_load<T>(a, ring, k1, b, s, kf0, kf1, kp0, kp1, bars_slot + 8 * (k1 & 1), ph, lane);
-        if (k1 - 1 >= kmin)
-            bwd_tile_load<T>(a, ring, k1 - 1, b, s, kf0, kf1, kp0, kp1, bars_slot + 8 * ((k1 - 1) & 1), ph, lane);
-    } else {
-        cp_async_wait<0>();
-        __syncwarp();
+    cp_async_wait<0>();
+    __syncwarp();
+    if (tiles)
+        bwd_tile_load<T>(a, ring, k1, b, s, kf0, kf1, kp0, kp1, lane);
+    else
         bwd_pair_load<T>(Rb, N, M, ring, k1, r0, lane);
-        cp_async_commit();
-        if (k1 - 1 >= kmin) bwd_pair_load<T>(Rb, N, M, ring, k1 - 1, r0, lane);
-        cp_async_commit();
+    cp_async_commit();
+    if (k1 - 1 >= kmin) {
+        if (tiles)
+            bwd_tile_load<T>(a, ring, k1 - 1, b, s, kf0, kf1, kp0, kp1, lane);
+        else
+            bwd_pair_load<T>(Rb, N, M, ring, k1 - 1, r0, lane);
     }
+    cp_async_commit();
 
     // Columns of each row outside the stored range [32*k0 - r, 32*k1 + 31 - r]: zero.
     for (int r = 0; r < nmat; ++r) {
@@ -730,12 +711,8 @@ __device__ bool bwd_pair_strip(const PairBwdArgs<T>& a, T* ring, const T* bin, u
 
 #pragma unroll 1
     for (int blk = k1; blk >= k0; --blk) {
-        if (tiles) {
-            if (!slot_wait(bars_slot, blk, ph, a.sy, lane)) return false;
-        } else {
-            cp_async_wait<1>();
-            __syncwarp();
-        }
+        cp_async_wait<1>();
+        __syncwarp();
         const int tau0 = 32 * blk;
         if (first) {
             if (has_producer && !fbar_wait_fast(bars_in + 8 * max(4 * k1 + 3 - 4, 0), par_in, a.sy, lane))
@@ -746,24 +723,24 @@ __device__ bool bwd_pair_strip(const PairBwdArgs<T>& a, T* ring, const T* bin, u
         const bool below = blk - 1 >= kmin;
         const bool ok = (tau0 >= st.Amax && tau0 + 31 <= st.Zmin)
                             ? bwd_pair_block<T, false>(ring, bin, bout, tau0, st, a.k, seed, has_producer, bars_in,
-                                                       par_in, publish, bars_out, below, tiles, bars_slot, ph, a.sy,
-                                                       src_lane, lane, sendv, pend, acc, bcar)
+                                                       par_in, publish, bars_out, below, a.sy, src_lane, lane, sendv,
+                                                       pend, acc, bcar)
                             : bwd_pair_block<T, true>(ring, bin, bout, tau0, st, a.k, seed, has_producer, bars_in,
-                                                      par_in, publish, bars_out, below, tiles, bars_slot, ph, a.sy,
-                                                      src_lane, lane, sendv, pend, acc, bcar);
+                                                      par_in, publish, bars_out, below, a.sy, src_lane, lane, sendv,
+                                                      pend, acc, bcar);
         if (!ok) return false;
         __syncwarp();
         bwd_pair_store<T>(Erow, M, ring, blk, nmat, lane);
         __syncwarp();
-        if (tiles) {
-            if (blk - 2 >= kmin)
-                bwd_tile_load<T>(a, ring, blk - 2, b, s, kf0, kf1, kp0, kp1, bars_slot + 8 * (blk & 1), ph, lane);
-        } else {
-            if (blk - 2 >= kmin) bwd_pair_load<T>(Rb, N, M, ring, blk - 2, r0, lane);
-            cp_async_commit();
+        if (blk - 2 >= kmin) {
+            if (tiles)
+                bwd_tile_load<T>(a, ring, blk - 2, b, s, kf0, kf1, kp0, kp1, lane);
+            else
+                bwd_pair_load<T>(Rb, N, M, ring, blk - 2, r0, lane);
         }
+        cp_async_commit();
     }
-    if (!tiles) cp_async_wait<0>();
+    cp_async_wait<0>();
     __syncwarp();
     if (publish) {
         // Lane 0's last diagonal push (into column 32*k0 - 1) and zeros below the sweep; then complete the
@@ -788,39 +765,23 @@ __global__ void __launch_bounds__(SDTW_PAIR_THREADS, SDTW_PAIR_MIN_CTAS) sdtw_bw
     T* rings = reinterpret_cast<T*>(smem);
     T* bufs = rings + static_cast<size_t>(W) * 33 * RS;
     T* zrow = bufs + static_cast<size_t>(W) * a.BL;
-    const uint32_t bars = (smem_addr(zrow + a.BL) + 7u) & ~7u;  // [W][G] progress mbarriers, then [W][2] slot ones
-    const uint32_t slot_bars = bars + 8 * W * a.G;
+    const uint32_t bars = (smem_addr(zrow + a.BL) + 7u) & ~7u;  // [W][G] progress mbarriers
     const int64_t b = blockIdx.x;
     for (int e = threadIdx.x; e < W * (33 * RS + a.BL) + a.BL; e += blockDim.x) rings[e] = T(0);
-    for (int e = threadIdx.x; e < W * (a.G + 2); e += blockDim.x)
+    for (int e = threadIdx.x; e < W * a.G; e += blockDim.x)
         asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bars + 8 * e), "r"(1) : "memory");
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     __syncthreads();
     T* ring = rings + static_cast<size_t>(warp) * 33 * RS;
-    SlotPhases ph = {{0u, 0u}, {0u, 0u}};
-    bool ok = true;
     for (int t = warp; t < a.S; t += W) {
         const int wp = (t + W - 1) % W;
         const uint32_t par_in = static_cast<uint32_t>(((t - 1) / W) & 1);  // round of the strip below in its warp
         if (!bwd_pair_strip<T, MC>(a, ring, bufs + static_cast<size_t>(wp) * a.BL, bars + 8 * wp * a.G, par_in, zrow,
-                                   bufs + static_cast<size_t>(warp) * a.BL, bars + 8 * warp * a.G,
-                                   slot_bars + 16 * warp, ph, b, a.S - 1 - t, lane)) {
-            ok = false;
+                                   bufs + static_cast<size_t>(warp) * a.BL, bars + 8 * warp * a.G, b, a.S - 1 - t,
+                                   lane))
             break;
-        }
     }
     cp_async_wait<0>();
-    if (a.Rt != nullptr && !ok) {
-        // A strip that stopped early (the launch aborted) may have bulk loads in flight into this warp's ring:
-        // they land before the CTA ends (each wait bounded by the library's wait limit, ignoring the abort).
-        for (int p = 0; p < 2; ++p) {
-            if (ph.n[p] == 0) continue;
-            const uint32_t bar = slot_bars + 16 * warp + 8 * p;
-            const uint64_t t0 = global_ns();
-            while (!__all_sync(kFull, fbar_try_wait(bar, ph.par[p])) && global_ns() - t0 <= a.sy.timeout_ns) {
-            }
-        }
-    }
 }
 
 // ==================================================================================================
@@ -836,7 +797,7 @@ template <typename T>
 size_t pair_bwd_smem_bytes(int W, int64_t M)
 {
     return (static_cast<size_t>(W) * 33 * BwdRing<T>::S + static_cast<size_t>(W + 1) * buf_len(M)) * sizeof(T) + 8 +
-           static_cast<size_t>(W) * (fwd_groups(M) + 2) * 8;
+           static_cast<size_t>(W) * fwd_groups(M) * 8;
 }
 
 template <typename T>

@@ -644,8 +644,12 @@ int choose_pair_warps(const DeviceInfo& di, bool backward, int64_t B, int64_t N,
     // Measured on B200, fp32, forward op (pair-resident / strip-ticket): 256 x 512 x 512 0.230 / 0.313 ms,
     // 512 x 256 x 256 0.148 / 0.172, 512 x 192 x 192 0.109 / 0.118, 1024 x 160 x 160 0.150 / 0.137,
     // 65536 x 64 x 64 2.08 / 1.30; backward op at 256 x 512 x 512: 0.243 / 0.272 ms. Both directions switch
-    // together (the module path then hands R over as tiles), for pairs of at least 6 strips.
-    if (g_force_path != 2 && (B < di.sms || strips_of(N) < 6)) return 0;
+    // together (the module path then hands R over as tiles), for pairs of at least 6 strips. Batches smaller
+    // than the SM count stay on the pair-resident kernels while one warp per strip fits a CTA (at most 16
+    // strips): every strip of a pair then runs at once and a pair takes its dependency chain's time, where the
+    // strip-ticket kernels' coarser hand-over through L2 makes the chain longer (128 x 512 x 512 forward:
+    // strip-ticket 0.233 ms).
+    if (g_force_path != 2 && ((B < di.sms && strips_of(N) > kPairMaxWarps) || strips_of(N) < 6)) return 0;
     if (B > 0x7fffffff || !pair_keys_fit(N, M)) return 0;
     // Enough CTAs per SM for the whole batch to be resident at once (up to 8), each as wide as its
     // share of the SM's shared memory and registers allows.
