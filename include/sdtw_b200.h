@@ -141,6 +141,24 @@ sdtw_status sdtw_backward_tiles(sdtw_dtype dtype, const void* R_tiles, int64_t B
                                 uint32_t* err_word, void* stream);
 
 /* ---------------------------------------------------------------------------------------------------
+ * Compensated fp32 forward / backward (no counterpart in the reference): the better-conditioned fp32 path.
+ * The reference's fp32 backward takes its softmin weights from exp((R[s] - R[p] - D[s]) / gamma)
+ * (src/torchsoftdtw/csrc/softdtw.cpp:248-256); an fp32 R carries an absolute error of about ulp(R), which a
+ * small gamma turns into O(1) weight errors. These entry points keep R as an unevaluated sum of two floats
+ * R_hi + R_lo (each cell accumulated exactly by TwoSum), so the weights come from R differences accurate to
+ * far below ulp(R). Inputs and outputs are fp32; R_hi and R_lo have the padded layout of R (B, N+2, M+2).
+ * costs = R_hi + R_lo of the terminal cell. Same lengths, band, error word and NaN conventions as
+ * sdtw_forward / sdtw_backward; no workspace (one warp per pair, strips in sequence: slower than the default
+ * kernels, for callers who need accurate fp32 gradients). M is limited by shared memory (about 6400).
+ * ------------------------------------------------------------------------------------------------- */
+sdtw_status sdtw_forward_x2(const float* D, int64_t B, int64_t N, int64_t M, const void* lengths_x,
+                            const void* lengths_y, int lengths_int32, double gamma, int64_t bandwidth, float* R_hi,
+                            float* R_lo, float* costs, uint32_t* err_word, void* stream);
+sdtw_status sdtw_backward_x2(const float* R_hi, const float* R_lo, int64_t B, int64_t N, int64_t M,
+                             const void* lengths_x, const void* lengths_y, int lengths_int32, double gamma,
+                             int64_t bandwidth, float* E, uint32_t* err_word, void* stream);
+
+/* ---------------------------------------------------------------------------------------------------
  * Pairwise squared Euclidean cost: D[b,i,j] = (|x_i|^2 + |y_j|^2) - 2 x_i.y_j, clamped at 0.
  * Replaces the reference's pairwise_l2_squared (src/torchsoftdtw/distances.py:4-18) on the module path.
  * Cells where the unclamped value is negative are stored as -0.0 (sign bit set), so that the

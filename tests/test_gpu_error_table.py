@@ -4,10 +4,12 @@ own fp32 error (the oracle in fp32, bit-identical to the reference's CPU operato
 
 * module level: costs (relative) and grad_X of ``SoftDTW(...)(X, Y).sum()`` (X, Y float32 -> fp64 truth from the
   same float32 inputs);
-* op level: E = d costs / d D on the same float32 D.
+* op level: E = d costs / d D on the same float32 D, by the default ops and by the compensated ops
+  (``torchsoftdtw_b200::forward_x2 / backward_x2``, R kept as R_hi + R_lo).
 
-Run with ``-s`` to print the table (one JSON line per workload). The assertions pin the ratio: this library's
-gradient error is at most 0.25 times the reference's on every workload (measured 0.02-0.13).
+Run with ``-s`` to print the table (one JSON line per workload). The assertions pin the ratios: this library's
+gradient error is at most 0.25 times the reference's on every workload (measured 0.02-0.13), and the
+compensated ops' E error at most 0.01 times the reference's.
 """
 
 import json
@@ -48,6 +50,12 @@ def test_fp32_gradient_error_table(cuda, name, batch):
     E64 = O.backward(D32.astype(np.float64), R64, lxn, lyn, w.gamma, w.bandwidth)
     _, R32 = O.forward(D32, lxn, lyn, w.gamma, w.bandwidth)
     E32 = O.backward(D32, R32, lxn, lyn, w.gamma, w.bandwidth).astype(np.float64)
+    cx, Rh, Rl = torch.ops.torchsoftdtw_b200.forward_x2(Dd, lx.to(cuda), ly.to(cuda), w.gamma, w.bandwidth)
+    Ex = torch.ops.torchsoftdtw_b200.backward_x2(Dd, Rh, Rl, lx.to(cuda), ly.to(cuda), w.gamma, w.bandwidth)
+    torch.cuda.synchronize()
+    T.check_errors(cuda)
+    Ex = Ex.cpu().numpy().astype(np.float64)
+    c64op, _ = O.forward(D32.astype(np.float64), lxn, lyn, w.gamma, w.bandwidth)
     with np.errstate(invalid="ignore"):
         row = {
             "workload": name, "batch": batch, "gamma": w.gamma,
@@ -58,8 +66,14 @@ def test_fp32_gradient_error_table(cuda, name, batch):
             "grad_x_max": float(np.max(np.abs(gx64))),
             "E_abs_ours": float(np.max(np.abs(E - E64))),
             "E_abs_ref": float(np.nanmax(np.abs(E32 - E64))),
+            "E_abs_compensated": float(np.max(np.abs(Ex - E64))),
+            "cost_rel_compensated": float(np.max(np.abs(cx.cpu().numpy() - c64op) / np.abs(c64op))),
         }
     print(json.dumps(row))
     assert row["cost_rel_ours"] <= 1e-5
     assert row["grad_x_abs_ours"] <= RATIO * row["grad_x_abs_ref"], row
     assert row["E_abs_ours"] <= RATIO * row["E_abs_ref"], row
+    assert row["E_abs_compensated"] <= 0.01 * row["E_abs_ref"], row
+    assert row["cost_rel_compensated"] <= 1e-6, row
+    # exact zeros through padding and outside the band, as on the default path
+    assert np.all(Ex[E64 == 0.0] == 0.0)

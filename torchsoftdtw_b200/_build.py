@@ -59,7 +59,7 @@ def _run(cmd: list[str]) -> None:
 def _extra_flags(src: str) -> list[str]:
     # The wavefront kernels spell out every fused multiply-add they use (fma()); no other product is
     # contracted, so the two kernel families (and both directions) round every cell identically.
-    if os.path.basename(src) in ("sdtw_wavefront.cu", "sdtw_pairwave.cu"):
+    if os.path.basename(src) in ("sdtw_wavefront.cu", "sdtw_pairwave.cu", "sdtw_compensated.cu"):
         return ["--fmad=false"]
     return []
 

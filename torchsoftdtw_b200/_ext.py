@@ -63,6 +63,8 @@ SIGNATURES: dict[str, tuple] = {
     "sdtw_r_tiles_elems": (_i64, [_i64, _i64, _i64]),
     "sdtw_forward_tiles": (_i, [_i, _p, _i64, _i64, _i64, _p, _p, _i, _d, _i64, _p, _p, _p, _sz, _p, _p]),
     "sdtw_backward_tiles": (_i, [_i, _p, _i64, _i64, _i64, _p, _p, _i, _d, _i64, _p, _p, _sz, _p, _p]),
+    "sdtw_forward_x2": (_i, [_p, _i64, _i64, _i64, _p, _p, _i, _d, _i64, _p, _p, _p, _p, _p]),
+    "sdtw_backward_x2": (_i, [_p, _p, _i64, _i64, _i64, _p, _p, _i, _d, _i64, _p, _p, _p]),
     "sdtw_pairwise_l2": (_i, [_i, _p, _p, _i64, _i64, _i64, _i64, _p, _p, _p]),
     "sdtw_grad_l2": (_i, [_i, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _p, _p, _p]),
     "sdtw_pairwise_dist": (_i, [_i, _i, _p, _p, _i64, _i64, _i64, _i64, _d, _p, _p]),

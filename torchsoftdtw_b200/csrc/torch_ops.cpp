@@ -378,6 +378,63 @@ std::tuple<Tensor, Tensor> dist_backward_cuda(const Tensor& X, const Tensor& Y, 
     return {gX, gY};
 }
 
+// ---------------------------------------------------------------------------------------------------
+// torchsoftdtw_b200::forward_x2 / backward_x2 — the compensated fp32 ops (R as R_hi + R_lo): the same
+// arguments and validation as torchsoftdtw::forward / backward, float32 (or float16 / bfloat16, promoted) D.
+// ---------------------------------------------------------------------------------------------------
+std::tuple<Tensor, Tensor, Tensor> forward_x2_cuda(const Tensor& D, const Tensor& lengths_x, const Tensor& lengths_y,
+                                                   double gamma, int64_t bandwidth)
+{
+    forward_checks(D, lengths_x, lengths_y, gamma);
+    TORCH_CHECK(D.scalar_type() != at::kDouble, "the compensated ops take float32 (or float16 / bfloat16) D");
+    TORCH_CHECK(D.is_cuda(), "torchsoftdtw_b200 runs on CUDA devices only (sm_100); got a tensor on ", D.device());
+    same_device(D, lengths_x, "lengths_x");
+    same_device(D, lengths_y, "lengths_y");
+    const c10::cuda::CUDAGuard guard(D.device());
+    const Tensor Dc = D.to(at::kFloat).contiguous();
+    const Tensor lx = prep_lengths(lengths_x), ly = prep_lengths(lengths_y);
+    const int64_t B = Dc.size(0), N = Dc.size(1), M = Dc.size(2);
+    Tensor Rh = at::empty({B, N + 2, M + 2}, Dc.options());
+    Tensor Rl = at::empty({B, N + 2, M + 2}, Dc.options());
+    Tensor costs = at::empty({B}, Dc.options());
+    cudaStream_t stream = at::cuda::getCurrentCUDAStream(D.get_device()).stream();
+    check_status(sdtw_forward_x2(Dc.data_ptr<float>(), B, N, M, lx.data_ptr(), ly.data_ptr(),
+                                 lx.scalar_type() == at::kInt, gamma, bandwidth, Rh.data_ptr<float>(),
+                                 Rl.data_ptr<float>(), costs.data_ptr<float>(), error_word(Dc), stream),
+                 "forward_x2");
+    maybe_sync_check(Dc, stream);
+    return {costs, Rh, Rl};
+}
+
+Tensor backward_x2_cuda(const Tensor& D, const Tensor& R_hi, const Tensor& R_lo, const Tensor& lengths_x,
+                        const Tensor& lengths_y, double gamma, int64_t bandwidth)
+{
+    forward_checks(D, lengths_x, lengths_y, gamma);
+    TORCH_CHECK(D.scalar_type() != at::kDouble, "the compensated ops take float32 (or float16 / bfloat16) D");
+    const int64_t B = D.size(0), N = D.size(1), M = D.size(2);
+    for (const Tensor* R : {&R_hi, &R_lo})
+        TORCH_CHECK(R->dim() == 3 && R->size(0) == B && R->size(1) == N + 2 && R->size(2) == M + 2 &&
+                        R->scalar_type() == at::kFloat,
+                    "R_hi and R_lo must be float32 (B, N+2, M+2) = (", B, ", ", N + 2, ", ", M + 2, "), got ",
+                    R->sizes());
+    same_device(D, R_hi, "R_hi");
+    same_device(D, R_lo, "R_lo");
+    same_device(D, lengths_x, "lengths_x");
+    same_device(D, lengths_y, "lengths_y");
+    const c10::cuda::CUDAGuard guard(D.device());
+    const Tensor Rh = R_hi.contiguous(), Rl = R_lo.contiguous();
+    const Tensor lx = prep_lengths(lengths_x), ly = prep_lengths(lengths_y);
+    Tensor E = at::empty({B, N, M}, Rh.options());
+    cudaStream_t stream = at::cuda::getCurrentCUDAStream(D.get_device()).stream();
+    check_status(sdtw_backward_x2(Rh.data_ptr<float>(), Rl.data_ptr<float>(), B, N, M, lx.data_ptr(), ly.data_ptr(),
+                                  lx.scalar_type() == at::kInt, gamma, bandwidth, E.data_ptr<float>(), error_word(Rh),
+                                  stream),
+                 "backward_x2");
+    maybe_sync_check(Rh, stream);
+    if (E.scalar_type() != D.scalar_type()) E = E.to(D.scalar_type());
+    return E;
+}
+
 Tensor error_bits(const Tensor& like)
 {
     // Reads and clears the sticky device error word of like's device (synchronises the current stream).
@@ -420,6 +477,9 @@ TORCH_LIBRARY(torchsoftdtw_b200, m)
     m.def("dist_backward(Tensor X, Tensor Y, Tensor D, Tensor R, Tensor lengths_x, Tensor lengths_y, "
           "Tensor grad_costs, float gamma, int bandwidth, int kind, float eps, bool need_x, bool need_y) "
           "-> (Tensor, Tensor)");
+    m.def("forward_x2(Tensor D, Tensor lengths_x, Tensor lengths_y, float gamma, int bandwidth) -> (Tensor, Tensor, Tensor)");
+    m.def("backward_x2(Tensor D, Tensor R_hi, Tensor R_lo, Tensor lengths_x, Tensor lengths_y, float gamma, "
+          "int bandwidth) -> Tensor");
     m.def("error_bits(Tensor like) -> Tensor");
 }
 
@@ -429,5 +489,7 @@ TORCH_LIBRARY_IMPL(torchsoftdtw_b200, CUDA, m)
     m.impl("l2_backward", &l2_backward_cuda);
     m.impl("dist_forward", &dist_forward_cuda);
     m.impl("dist_backward", &dist_backward_cuda);
+    m.impl("forward_x2", &forward_x2_cuda);
+    m.impl("backward_x2", &backward_x2_cuda);
     m.impl("error_bits", &error_bits);
 }

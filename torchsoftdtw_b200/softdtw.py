@@ -62,6 +62,20 @@ def _l2_forward_fake(X, Y, lengths_x, lengths_y, gamma, bandwidth):
             X.new_empty((B,), dtype=torch.int32))
 
 
+@torch.library.register_fake("torchsoftdtw_b200::forward_x2")
+def _forward_x2_fake(D, lengths_x, lengths_y, gamma, bandwidth):
+    B, N, M = D.shape
+    f32 = torch.float32
+    return (D.new_empty((B,), dtype=f32), D.new_empty((B, N + 2, M + 2), dtype=f32),
+            D.new_empty((B, N + 2, M + 2), dtype=f32))
+
+
+@torch.library.register_fake("torchsoftdtw_b200::backward_x2")
+def _backward_x2_fake(D, R_hi, R_lo, lengths_x, lengths_y, gamma, bandwidth):
+    B, N, M = D.shape
+    return D.new_empty((B, N, M))
+
+
 @torch.library.register_fake("torchsoftdtw_b200::l2_backward")
 def _l2_backward_fake(X, Y, D, R, clamp_flags, lengths_x, lengths_y, grad_costs, gamma, bandwidth, need_x, need_y):
     gX = X.new_empty(X.shape) if need_x else X.new_empty((0,))
@@ -102,6 +116,27 @@ class SoftDTWAutograd(Function):
         D, R, lengths_x, lengths_y = ctx.saved_tensors
         E = torch.ops.torchsoftdtw.backward(D, R, lengths_x, lengths_y, ctx.gamma, ctx.bandwidth)
         return grad_output.unsqueeze(-1).unsqueeze(-1) * E, None, None, None, None
+
+
+class _SoftDTWCompensated(Function):
+    """SoftDTWAutograd over the compensated fp32 ops (R kept as R_hi + R_lo): the better-conditioned fp32
+    backward. Costs in float32, the gradient in D's dtype."""
+
+    @staticmethod
+    @torch.amp.custom_fwd(device_type="cuda")
+    def forward(ctx, D, lengths_x, lengths_y, gamma, bandwidth):
+        costs, R_hi, R_lo = torch.ops.torchsoftdtw_b200.forward_x2(D, lengths_x, lengths_y, gamma, bandwidth)
+        ctx.save_for_backward(D, R_hi, R_lo, lengths_x, lengths_y)
+        ctx.gamma = gamma
+        ctx.bandwidth = bandwidth
+        return costs
+
+    @staticmethod
+    @torch.amp.custom_bwd(device_type="cuda")
+    def backward(ctx, grad_output):
+        D, R_hi, R_lo, lengths_x, lengths_y = ctx.saved_tensors
+        E = torch.ops.torchsoftdtw_b200.backward_x2(D, R_hi, R_lo, lengths_x, lengths_y, ctx.gamma, ctx.bandwidth)
+        return grad_output.unsqueeze(-1).unsqueeze(-1).to(E.dtype) * E, None, None, None, None
 
 
 class _SoftDTWL2(Function):
@@ -167,6 +202,7 @@ def soft_dtw(
     gamma: float = 1.0,
     bandwidth: int = -1,
     dp_dtype: torch.dtype | None = None,
+    compensated: bool = False,
 ) -> torch.Tensor:
     """Compute soft-DTW on a pre-computed cost matrix.
 
@@ -184,6 +220,11 @@ def soft_dtw(
             error of about ulp(R) and, divided by a small gamma, make float32 gradients noisy; in float64
             they do not. Costs and gradients are returned in D's dtype. An addition of this package (the
             reference has no such argument); the default leaves the reference's behaviour unchanged.
+        compensated: for a float32 (or float16 / bfloat16) D, run the dynamic program in compensated float32:
+            R kept as the unevaluated sum of two floats, so the backward's softmin weights come from R
+            differences accurate far below ulp(R). Better-conditioned fp32 gradients without float64
+            arithmetic (float32 costs, the gradient in D's dtype); slower than the default kernels. An addition
+            of this package.
 
     Returns:
         costs: (B,) soft-DTW values.
@@ -193,6 +234,10 @@ def soft_dtw(
         lengths_x = torch.full((B,), N, dtype=torch.long, device=D.device)
     if lengths_y is None:
         lengths_y = torch.full((B,), M, dtype=torch.long, device=D.device)
+    if compensated:
+        if D.dtype == torch.float64:
+            raise ValueError("compensated=True is a float32 option; float64 D needs no compensation")
+        return _SoftDTWCompensated.apply(D, lengths_x, lengths_y, gamma, bandwidth)
     if dp_dtype is not None and dp_dtype != D.dtype:
         return SoftDTWAutograd.apply(D.to(dp_dtype), lengths_x, lengths_y, gamma, bandwidth).to(D.dtype)
     return SoftDTWAutograd.apply(D, lengths_x, lengths_y, gamma, bandwidth)
@@ -206,6 +251,7 @@ class SoftDTW(nn.Module):
         normalize: bool = False,
         distance: str = "l2_squared",
         dp_dtype: torch.dtype | None = None,
+        compensated: bool = False,
     ):
         """
         Args:
@@ -220,6 +266,9 @@ class SoftDTW(nn.Module):
                 ``torch.float64`` with float32 inputs is the better-conditioned option (see ``soft_dtw``):
                 the cost matrix and the dynamic program run in float64 and the costs and gradients come back
                 in the inputs' dtype. Not an argument of the reference; the default keeps its behaviour.
+            compensated: float32 inputs only: the dynamic program in compensated float32 (see ``soft_dtw``), the
+                better-conditioned fp32 backward. The cost matrix is the distance's tensor expression and its
+                gradient flows through torch autograd. Not an argument of the reference.
         """
         super().__init__()
         if distance not in PAIRWISE_DISTANCES:
@@ -229,6 +278,7 @@ class SoftDTW(nn.Module):
         self.normalize = normalize
         self.distance = distance
         self.dp_dtype = dp_dtype
+        self.compensated = compensated
 
     def forward(
         self,
@@ -259,7 +309,10 @@ class SoftDTW(nn.Module):
 
         B = X.size(0)
 
-        if X.is_cuda and Y.is_cuda and X.dtype == Y.dtype:
+        if self.compensated:
+            D = PAIRWISE_DISTANCES[self.distance](X, Y)
+            costs = soft_dtw(D, lengths_x, lengths_y, self.gamma, self.bandwidth, compensated=True)
+        elif X.is_cuda and Y.is_cuda and X.dtype == Y.dtype:
             lx = lengths_x if lengths_x is not None else torch.full((B,), X.size(1), dtype=torch.long, device=X.device)
             ly = lengths_y if lengths_y is not None else torch.full((B,), Y.size(1), dtype=torch.long, device=X.device)
             if self.distance == "l2_squared":
