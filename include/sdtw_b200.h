@@ -41,6 +41,8 @@ typedef int sdtw_status;
 
 #define SDTW_ERR_TIMEOUT 1u    /* a wait on a neighbouring strip's progress ran out (kernel returned early) */
 #define SDTW_ERR_BAD_LENGTH 2u /* some lengths value was outside [0, N] or [0, M] */
+#define SDTW_ERR_BOUNDS 4u     /* debug build (libsdtw_b200_debug.so) only: a kernel's global access fell outside
+                                  its buffer and was skipped */
 
 typedef enum { SDTW_F32 = 0, SDTW_F64 = 1 } sdtw_dtype;
 

@@ -35,6 +35,12 @@ def test_every_header_function_is_exported(lib):
         assert name in _ext.SIGNATURES, f"{name} has no ctypes signature"
 
 
+def test_debug_bounds_library_exports_the_same_functions():
+    dbg = _ext.debug_capi()
+    for name in header_functions():
+        assert hasattr(dbg, name), f"{name} missing from the debug-bounds build"
+
+
 def test_ops_library_links_kernel_library():
     import subprocess
 

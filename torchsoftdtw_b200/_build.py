@@ -3,6 +3,9 @@
 * ``lib/libsdtw_b200.so`` — the CUDA kernel library with the C ABI of ``include/sdtw_b200.h``,
   compiled by nvcc for sm_100a only (``-gencode arch=compute_100a,code=sm_100a``), CUDA runtime linked
   statically so the library carries the runtime its kernels were built with.
+* ``lib/libsdtw_b200_debug.so`` — the same library built with ``-DSDTW_DEBUG_BOUNDS``: the pair-resident
+  wavefront kernels check every global access against its buffer and report one outside as the error bit 4
+  (``SDTW_ERR_BOUNDS``) instead of performing it. A test build, loaded only through ctypes by the tests.
 * ``_C<ext>.so`` — the PyTorch operator layer (``csrc/torch_ops.cpp``), compiled by the host C++
   compiler against libtorch and linked to ``lib/libsdtw_b200.so`` through ``$ORIGIN/lib``.
 
@@ -26,7 +29,9 @@ CSRC = os.path.join(PKG, "csrc")
 INCLUDE = os.path.join(ROOT, "include")
 LIBDIR = os.path.join(PKG, "lib")
 KERNEL_LIB = os.path.join(LIBDIR, "libsdtw_b200.so")
+DEBUG_KERNEL_LIB = os.path.join(LIBDIR, "libsdtw_b200_debug.so")
 OBJDIR = os.path.join(PKG, "_build")
+DEBUG_OBJDIR = os.path.join(PKG, "_build", "debug_bounds")
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 
@@ -64,27 +69,30 @@ def _extra_flags(src: str) -> list[str]:
     return []
 
 
-def build_kernels(force: bool = False) -> str:
-    """nvcc: csrc/*.cu -> lib/libsdtw_b200.so (sm_100a)."""
+def build_kernels(force: bool = False, debug_bounds: bool = False) -> str:
+    """nvcc: csrc/*.cu -> lib/libsdtw_b200.so (sm_100a); with debug_bounds, lib/libsdtw_b200_debug.so."""
+    out = DEBUG_KERNEL_LIB if debug_bounds else KERNEL_LIB
+    objdir = DEBUG_OBJDIR if debug_bounds else OBJDIR
     os.makedirs(LIBDIR, exist_ok=True)
-    os.makedirs(OBJDIR, exist_ok=True)
+    os.makedirs(objdir, exist_ok=True)
     nvcc = os.path.join(_cuda_home(), "bin", "nvcc")
     sources = sorted(glob.glob(os.path.join(CSRC, "*.cu")))
     headers = sorted(glob.glob(os.path.join(CSRC, "*.cuh")) + glob.glob(os.path.join(CSRC, "*.h"))) + [os.path.join(INCLUDE, "sdtw_b200.h")]
+    defs = ["-DSDTW_DEBUG_BOUNDS"] if debug_bounds else []
     objs = []
     jobs = []
     for src in sources:
-        obj = os.path.join(OBJDIR, os.path.basename(src) + ".o")
+        obj = os.path.join(objdir, os.path.basename(src) + ".o")
         objs.append(obj)
         if force or _stale(obj, [src] + headers + [__file__]):
-            jobs.append([nvcc, *ARCH_FLAGS, "-O3", "-lineinfo", "-std=c++17", *_extra_flags(src), "-Xcompiler",
+            jobs.append([nvcc, *ARCH_FLAGS, "-O3", "-lineinfo", "-std=c++17", *defs, *_extra_flags(src), "-Xcompiler",
                          "-fPIC", "-I" + INCLUDE, "-I" + CSRC, "-c", src, "-o", obj])
     if jobs:
         with ThreadPoolExecutor(max_workers=len(jobs)) as ex:
             list(ex.map(_run, jobs))
-    if force or _stale(KERNEL_LIB, objs):
-        _run([nvcc, *ARCH_FLAGS, "-shared", "-cudart", "static", "-o", KERNEL_LIB, *objs])
-    return KERNEL_LIB
+    if force or _stale(out, objs):
+        _run([nvcc, *ARCH_FLAGS, "-shared", "-cudart", "static", "-o", out, *objs])
+    return out
 
 
 def build_ops(force: bool = False) -> str:
@@ -115,6 +123,7 @@ def build_ops(force: bool = False) -> str:
 def build(force: bool = False) -> None:
     build_kernels(force)
     build_ops(force)
+    build_kernels(force, debug_bounds=True)
 
 
 if __name__ == "__main__":

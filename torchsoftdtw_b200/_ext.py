@@ -81,19 +81,37 @@ DEBUG_SIGNATURES: dict[str, tuple] = {
 }
 
 
+def _declare(path: str) -> ctypes.CDLL:
+    lib = ctypes.CDLL(path)
+    for name, (res, args) in {**SIGNATURES, **DEBUG_SIGNATURES}.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    return lib
+
+
 def capi() -> ctypes.CDLL:
     """ctypes handle of lib/libsdtw_b200.so with every C-ABI signature declared."""
     global _capi
     if _capi is None:
         if not os.path.exists(_build.KERNEL_LIB):
             raise ImportError(f"torchsoftdtw_b200: {_build.KERNEL_LIB} is not built")
-        lib = ctypes.CDLL(_build.KERNEL_LIB)
-        for name, (res, args) in {**SIGNATURES, **DEBUG_SIGNATURES}.items():
-            fn = getattr(lib, name)
-            fn.restype = res
-            fn.argtypes = args
-        _capi = lib
+        _capi = _declare(_build.KERNEL_LIB)
     return _capi
+
+
+_debug_capi = None
+
+
+def debug_capi() -> ctypes.CDLL:
+    """ctypes handle of lib/libsdtw_b200_debug.so, the build whose pair-resident kernels check every global
+    access against its buffer (SDTW_ERR_BOUNDS instead of the access). For tests; nothing else loads it."""
+    global _debug_capi
+    if _debug_capi is None:
+        if not os.path.exists(_build.DEBUG_KERNEL_LIB):
+            raise ImportError(f"torchsoftdtw_b200: {_build.DEBUG_KERNEL_LIB} is not built")
+        _debug_capi = _declare(_build.DEBUG_KERNEL_LIB)
+    return _debug_capi
 
 
 def r_tiled(B: int, N: int, M: int, dtype: torch.dtype, device) -> bool:

@@ -47,6 +47,13 @@ constexpr unsigned kFull = 0xffffffffu;
 enum : uint32_t {
     kErrTimeout = 1u,    // a wait on a neighbouring strip's progress ran out
     kErrBadLength = 2u,  // a lengths_x / lengths_y value outside [0, N] / [0, M]
+    kErrBounds = 4u,     // debug builds only: a global access fell outside its buffer (and was skipped)
+};
+
+// A global buffer of `bytes` bytes at `base`: the extent the debug build checks accesses against.
+struct Extent {
+    const void* base;
+    size_t bytes;
 };
 
 // --------------------------------------------------------------------------------------------------
@@ -213,6 +220,28 @@ __device__ __forceinline__ void st_relaxed(double* p, double v)
 }
 __device__ __forceinline__ bool is_absent(float v) { return __float_as_uint(v) == 0xffffffffu; }
 __device__ __forceinline__ bool is_absent(double v) { return __double_as_longlong(v) == -1ll; }
+
+// --------------------------------------------------------------------------------------------------
+// Bounds checks of the debug build (compiled with SDTW_DEBUG_BOUNDS; the library is then built as
+// libsdtw_b200_debug.so). SDTW_IN_BOUNDS(ext, p, n, err) is true when the n bytes at p lie inside the
+// extent; otherwise it sets kErrBounds in the error word `err` and the caller skips the access (a load reads
+// nothing, a store writes nothing): no trap, the context stays usable, the host reads the bit. In the
+// release build the check is the constant true and costs nothing. It stands in for a memory checker where
+// none can run.
+// --------------------------------------------------------------------------------------------------
+__device__ __forceinline__ bool bounds_check(const Extent& x, const void* p, size_t n, uint32_t* err)
+{
+    const char* c = static_cast<const char*>(p);
+    const char* b0 = static_cast<const char*>(x.base);
+    if (b0 != nullptr && c >= b0 && c + n <= b0 + x.bytes) return true;
+    atomicOr(err, kErrBounds);
+    return false;
+}
+#ifdef SDTW_DEBUG_BOUNDS
+#define SDTW_IN_BOUNDS(ext, p, n, err) ::sdtw::bounds_check((ext), (p), (n), (err))
+#else
+#define SDTW_IN_BOUNDS(ext, p, n, err) true
+#endif
 
 __device__ __forceinline__ uint64_t global_ns()
 {

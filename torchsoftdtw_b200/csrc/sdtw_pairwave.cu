@@ -99,6 +99,7 @@ struct PairFwdArgs {
     int64_t B, N, M, bw;
     int S, W, BL, G;  // strips, warps, boundary row length, progress barriers per warp
     T k, gl;
+    Extent xD, xR, xRt, xC;  // buffers, for the debug build's bounds checks
     Sync sy;
     int64_t inject;  // b * S + s: that strip never publishes its boundary row (failure-path test); -1 = none
 };
@@ -106,7 +107,8 @@ struct PairFwdArgs {
 // D rows r0..r0+31, skewed slot of block `blk` (positions 32*blk + lane) <- global, asynchronously. Ring row
 // r holds column c at position c + r + 1. Rows at or beyond `nrows` and columns outside [0, M) are zero-filled.
 template <typename T>
-__device__ __forceinline__ void fwd_pair_load(const T* Db, int64_t M, T* ring, int blk, int nrows, int lane)
+__device__ __forceinline__ void fwd_pair_load(const T* Db, int64_t M, T* ring, int blk, int nrows, int lane,
+                                              const Extent& xD, uint32_t* err)
 {
     constexpr int S = FwdRing<T>::S;
     T* dst = ring + (blk & 1) * 32 + lane;
@@ -115,12 +117,15 @@ __device__ __forceinline__ void fwd_pair_load(const T* Db, int64_t M, T* ring, i
         const T* src = Db + c0;
         const int64_t step = M - 1;  // a compile-time constant in the kernels specialized on M
 #pragma unroll
-        for (int r = 0; r < 32; ++r)
-            cp_async_scalar<sizeof(T)>(dst + r * S, src + r * step, static_cast<int>(sizeof(T)));
+        for (int r = 0; r < 32; ++r) {
+            const bool ok = SDTW_IN_BOUNDS(xD, src + r * step, sizeof(T), err);
+            cp_async_scalar<sizeof(T)>(dst + r * S, ok ? src + r * step : Db, ok ? static_cast<int>(sizeof(T)) : 0);
+        }
     } else {
         for (int r = 0; r < 32; ++r) {
             const int c = c0 - r;
-            const bool in = r < nrows && c >= 0 && c < M;
+            bool in = r < nrows && c >= 0 && c < M;
+            if (in) in = SDTW_IN_BOUNDS(xD, Db + static_cast<int64_t>(r) * M + c, sizeof(T), err);
             cp_async_scalar<sizeof(T)>(dst + r * S, in ? Db + static_cast<int64_t>(r) * M + c : Db,
                                        in ? static_cast<int>(sizeof(T)) : 0);
         }
@@ -130,7 +135,7 @@ __device__ __forceinline__ void fwd_pair_load(const T* Db, int64_t M, T* ring, i
 // Finished slot of block `blk` -> R (padded layout; Rrow = padded row of DP row r0), rows < nmat.
 template <typename T>
 __device__ __forceinline__ void fwd_pair_store(T* Rrow, int64_t pitch, int64_t M, const T* ring, int blk, int nmat,
-                                               int lane)
+                                               int lane, const Extent& xR, uint32_t* err)
 {
     constexpr int S = FwdRing<T>::S;
     const T* src = ring + (blk & 1) * 32 + lane;
@@ -139,11 +144,13 @@ __device__ __forceinline__ void fwd_pair_store(T* Rrow, int64_t pitch, int64_t M
         T* dst = Rrow + c0 + 1;
         const int64_t step = pitch - 1;
 #pragma unroll
-        for (int r = 0; r < 32; ++r) dst[r * step] = src[r * S];
+        for (int r = 0; r < 32; ++r)
+            if (SDTW_IN_BOUNDS(xR, dst + r * step, sizeof(T), err)) dst[r * step] = src[r * S];
     } else {
         for (int r = 0; r < nmat; ++r) {
             const int c = c0 - r;
-            if (c >= 0 && c < M) Rrow[r * pitch + c + 1] = src[r * S];
+            if (c >= 0 && c < M && SDTW_IN_BOUNDS(xR, Rrow + r * pitch + c + 1, sizeof(T), err))
+                Rrow[r * pitch + c + 1] = src[r * S];
         }
     }
 }
@@ -200,7 +207,8 @@ __device__ __forceinline__ bool fbar_wait_fast(uint32_t bar, uint32_t parity, co
 // Finished slot of block `blk` -> its 32 x 32 tile (module path): 16-byte pieces, each store instruction writing
 // whole 128-byte tile rows (4 rows of floats, 2 of doubles), read from the ring row by row.
 template <typename T>
-__device__ __forceinline__ void fwd_tile_store(T* tile, const T* ring, int blk, int lane)
+__device__ __forceinline__ void fwd_tile_store(T* tile, const T* ring, int blk, int lane, const Extent& xRt,
+                                               uint32_t* err)
 {
     constexpr int RS = FwdRing<T>::S;
     constexpr int EPP = 16 / sizeof(T);  // elements per piece
@@ -212,7 +220,7 @@ __device__ __forceinline__ void fwd_tile_store(T* tile, const T* ring, int blk, 
 #pragma unroll
     for (int i = 0; i < 32; i += RPI) {
         const uint4 v = *reinterpret_cast<const uint4*>(src + i * RS);
-        *reinterpret_cast<uint4*>(dst + i * 32) = v;
+        if (SDTW_IN_BOUNDS(xRt, dst + i * 32, 16, err)) *reinterpret_cast<uint4*>(dst + i * 32) = v;
     }
 }
 
@@ -287,7 +295,7 @@ __device__ bool fwd_pair_strip(const PairFwdArgs<T>& a, T* ring, const T* bin, u
     T* Rrow = tiles ? nullptr : a.R + b * (N + 2) * pitch + static_cast<int64_t>(r0 + 1) * pitch;
     Strip st;
     if (!make_strip(st, a.len, b, s, N, M, a.bw, lane)) {
-        if (s == 0 && lane == 0) {
+        if (s == 0 && lane == 0 && SDTW_IN_BOUNDS(a.xC, a.costs + b, sizeof(T), a.sy.err)) {
             if (st.bad) {
                 atomicOr(a.sy.err, kErrBadLength);
                 a.costs[b] = Num<T>::nan();
@@ -297,7 +305,8 @@ __device__ bool fwd_pair_strip(const PairFwdArgs<T>& a, T* ring, const T* bin, u
         }
         if (!tiles)
             for (int r = 0; r < nmat; ++r)
-                for (int c = lane; c < M + 2; c += 32) Rrow[r * pitch + c] = INF;
+                for (int c = lane; c < M + 2; c += 32)
+                    if (SDTW_IN_BOUNDS(a.xR, Rrow + r * pitch + c, sizeof(T), a.sy.err)) Rrow[r * pitch + c] = INF;
         // No barrier arrivals: every later strip of this pair is empty too, so nothing waits on this
         // warp's barriers again (arriving here could lap the phase the strip below the previous round
         // is still waiting for).
@@ -314,7 +323,7 @@ __device__ bool fwd_pair_strip(const PairFwdArgs<T>& a, T* ring, const T* bin, u
 
     cp_async_wait<0>();
     __syncwarp();
-    fwd_pair_load<T>(Db, M, ring, k0, st.rows, lane);
+    fwd_pair_load<T>(Db, M, ring, k0, st.rows, lane, a.xD, a.sy.err);
     cp_async_commit();
 
     if (!tiles) {
@@ -326,8 +335,10 @@ __device__ bool fwd_pair_strip(const PairFwdArgs<T>& a, T* ring, const T* bin, u
             pe = pe < 0 ? 0 : pe;
             int ss = 32 * k1 + 32 - r;
             ss = ss > M + 1 ? static_cast<int>(M + 1) : ss;
-            for (int c = lane; c <= pe; c += 32) row[c] = INF;
-            for (int c = ss + lane; c < M + 2; c += 32) row[c] = INF;
+            for (int c = lane; c <= pe; c += 32)
+                if (SDTW_IN_BOUNDS(a.xR, row + c, sizeof(T), a.sy.err)) row[c] = INF;
+            for (int c = ss + lane; c < M + 2; c += 32)
+                if (SDTW_IN_BOUNDS(a.xR, row + c, sizeof(T), a.sy.err)) row[c] = INF;
         }
     }
 
@@ -363,7 +374,7 @@ __device__ bool fwd_pair_strip(const PairFwdArgs<T>& a, T* ring, const T* bin, u
         if (!ok) return false;
         if (blk + 1 <= k1) {
             __syncwarp();
-            fwd_pair_load<T>(Db, M, ring, blk + 1, st.rows, lane);
+            fwd_pair_load<T>(Db, M, ring, blk + 1, st.rows, lane, a.xD, a.sy.err);
         }
         cp_async_commit();
         ok = full ? fwd_pair_block<T, false, 1, 3>(cell, top, last, bout, tau0, A, Z, a.k, a.gl, wait_in, bars_in,
@@ -375,10 +386,11 @@ __device__ bool fwd_pair_strip(const PairFwdArgs<T>& a, T* ring, const T* bin, u
         if (!ok) return false;
         __syncwarp();
         if (tiles)
-            fwd_tile_store<T>(tile0 + static_cast<int64_t>(blk) * 1024, ring, blk, lane);
+            fwd_tile_store<T>(tile0 + static_cast<int64_t>(blk) * 1024, ring, blk, lane, a.xRt, a.sy.err);
         else
-            fwd_pair_store<T>(Rrow, pitch, M, ring, blk, nmat, lane);
-        if (blk == bstar && lane == lstar) a.costs[b] = cell[tstar - tau0];
+            fwd_pair_store<T>(Rrow, pitch, M, ring, blk, nmat, lane, a.xR, a.sy.err);
+        if (blk == bstar && lane == lstar && SDTW_IN_BOUNDS(a.xC, a.costs + b, sizeof(T), a.sy.err))
+            a.costs[b] = cell[tstar - tau0];
     }
     if (!skip) {
         // The strip below may read columns past this sweep as its row above: they are out of band (+inf).
@@ -419,8 +431,9 @@ __global__ void __launch_bounds__(SDTW_PAIR_THREADS, SDTW_PAIR_MIN_CTAS) sdtw_fw
     if (a.Rt == nullptr) {
         T* Rb = a.R + b * (a.N + 2) * (a.M + 2);
         for (int64_t e = threadIdx.x; e < a.M + 2; e += blockDim.x) {
-            Rb[e] = e == 0 ? T(0) : INF;
-            Rb[(a.N + 1) * (a.M + 2) + e] = INF;
+            if (SDTW_IN_BOUNDS(a.xR, Rb + e, sizeof(T), a.sy.err)) Rb[e] = e == 0 ? T(0) : INF;
+            T* last_row = Rb + (a.N + 1) * (a.M + 2) + e;
+            if (SDTW_IN_BOUNDS(a.xR, last_row, sizeof(T), a.sy.err)) *last_row = INF;
         }
     }
     __syncthreads();
@@ -460,13 +473,15 @@ struct PairBwdArgs {
     int64_t B, N, M, bw;
     int S, W, BL, G;  // strips, warps, boundary row length, progress barriers per warp
     T k;
+    Extent xR, xRt, xE;  // buffers, for the debug build's bounds checks
     Sync sy;
     int64_t inject;
 };
 
 // Padded R rows r0 .. r0+32 (DP rows r0-1 .. r0+31), skewed slot of block `blk` <- global.
 template <typename T>
-__device__ __forceinline__ void bwd_pair_load(const T* Rb, int64_t N, int64_t M, T* ring, int blk, int r0, int lane)
+__device__ __forceinline__ void bwd_pair_load(const T* Rb, int64_t N, int64_t M, T* ring, int blk, int r0, int lane,
+                                              const Extent& xR, uint32_t* err)
 {
     constexpr int S = BwdRing<T>::S;
     const int64_t pitch = M + 2;
@@ -477,13 +492,15 @@ __device__ __forceinline__ void bwd_pair_load(const T* Rb, int64_t N, int64_t M,
         const int64_t step = pitch - 1;
 #pragma unroll 11
         for (int p = 0; p < 33; ++p) {
-            cp_async_scalar<sizeof(T)>(dst + p * S, src, static_cast<int>(sizeof(T)));
+            const bool ok = SDTW_IN_BOUNDS(xR, src, sizeof(T), err);
+            cp_async_scalar<sizeof(T)>(dst + p * S, ok ? src : Rb, ok ? static_cast<int>(sizeof(T)) : 0);
             src += step;
         }
     } else {
         for (int p = 0; p < 33; ++p) {
             const int pc = c0 - p + 1;  // padded column
-            const bool in = r0 + p <= N + 1 && pc >= 0 && pc <= M + 1;
+            bool in = r0 + p <= N + 1 && pc >= 0 && pc <= M + 1;
+            if (in) in = SDTW_IN_BOUNDS(xR, Rb + static_cast<int64_t>(r0 + p) * pitch + pc, sizeof(T), err);
             cp_async_scalar<sizeof(T)>(dst + p * S, in ? Rb + static_cast<int64_t>(r0 + p) * pitch + pc : Rb,
                                        in ? static_cast<int>(sizeof(T)) : 0);
         }
@@ -508,14 +525,20 @@ __device__ __forceinline__ void bwd_tile_load(const PairBwdArgs<T>& a, T* ring, 
     if (blk >= kf0 && blk <= kf1) {
         const T* src = a.Rt + (((b * a.S + s) * static_cast<int64_t>(a.NBt) + blk) * 32 + lane) * 32;
 #pragma unroll
-        for (int i = 0; i < 32; i += EPP) cp_async_16(row + i, src + i, 16);
+        for (int i = 0; i < 32; i += EPP) {
+            const bool ok = SDTW_IN_BOUNDS(a.xRt, src + i, 16, a.sy.err);
+            cp_async_16(row + i, ok ? src + i : a.Rt, ok ? 16 : 0);
+        }
     } else {
 #pragma unroll
         for (int i = 0; i < 32; ++i) row[i] = INF;
     }
     if (s > 0 && blk + 1 >= kp0 && blk + 1 <= kp1) {
         const T* src = a.Rt + (((b * a.S + s - 1) * static_cast<int64_t>(a.NBt) + blk + 1) * 32 + 31) * 32;
-        if (lane < 32 / EPP) cp_async_16(slot + lane * EPP, src + lane * EPP, 16);
+        if (lane < 32 / EPP) {
+            const bool ok = SDTW_IN_BOUNDS(a.xRt, src + lane * EPP, 16, a.sy.err);
+            cp_async_16(slot + lane * EPP, ok ? src + lane * EPP : a.Rt, ok ? 16 : 0);
+        }
     } else {
         slot[lane] = (s == 0 && blk == -1 && lane == 31) ? T(0) : INF;
     }
@@ -524,7 +547,8 @@ __device__ __forceinline__ void bwd_tile_load(const PairBwdArgs<T>& a, T* ring, 
 // E of slot `blk` -> global (Erow = E row of DP row r0): ring row r + 1 holds E[r0 + r][c] at position c + r.
 // Every position of the slot was written by the block's sweep (zeros where a step was outside the band).
 template <typename T>
-__device__ __forceinline__ void bwd_pair_store(T* Erow, int64_t M, const T* ring, int blk, int nmat, int lane)
+__device__ __forceinline__ void bwd_pair_store(T* Erow, int64_t M, const T* ring, int blk, int nmat, int lane,
+                                               const Extent& xE, uint32_t* err)
 {
     constexpr int S = BwdRing<T>::S;
     const T* src = ring + S + (blk & 1) * 32 + lane;
@@ -534,13 +558,13 @@ __device__ __forceinline__ void bwd_pair_store(T* Erow, int64_t M, const T* ring
         const int64_t step = M - 1;
 #pragma unroll 8
         for (int r = 0; r < 32; ++r) {
-            *dst = src[r * S];
+            if (SDTW_IN_BOUNDS(xE, dst, sizeof(T), err)) *dst = src[r * S];
             dst += step;
         }
     } else {
         for (int r = 0; r < nmat; ++r) {
             const int c = c0 - r;
-            if (c >= 0 && c < M) Erow[r * M + c] = src[r * S];
+            if (c >= 0 && c < M && SDTW_IN_BOUNDS(xE, Erow + r * M + c, sizeof(T), err)) Erow[r * M + c] = src[r * S];
         }
     }
 }
@@ -647,7 +671,8 @@ __device__ bool bwd_pair_strip(const PairBwdArgs<T>& a, T* ring, const T* bin, u
     if (!make_strip(st, a.len, b, s, N, M, a.bw, lane)) {
         if (st.bad && s == 0 && lane == 0) atomicOr(a.sy.err, kErrBadLength);
         for (int r = 0; r < nmat; ++r)
-            for (int c = lane; c < M; c += 32) Erow[r * M + c] = T(0);
+            for (int c = lane; c < M; c += 32)
+                if (SDTW_IN_BOUNDS(a.xE, Erow + r * M + c, sizeof(T), a.sy.err)) Erow[r * M + c] = T(0);
         // Empty strips (rows past the pair's length) come first in the bottom-up order, and their warps sweep
         // non-empty strips in later rounds: complete every barrier once here too, so that a warp's barrier
         // phases keep counting its rounds (nothing waits on these arrivals: the strip above an empty strip
@@ -681,13 +706,13 @@ __device__ bool bwd_pair_strip(const PairBwdArgs<T>& a, T* ring, const T* bin, u
     if (tiles)
         bwd_tile_load<T>(a, ring, k1, b, s, kf0, kf1, kp0, kp1, lane);
     else
-        bwd_pair_load<T>(Rb, N, M, ring, k1, r0, lane);
+        bwd_pair_load<T>(Rb, N, M, ring, k1, r0, lane, a.xR, a.sy.err);
     cp_async_commit();
     if (k1 - 1 >= kmin) {
         if (tiles)
             bwd_tile_load<T>(a, ring, k1 - 1, b, s, kf0, kf1, kp0, kp1, lane);
         else
-            bwd_pair_load<T>(Rb, N, M, ring, k1 - 1, r0, lane);
+            bwd_pair_load<T>(Rb, N, M, ring, k1 - 1, r0, lane, a.xR, a.sy.err);
     }
     cp_async_commit();
 
@@ -698,8 +723,10 @@ __device__ bool bwd_pair_strip(const PairBwdArgs<T>& a, T* ring, const T* bin, u
         pe = pe < 0 ? 0 : (pe > M ? static_cast<int>(M) : pe);
         int ss = 32 * k1 + 32 - r;
         ss = ss > M ? static_cast<int>(M) : ss;
-        for (int c = lane; c < pe; c += 32) row[c] = T(0);
-        for (int c = ss + lane; c < M; c += 32) row[c] = T(0);
+        for (int c = lane; c < pe; c += 32)
+            if (SDTW_IN_BOUNDS(a.xE, row + c, sizeof(T), a.sy.err)) row[c] = T(0);
+        for (int c = ss + lane; c < M; c += 32)
+            if (SDTW_IN_BOUNDS(a.xE, row + c, sizeof(T), a.sy.err)) row[c] = T(0);
     }
 
     T sendv = T(0), pend = T(0), acc = seed;
@@ -730,13 +757,13 @@ __device__ bool bwd_pair_strip(const PairBwdArgs<T>& a, T* ring, const T* bin, u
                                                       pend, acc, bcar);
         if (!ok) return false;
         __syncwarp();
-        bwd_pair_store<T>(Erow, M, ring, blk, nmat, lane);
+        bwd_pair_store<T>(Erow, M, ring, blk, nmat, lane, a.xE, a.sy.err);
         __syncwarp();
         if (blk - 2 >= kmin) {
             if (tiles)
                 bwd_tile_load<T>(a, ring, blk - 2, b, s, kf0, kf1, kp0, kp1, lane);
             else
-                bwd_pair_load<T>(Rb, N, M, ring, blk - 2, r0, lane);
+                bwd_pair_load<T>(Rb, N, M, ring, blk - 2, r0, lane, a.xR, a.sy.err);
         }
         cp_async_commit();
     }
@@ -869,6 +896,12 @@ cudaError_t pair_forward(const T* D, T* R, T* Rt, T* costs, const void* lx, cons
     a.R = R;
     a.Rt = Rt;
     a.NBt = pair_tile_blocks(M);
+    const size_t es = sizeof(T);
+    const int64_t S = N > 0 ? (N + 31) / 32 : 1;
+    a.xD = Extent{D, static_cast<size_t>(B * N * M) * es};
+    a.xR = Extent{R, R ? static_cast<size_t>(B * (N + 2) * (M + 2)) * es : 0};
+    a.xRt = Extent{Rt, Rt ? static_cast<size_t>(B * S * a.NBt) * 1024 * es : 0};
+    a.xC = Extent{costs, static_cast<size_t>(B) * es};
     a.costs = costs;
     a.len = Lengths{lx, ly, is32};
     a.B = B;
@@ -905,6 +938,11 @@ cudaError_t pair_backward(const T* R, const T* Rt, T* E, const void* lx, const v
     a.R = R;
     a.Rt = Rt;
     a.NBt = pair_tile_blocks(M);
+    const size_t es = sizeof(T);
+    const int64_t S = N > 0 ? (N + 31) / 32 : 1;
+    a.xR = Extent{R, R ? static_cast<size_t>(B * (N + 2) * (M + 2)) * es : 0};
+    a.xRt = Extent{Rt, Rt ? static_cast<size_t>(B * S * a.NBt) * 1024 * es : 0};
+    a.xE = Extent{E, static_cast<size_t>(B * N * M) * es};
     a.E = E;
     a.len = Lengths{lx, ly, is32};
     a.B = B;
