@@ -354,35 +354,25 @@ __device__ bool fwd_pair_strip(const PairFwdArgs<T>& a, T* ring, const T* bin, u
     T outp = INF;
     const int src_lane = (lane + 31) & 31;
 
-    // D of the first block is in flight; the loop prefetches D of block blk + 1 after the first group of block
-    // blk, into the slot of block blk - 1 (whose R was written back at the end of that block).
+    // D of the first block is in flight; each block prefetches D of the next one into the other slot as it
+    // starts (that slot's R was written back, synchronously, at the end of the block before).
 #pragma unroll 1
     for (int blk = k0; blk <= k1; ++blk) {
         cp_async_wait<0>();
         __syncwarp();
+        if (blk + 1 <= k1) fwd_pair_load<T>(Db, M, ring, blk + 1, st.rows, lane, a.xD, a.sy.err);
+        cp_async_commit();
         const int tau0 = 32 * blk;
         T* cell = ring + lane * RS + (blk & 1) * 32;
         const T* top = bin + tau0 + kBufPad;
         const T* last = ring + 31 * RS + (blk & 1) * 32;  // the strip's last row, positions tau0 ..
-        const bool full = tau0 >= Amax && tau0 + 31 <= Zmin;
-        bool ok = full ? fwd_pair_block<T, false, 0, 0>(cell, top, last, bout, tau0, A, Z, a.k, a.gl, wait_in, bars_in,
-                                                        par_in, glast, !skip, has_consumer, bars_out, a.sy, src_lane,
-                                                        lane, outp, upp)
-                       : fwd_pair_block<T, true, 0, 0>(cell, top, last, bout, tau0, A, Z, a.k, a.gl, wait_in, bars_in,
-                                                       par_in, glast, !skip, has_consumer, bars_out, a.sy, src_lane,
-                                                       lane, outp, upp);
-        if (!ok) return false;
-        if (blk + 1 <= k1) {
-            __syncwarp();
-            fwd_pair_load<T>(Db, M, ring, blk + 1, st.rows, lane, a.xD, a.sy.err);
-        }
-        cp_async_commit();
-        ok = full ? fwd_pair_block<T, false, 1, 3>(cell, top, last, bout, tau0, A, Z, a.k, a.gl, wait_in, bars_in,
-                                                   par_in, glast, !skip, has_consumer, bars_out, a.sy, src_lane, lane,
-                                                   outp, upp)
-                  : fwd_pair_block<T, true, 1, 3>(cell, top, last, bout, tau0, A, Z, a.k, a.gl, wait_in, bars_in,
-                                                  par_in, glast, !skip, has_consumer, bars_out, a.sy, src_lane, lane,
-                                                  outp, upp);
+        const bool ok = (tau0 >= Amax && tau0 + 31 <= Zmin)
+                            ? fwd_pair_block<T, false, 0, 3>(cell, top, last, bout, tau0, A, Z, a.k, a.gl, wait_in,
+                                                             bars_in, par_in, glast, !skip, has_consumer, bars_out,
+                                                             a.sy, src_lane, lane, outp, upp)
+                            : fwd_pair_block<T, true, 0, 3>(cell, top, last, bout, tau0, A, Z, a.k, a.gl, wait_in,
+                                                            bars_in, par_in, glast, !skip, has_consumer, bars_out,
+                                                            a.sy, src_lane, lane, outp, upp);
         if (!ok) return false;
         __syncwarp();
         if (tiles)
@@ -391,6 +381,7 @@ __device__ bool fwd_pair_strip(const PairFwdArgs<T>& a, T* ring, const T* bin, u
             fwd_pair_store<T>(Rrow, pitch, M, ring, blk, nmat, lane, a.xR, a.sy.err);
         if (blk == bstar && lane == lstar && SDTW_IN_BOUNDS(a.xC, a.costs + b, sizeof(T), a.sy.err))
             a.costs[b] = cell[tstar - tau0];
+        __syncwarp();
     }
     if (!skip) {
         // The strip below may read columns past this sweep as its row above: they are out of band (+inf).
