@@ -63,6 +63,11 @@ SIGNATURES: dict[str, tuple] = {
     "sdtw_r_tiles_elems": (_i64, [_i64, _i64, _i64]),
     "sdtw_forward_tiles": (_i, [_i, _p, _i64, _i64, _i64, _p, _p, _i, _d, _i64, _p, _p, _p, _sz, _p, _p]),
     "sdtw_backward_tiles": (_i, [_i, _p, _i64, _i64, _i64, _p, _p, _i, _d, _i64, _p, _p, _sz, _p, _p]),
+    "sdtw_forward_l2_fused_ok": (_i, [_i64, _i64, _i64, _i64]),
+    "sdtw_clamp_mask_words": (_i64, [_i64, _i64, _i64]),
+    "sdtw_forward_l2_tiles": (_i, [_p, _p, _i64, _i64, _i64, _i64, _p, _p, _i, _d, _i64, _p, _p, _p, _p, _p, _sz, _p,
+                                   _p]),
+    "sdtw_apply_clamp_mask": (_i, [_p, _p, _p, _i64, _i64, _i64, _p]),
     "sdtw_forward_x2": (_i, [_p, _i64, _i64, _i64, _p, _p, _i, _d, _i64, _p, _p, _p, _p, _p]),
     "sdtw_backward_x2": (_i, [_p, _p, _i64, _i64, _i64, _p, _p, _i, _d, _i64, _p, _p, _p]),
     "sdtw_pairwise_l2": (_i, [_i, _p, _p, _i64, _i64, _i64, _i64, _p, _p, _p]),
@@ -124,3 +129,22 @@ def r_tiled(B: int, N: int, M: int, dtype: torch.dtype, device) -> bool:
         return False
     with torch.cuda.device(dev):
         return bool(capi().sdtw_r_tiled(B, N, M, 1 if dtype == torch.float64 else 0))
+
+
+FUSED_COST_ENV = "TORCHSOFTDTW_B200_FUSED_COST"
+
+
+def l2_fused(B: int, N: int, M: int, d: int, dtype: torch.dtype, device) -> bool:
+    """Whether ``torchsoftdtw_b200::l2_forward`` computes the cost matrix inside the forward wavefront
+    (sdtw_forward_l2_tiles) instead of storing it: only with ``TORCHSOFTDTW_B200_FUSED_COST=1`` in the
+    environment, for fp32 shapes the library accepts (sdtw_forward_l2_fused_ok). The op's third output is
+    then the clamp mask in place of D. The op layer reads the same variable on every call."""
+    if os.environ.get(FUSED_COST_ENV, "0") in ("", "0") or dtype != torch.float32:
+        return False
+    if B <= 0 or N <= 0 or M <= 0 or d <= 0:
+        return False
+    dev = torch.device(device)
+    if dev.type != "cuda":
+        return False
+    with torch.cuda.device(dev):
+        return bool(capi().sdtw_forward_l2_fused_ok(B, N, M, d))

@@ -88,6 +88,28 @@ struct FwdRing {
     static constexpr int S = sizeof(T) == 4 ? 68 : 66;
 };
 
+// Fused forward: byte offset of the |y|^2 array in shared memory (after the rings, boundary rows, scratch and
+// barriers of pair_fwd_smem_bytes<float>), and the CTA's total.
+inline __host__ __device__ size_t fused_y2_offset(int W, int64_t M)
+{
+    const size_t end = (static_cast<size_t>(W) * (32 * FwdRing<float>::S + 32) + static_cast<size_t>(W + 1) * buf_len(M)) *
+                           sizeof(float) +
+                       8 + static_cast<size_t>(W) * fwd_groups(M) * 8;
+    return (end + 15) / 16 * 16;
+}
+inline size_t fused_smem_bytes(int W, int64_t M) { return fused_y2_offset(W, M) + static_cast<size_t>(M + 96) * 4; }
+
+// Inputs of the fused squared-L2 forward (the cost matrix computed inside the wavefront, never stored).
+struct FusedL2 {
+    const float* X;   // (B, N, d)
+    const float* Y;   // (B, M, d)
+    int d;            // a multiple of 16
+    uint32_t* cmask;  // (B, N, MW): bit c % 32 of word c / 32 set where the clamp at 0 was active
+    int* cflags;      // (B,): set for pairs with a clamped cell
+    int MW;
+    Extent xX, xY, xMask, xFlags;
+};
+
 template <typename T>
 struct PairFwdArgs {
     const T* D;
@@ -102,7 +124,120 @@ struct PairFwdArgs {
     Extent xD, xR, xRt, xC;  // buffers, for the debug build's bounds checks
     Sync sy;
     int64_t inject;  // b * S + s: that strip never publishes its boundary row (failure-path test); -1 = none
+    FusedL2 f;       // the fused kernel's inputs (D unused)
 };
+
+// ---- cost rectangles of the fused squared-L2 forward ------------------------------------------------------
+// D = (|x|^2 + |y|^2) - 2 x.y clamped at 0, the form of distances.py:14-18, with x.y from 3xTF32 warp MMAs:
+// each operand splits into a head (the nearest TF32 value) and a tail (the nearest TF32 value of the
+// remainder), the split of the tcgen05 cost kernel, and x.y = head.head + head.tail + tail.head; the
+// tail.tail term left out is below 2^-22 of |x||y| and has no fixed sign after round-to-nearest, so the
+// products of identical rows land on either side of |x|^2 like an fp32 dot product does.
+__device__ __forceinline__ void mma_tf32(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1)
+{
+    asm("mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%0, %1, %2, %3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ void tf32_split(float v, uint32_t& hi, uint32_t& lo)
+{
+    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(hi) : "f"(v));
+    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(lo) : "f"(v - __uint_as_float(hi)));
+}
+__device__ __forceinline__ float f4c(const float4& v, int i) { return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w; }
+
+// D of the 32 x 32 rectangle rows r0 .. r0+31, columns 32K .. 32K+31 of one pair -> the forward ring: element
+// (r, c) at position (c + r + 1) mod 64 of ring row r, the position the forward sweep reads it at. Xs: row r0 of
+// X; Yb: row 0 of Y; x2[i]: |x|^2 of row r0 + lane/4 + 8i; y2: |y|^2 by column (zero outside [0, M), 32 before
+// column 0 and 64 after M-1 readable). Rows past N and columns outside [0, M) read zero operands; the sweep
+// masks those cells. A clamp of a cell inside the matrix sets its bit in the pair's clamp mask and its flag.
+//
+// Fragment layout (mma.m16n8k8 .tf32): lane = 4 g + t holds A rows g, g+8 at k = t, t+4, B column g at
+// k = t, t+4, and C rows g, g+8 at columns 2t, 2t+1. The 8 k of MMA step 2p+ks are the feature dimensions
+// 16p + 4t + 2ks + {0, 1} (k = t -> +0, k = t+4 -> +1): a permutation of the 16 dimensions of chunk p that is
+// the same for both operands, so each lane loads its operands as whole 16-byte vectors.
+__device__ __forceinline__ void fused_rect(const FusedL2& f, float* ring, const float* Xs, const float* Yb,
+                                           const float (&x2)[4], const float* y2, int64_t b, int r0, int64_t N,
+                                           int64_t M, int K, int lane, uint32_t* err)
+{
+    constexpr int RS = FwdRing<float>::S;
+    const int g = lane >> 2, t = lane & 3, d = f.d;
+    const int cb = 32 * K;
+    // Operand rows: rows past N and columns outside [0, M) read a row of the matrix instead (any finite
+    // value will do, the sweep masks those cells), so the loads need no predicate.
+    int xo[4], yo[4];  // element offsets from Xs and Yb
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int64_t row = min(static_cast<int64_t>(r0 + g + 8 * i), N - 1) - r0;
+        xo[i] = static_cast<int>(row * d) + 4 * t;
+        const int64_t col = min(static_cast<int64_t>(max(cb + 8 * i + g, 0)), M - 1);
+        yo[i] = static_cast<int>(col * d) + 4 * t;
+    }
+    float acc[2][4][4];
+#pragma unroll
+    for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+        for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+            for (int c = 0; c < 4; ++c) acc[mt][nt][c] = 0.f;
+#pragma unroll 1
+    for (int p = 0; p < d / 16; ++p) {
+        float4 xa[4], yb[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float4* xq = reinterpret_cast<const float4*>(Xs + xo[i] + 16 * p);
+            const float4* yq = reinterpret_cast<const float4*>(Yb + yo[i] + 16 * p);
+            xa[i] = SDTW_IN_BOUNDS(f.xX, xq, 16, err) ? __ldg(xq) : make_float4(0.f, 0.f, 0.f, 0.f);
+            yb[i] = SDTW_IN_BOUNDS(f.xY, yq, 16, err) ? __ldg(yq) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int ks = 0; ks < 2; ++ks) {
+            uint32_t ah[4][2], al[4][2];  // [row set][k = t, t + 4]
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int h = 0; h < 2; ++h) tf32_split(f4c(xa[i], 2 * ks + h), ah[i][h], al[i][h]);
+#pragma unroll
+            for (int nt = 0; nt < 4; ++nt) {
+                uint32_t bh[2], bl[2];
+#pragma unroll
+                for (int h = 0; h < 2; ++h) tf32_split(f4c(yb[nt], 2 * ks + h), bh[h], bl[h]);
+#pragma unroll
+                for (int mt = 0; mt < 2; ++mt) {
+                    mma_tf32(acc[mt][nt], al[2 * mt][0], al[2 * mt + 1][0], al[2 * mt][1], al[2 * mt + 1][1], bh[0],
+                             bh[1]);
+                    mma_tf32(acc[mt][nt], ah[2 * mt][0], ah[2 * mt + 1][0], ah[2 * mt][1], ah[2 * mt + 1][1], bl[0],
+                             bl[1]);
+                    mma_tf32(acc[mt][nt], ah[2 * mt][0], ah[2 * mt + 1][0], ah[2 * mt][1], ah[2 * mt + 1][1], bh[0],
+                             bh[1]);
+                }
+            }
+        }
+    }
+#pragma unroll
+    for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+        for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                const int r = 16 * mt + g + 8 * (c >> 1);
+                const int cc = 8 * nt + 2 * t + (c & 1);
+                float v = (x2[2 * mt + (c >> 1)] + y2[cb + cc]) - 2.f * acc[mt][nt][c];
+                if (v < 0.f) {
+                    const int64_t row = r0 + r;
+                    const int col = cb + cc;
+                    if (row < N && col >= 0 && col < M) {
+                        uint32_t* w = f.cmask + (b * N + row) * f.MW + (col >> 5);
+                        if (SDTW_IN_BOUNDS(f.xMask, w, 4, err)) atomicOr(w, 1u << (col & 31));
+                        if (SDTW_IN_BOUNDS(f.xFlags, f.cflags + b, 4, err)) f.cflags[b] = 1;
+                    }
+                    v = 0.f;
+                }
+                ring[r * RS + ((cb + cc + r + 1) & 63)] = v;
+            }
+}
 
 // D rows r0..r0+31, skewed slot of block `blk` (positions 32*blk + lane) <- global, asynchronously. Ring row
 // r holds column c at position c + r + 1. Rows at or beyond `nrows` and columns outside [0, M) are zero-filled.
@@ -282,9 +417,13 @@ __device__ __forceinline__ bool fwd_pair_block(T* cell, const T* top, const T* l
 // strip-ticket kernels: a block's slot then holds, for row l, exactly the columns 32*blk + x - l - 1 that the
 // backward's ring row l + 1 needs at its positions 32*blk + x, so that R can travel between the two as whole
 // 32 x 32 tiles (PairFwdArgs::Rt). The boundary rows are indexed by column + kBufPad + 1.
-template <typename T, int MC>
+//
+// FUSED (float only, tiles only): D comes from fused_rect instead of a.D. Rectangle K lands in the slots of
+// blocks K and K + 1, so it is computed after block K - 1 has written back its slot and before block K starts
+// (rectangles k0 - 1 and k0 before the first block).
+template <typename T, int MC, bool FUSED>
 __device__ bool fwd_pair_strip(const PairFwdArgs<T>& a, T* ring, const T* bin, uint32_t bars_in, uint32_t par_in,
-                               T* bout, uint32_t bars_out, int64_t b, int s, int lane)
+                               T* bout, uint32_t bars_out, const float* y2, int64_t b, int s, int lane)
 {
     constexpr int RS = FwdRing<T>::S;
     const T INF = Num<T>::inf();
@@ -321,10 +460,36 @@ __device__ bool fwd_pair_strip(const PairFwdArgs<T>& a, T* ring, const T* bin, u
     const T* Db = a.D + (b * N + r0) * M;
     T* tile0 = tiles ? a.Rt + (b * a.S + s) * static_cast<int64_t>(a.NBt) * 1024 : nullptr;
 
-    cp_async_wait<0>();
-    __syncwarp();
-    fwd_pair_load<T>(Db, M, ring, k0, st.rows, lane, a.xD, a.sy.err);
-    cp_async_commit();
+    float x2[4];  // FUSED: |x|^2 of rows r0 + lane/4 + 8i
+    const float* Xs = nullptr;
+    const float* Yb = nullptr;
+    if constexpr (FUSED) {
+        Xs = a.f.X + (b * N + r0) * a.f.d;
+        Yb = a.f.Y + b * M * a.f.d;
+        float xn = 0.f;
+        if (r0 + lane < N) {
+            const float4* xr = reinterpret_cast<const float4*>(Xs + static_cast<int64_t>(lane) * a.f.d);
+            for (int q = 0; q < a.f.d / 4; ++q) {
+                const float4 v = SDTW_IN_BOUNDS(a.f.xX, xr + q, 16, a.sy.err) ? __ldg(xr + q)
+                                                                               : make_float4(0.f, 0.f, 0.f, 0.f);
+                xn = fmaf(v.x, v.x, xn);
+                xn = fmaf(v.y, v.y, xn);
+                xn = fmaf(v.z, v.z, xn);
+                xn = fmaf(v.w, v.w, xn);
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i) x2[i] = __shfl_sync(kFull, xn, (lane >> 2) + 8 * i);
+        __syncwarp();
+        if (k0 > 0) fused_rect(a.f, ring, Xs, Yb, x2, y2, b, r0, N, M, k0 - 1, lane, a.sy.err);
+        fused_rect(a.f, ring, Xs, Yb, x2, y2, b, r0, N, M, k0, lane, a.sy.err);
+        __syncwarp();
+    } else {
+        cp_async_wait<0>();
+        __syncwarp();
+        fwd_pair_load<T>(Db, M, ring, k0, st.rows, lane, a.xD, a.sy.err);
+        cp_async_commit();
+    }
 
     if (!tiles) {
         // Padded columns of each row outside the swept range (columns 32*k0 - r - 1 .. 32*k1 + 30 - r, padded
@@ -358,10 +523,12 @@ __device__ bool fwd_pair_strip(const PairFwdArgs<T>& a, T* ring, const T* bin, u
     // starts (that slot's R was written back, synchronously, at the end of the block before).
 #pragma unroll 1
     for (int blk = k0; blk <= k1; ++blk) {
-        cp_async_wait<0>();
-        __syncwarp();
-        if (blk + 1 <= k1) fwd_pair_load<T>(Db, M, ring, blk + 1, st.rows, lane, a.xD, a.sy.err);
-        cp_async_commit();
+        if constexpr (!FUSED) {
+            cp_async_wait<0>();
+            __syncwarp();
+            if (blk + 1 <= k1) fwd_pair_load<T>(Db, M, ring, blk + 1, st.rows, lane, a.xD, a.sy.err);
+            cp_async_commit();
+        }
         const int tau0 = 32 * blk;
         T* cell = ring + lane * RS + (blk & 1) * 32;
         const T* top = bin + tau0 + kBufPad;
@@ -382,6 +549,12 @@ __device__ bool fwd_pair_strip(const PairFwdArgs<T>& a, T* ring, const T* bin, u
         if (blk == bstar && lane == lstar && SDTW_IN_BOUNDS(a.xC, a.costs + b, sizeof(T), a.sy.err))
             a.costs[b] = cell[tstar - tau0];
         __syncwarp();
+        if constexpr (FUSED) {
+            if (blk + 1 <= k1) {
+                fused_rect(a.f, ring, Xs, Yb, x2, y2, b, r0, N, M, blk + 1, lane, a.sy.err);
+                __syncwarp();
+            }
+        }
     }
     if (!skip) {
         // The strip below may read columns past this sweep as its row above: they are out of band (+inf).
@@ -396,7 +569,7 @@ __device__ bool fwd_pair_strip(const PairFwdArgs<T>& a, T* ring, const T* bin, u
     return true;
 }
 
-template <typename T, int MC>
+template <typename T, int MC, bool FUSED>
 __global__ void __launch_bounds__(SDTW_PAIR_THREADS, SDTW_PAIR_MIN_CTAS) sdtw_fwd_pair_kernel(PairFwdArgs<T> a)
 {
     extern __shared__ __align__(16) unsigned char smem[];
@@ -418,6 +591,29 @@ __global__ void __launch_bounds__(SDTW_PAIR_THREADS, SDTW_PAIR_MIN_CTAS) sdtw_fw
     for (int e = threadIdx.x; e < W * a.G; e += blockDim.x)
         asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bars + 8 * e), "r"(kPubLanes) : "memory");
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    // FUSED: |y|^2 of the pair's columns, zero-padded by 32 before column 0 and 64 after M - 1.
+    float* y2 = nullptr;
+    if constexpr (FUSED) {
+        float* y2s = reinterpret_cast<float*>(smem + fused_y2_offset(W, a.M));
+        const float* Yb = a.f.Y + b * a.M * a.f.d;
+        for (int e = threadIdx.x; e < a.M + 96; e += blockDim.x) {
+            const int64_t c = e - 32;
+            float sq = 0.f;
+            if (c >= 0 && c < a.M) {
+                const float4* yr = reinterpret_cast<const float4*>(Yb + c * a.f.d);
+                for (int q = 0; q < a.f.d / 4; ++q) {
+                    const float4 v = SDTW_IN_BOUNDS(a.f.xY, yr + q, 16, a.sy.err) ? __ldg(yr + q)
+                                                                                   : make_float4(0.f, 0.f, 0.f, 0.f);
+                    sq = fmaf(v.x, v.x, sq);
+                    sq = fmaf(v.y, v.y, sq);
+                    sq = fmaf(v.z, v.z, sq);
+                    sq = fmaf(v.w, v.w, sq);
+                }
+            }
+            y2s[e] = sq;
+        }
+        y2 = y2s + 32;
+    }
     // Padded rows 0 and N+1 of R (softdtw.cpp:114-121: +inf with R[b,0,0] = 0).
     if (a.Rt == nullptr) {
         T* Rb = a.R + b * (a.N + 2) * (a.M + 2);
@@ -433,8 +629,9 @@ __global__ void __launch_bounds__(SDTW_PAIR_THREADS, SDTW_PAIR_MIN_CTAS) sdtw_fw
         const int wp = (s + W - 1) % W;
         const T* bin = s > 0 ? bufs + static_cast<size_t>(wp) * a.BL : crow;
         const uint32_t par_in = static_cast<uint32_t>(((s - 1) / W) & 1);  // round of the strip above in its warp
-        if (!fwd_pair_strip<T, MC>(a, ring, bin, bars + 8 * wp * a.G, par_in, bufs + static_cast<size_t>(warp) * a.BL,
-                                   bars + 8 * warp * a.G, b, s, lane))
+        if (!fwd_pair_strip<T, MC, FUSED>(a, ring, bin, bars + 8 * wp * a.G, par_in,
+                                          bufs + static_cast<size_t>(warp) * a.BL, bars + 8 * warp * a.G, y2, b, s,
+                                          lane))
             break;
     }
     cp_async_wait<0>();
@@ -821,12 +1018,20 @@ size_t pair_bwd_smem_bytes(int W, int64_t M)
 template <typename T>
 cudaError_t pair_init_attrs(int max_smem)
 {
-    cudaError_t e = cudaFuncSetAttribute(sdtw_fwd_pair_kernel<T, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
+    cudaError_t e = cudaFuncSetAttribute(sdtw_fwd_pair_kernel<T, 0, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
     if (e != cudaSuccess) return e;
-    e = cudaFuncSetAttribute(sdtw_fwd_pair_kernel<T, kPairSpecialM>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
+    e = cudaFuncSetAttribute(sdtw_fwd_pair_kernel<T, kPairSpecialM, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
     if (e != cudaSuccess) return e;
     e = cudaFuncSetAttribute(sdtw_bwd_pair_kernel<T, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
     if (e != cudaSuccess) return e;
+    if constexpr (sizeof(T) == 4) {
+        e = cudaFuncSetAttribute(sdtw_fwd_pair_kernel<float, 0, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 max_smem);
+        if (e != cudaSuccess) return e;
+        e = cudaFuncSetAttribute(sdtw_fwd_pair_kernel<float, kPairSpecialM, true>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
+        if (e != cudaSuccess) return e;
+    }
     return cudaFuncSetAttribute(sdtw_bwd_pair_kernel<T, kPairSpecialM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 max_smem);
 }
@@ -839,15 +1044,26 @@ cudaError_t pair_regs(bool backward, int& regs)
     // The largest count over the kernel's instantiations (the one specialized on M can need more).
     cudaFuncAttributes fa, fb;
     cudaError_t e = backward ? cudaFuncGetAttributes(&fa, sdtw_bwd_pair_kernel<T, 0>)
-                             : cudaFuncGetAttributes(&fa, sdtw_fwd_pair_kernel<T, 0>);
+                             : cudaFuncGetAttributes(&fa, sdtw_fwd_pair_kernel<T, 0, false>);
     if (e == cudaSuccess)
         e = backward ? cudaFuncGetAttributes(&fb, sdtw_bwd_pair_kernel<T, kPairSpecialM>)
-                     : cudaFuncGetAttributes(&fb, sdtw_fwd_pair_kernel<T, kPairSpecialM>);
+                     : cudaFuncGetAttributes(&fb, sdtw_fwd_pair_kernel<T, kPairSpecialM, false>);
     regs = e == cudaSuccess ? (fa.numRegs > fb.numRegs ? fa.numRegs : fb.numRegs) : 0;
     return e;
 }
 template cudaError_t pair_regs<float>(bool, int&);
 template cudaError_t pair_regs<double>(bool, int&);
+
+size_t pair_fused_smem_bytes(int W, int64_t M) { return fused_smem_bytes(W, M); }
+
+cudaError_t pair_fused_regs(int& regs)
+{
+    cudaFuncAttributes fa, fb;
+    cudaError_t e = cudaFuncGetAttributes(&fa, sdtw_fwd_pair_kernel<float, 0, true>);
+    if (e == cudaSuccess) e = cudaFuncGetAttributes(&fb, sdtw_fwd_pair_kernel<float, kPairSpecialM, true>);
+    regs = e == cudaSuccess ? (fa.numRegs > fb.numRegs ? fa.numRegs : fb.numRegs) : 0;
+    return e;
+}
 
 // Warps per CTA: at most `cap` and the pair's strip count, and few enough for the CTA to fit `budget`.
 template <typename T>
@@ -909,11 +1125,57 @@ cudaError_t pair_forward(const T* D, T* R, T* Rt, T* costs, const void* lx, cons
     a.inject = inject;
     count_launch();
     if (M == kPairSpecialM)
-        sdtw_fwd_pair_kernel<T, kPairSpecialM><<<static_cast<unsigned>(B), W * 32, pair_fwd_smem_bytes<T>(W, M), stream>>>(a);
+        sdtw_fwd_pair_kernel<T, kPairSpecialM, false><<<static_cast<unsigned>(B), W * 32, pair_fwd_smem_bytes<T>(W, M), stream>>>(a);
     else
-        sdtw_fwd_pair_kernel<T, 0><<<static_cast<unsigned>(B), W * 32, pair_fwd_smem_bytes<T>(W, M), stream>>>(a);
+        sdtw_fwd_pair_kernel<T, 0, false><<<static_cast<unsigned>(B), W * 32, pair_fwd_smem_bytes<T>(W, M), stream>>>(a);
     return cudaGetLastError();
 }
+cudaError_t pair_forward_fused(const float* X, const float* Y, int64_t d, float* Rt, float* costs, uint32_t* cmask,
+                               int* cflags, const void* lx, const void* ly, int is32, int64_t B, int64_t N, int64_t M,
+                               int64_t bw, double gamma, int W, Sync sy, int64_t inject, cudaStream_t stream)
+{
+    PairFwdArgs<float> a;
+    a.D = nullptr;
+    a.R = nullptr;
+    a.Rt = Rt;
+    a.NBt = pair_tile_blocks(M);
+    const int64_t S = N > 0 ? (N + 31) / 32 : 1;
+    a.xD = Extent{nullptr, 0};
+    a.xR = Extent{nullptr, 0};
+    a.xRt = Extent{Rt, static_cast<size_t>(B * S * a.NBt) * 1024 * sizeof(float)};
+    a.xC = Extent{costs, static_cast<size_t>(B) * sizeof(float)};
+    a.costs = costs;
+    a.len = Lengths{lx, ly, is32};
+    a.B = B;
+    a.N = N;
+    a.M = M;
+    a.bw = bw;
+    a.S = static_cast<int>(S);
+    a.W = W;
+    a.BL = buf_len(M);
+    a.G = fwd_groups(M);
+    a.k = static_cast<float>(1.4426950408889634 / gamma);
+    a.gl = static_cast<float>(gamma * 0.6931471805599453);
+    a.sy = sy;
+    a.inject = inject;
+    a.f.X = X;
+    a.f.Y = Y;
+    a.f.d = static_cast<int>(d);
+    a.f.cmask = cmask;
+    a.f.cflags = cflags;
+    a.f.MW = static_cast<int>((M + 31) / 32);
+    a.f.xX = Extent{X, static_cast<size_t>(B * N * d) * sizeof(float)};
+    a.f.xY = Extent{Y, static_cast<size_t>(B * M * d) * sizeof(float)};
+    a.f.xMask = Extent{cmask, static_cast<size_t>(B * N * a.f.MW) * sizeof(uint32_t)};
+    a.f.xFlags = Extent{cflags, static_cast<size_t>(B) * sizeof(int)};
+    count_launch();
+    if (M == kPairSpecialM)
+        sdtw_fwd_pair_kernel<float, kPairSpecialM, true><<<static_cast<unsigned>(B), W * 32, fused_smem_bytes(W, M), stream>>>(a);
+    else
+        sdtw_fwd_pair_kernel<float, 0, true><<<static_cast<unsigned>(B), W * 32, fused_smem_bytes(W, M), stream>>>(a);
+    return cudaGetLastError();
+}
+
 template cudaError_t pair_forward<float>(const float*, float*, float*, float*, const void*, const void*, int, int64_t,
                                          int64_t, int64_t, int64_t, double, int, Sync, int64_t, cudaStream_t);
 template cudaError_t pair_forward<double>(const double*, double*, double*, double*, const void*, const void*, int,

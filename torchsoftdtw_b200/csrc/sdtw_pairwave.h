@@ -51,6 +51,16 @@ bool pair_keys_fit(int64_t N, int64_t M);
 // lengths); tiles of blocks a strip does not sweep are never written. Blocks per strip: pair_tile_blocks(M).
 inline int pair_tile_blocks(int64_t M) { return static_cast<int>((M + 31) / 32) + 1; }
 
+// Fused squared-L2 forward (fp32, R as strip tiles): the cost matrix D = (|x|^2 + |y|^2) - 2 x.y, clamped
+// at 0, is computed tile by tile inside the forward from X (B, N, d) and Y (B, M, d) (d a multiple of 16,
+// both 16-byte aligned) and never stored. Clamped cells inside the matrix set bit c % 32 of word
+// cmask[(b N + i) ((M + 31) / 32) + c / 32] and cflags[b] (both zeroed by the caller).
+size_t pair_fused_smem_bytes(int W, int64_t M);
+cudaError_t pair_fused_regs(int& regs);
+cudaError_t pair_forward_fused(const float* X, const float* Y, int64_t d, float* Rt, float* costs, uint32_t* cmask,
+                               int* cflags, const void* lx, const void* ly, int is32, int64_t B, int64_t N, int64_t M,
+                               int64_t bw, double gamma, int W, Sync sy, int64_t inject, cudaStream_t stream);
+
 // Forward: writes the padded R (B, N+2, M+2) when Rt is null, else the tiles Rt (R unused).
 template <typename T>
 cudaError_t pair_forward(const T* D, T* R, T* Rt, T* costs, const void* lx, const void* ly, int is32, int64_t B,

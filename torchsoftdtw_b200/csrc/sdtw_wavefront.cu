@@ -520,6 +520,27 @@ int g_inject_skip = -1;  // set only through sdtw_debug_inject_stall (tests of t
 int g_force_path = 0;    // 0: automatic, 1: strip-ticket kernels, 2: pair-resident kernels, 3: warp-per-pair
 int g_pair_warps = kPairMaxWarps;  // warps per CTA of the pair-resident kernels (upper bound)
 
+// E[b, i, c] = 0 where bit c % 32 of clamp_mask[(b N + i) MW + c / 32] is set, in pairs whose clamp flag is
+// set (one CTA per pair; the others return at once). The fused forward's clamp record applied to the
+// backward's E, so that the gradient kernels see the clamp of the cost matrix already folded in.
+__global__ void sdtw_clamp_mask_kernel(float* E, const uint32_t* clamp_mask, const int* clamp_flags, int64_t N,
+                                       int64_t M)
+{
+    const int64_t b = blockIdx.x;
+    if (clamp_flags[b] == 0) return;
+    const int64_t MW = (M + 31) / 32;
+    const uint32_t* mb = clamp_mask + b * N * MW;
+    for (int64_t w = threadIdx.x; w < N * MW; w += blockDim.x) {
+        uint32_t bits = mb[w];
+        const int64_t i = w / MW, c0 = (w % MW) * 32;
+        while (bits != 0) {
+            const int k = __ffs(static_cast<int>(bits)) - 1;
+            bits &= bits - 1;
+            if (c0 + k < M) E[(b * N + i) * M + c0 + k] = 0.f;
+        }
+    }
+}
+
 struct DeviceInfo {
     bool ready = false;
     int sms = 0;
@@ -980,6 +1001,64 @@ sdtw_status sdtw_forward_tiles(sdtw_dtype dtype, const void* D, int64_t B, int64
                                      costs, workspace, err_word, s, R_tiles);
     return launch_forward<double>(D, B, N, M, lengths_x, lengths_y, lengths_int32, gamma, bandwidth, nullptr, costs,
                                   workspace, err_word, s, R_tiles);
+}
+
+int sdtw_forward_l2_fused_ok(int64_t B, int64_t N, int64_t M, int64_t d)
+{
+    if (B <= 0 || N <= 0 || M <= 0 || d <= 0 || d % 16 != 0 || d > (int64_t(1) << 20)) return 0;
+    const DeviceInfo* di = nullptr;
+    if (device_info(di) != cudaSuccess || !uses_tiles<float>(*di, B, N, M)) return 0;
+    const int W = choose_pair_warps<float>(*di, false, B, N, M);
+    return W > 0 && pair_fused_smem_bytes(W, M) <= static_cast<size_t>(di->max_smem);
+}
+
+int64_t sdtw_clamp_mask_words(int64_t B, int64_t N, int64_t M)
+{
+    if (B < 0 || N < 0 || M < 0) return 0;
+    return B * N * ((M + 31) / 32);
+}
+
+sdtw_status sdtw_forward_l2_tiles(const float* X, const float* Y, int64_t B, int64_t N, int64_t M, int64_t d,
+                                  const void* lengths_x, const void* lengths_y, int lengths_int32, double gamma,
+                                  int64_t bandwidth, void* R_tiles, float* costs, uint32_t* clamp_mask,
+                                  int* clamp_flags, void* workspace, size_t workspace_bytes, uint32_t* err_word,
+                                  void* stream)
+{
+    if (!common_args_ok(B, N, M, gamma) || d < 0) return SDTW_EINVAL;
+    if (B == 0) return SDTW_OK;
+    if (!sdtw_forward_l2_fused_ok(B, N, M, d)) return SDTW_EINVAL;
+    if (!X || !Y || !lengths_x || !lengths_y || !R_tiles || !costs || !clamp_mask || !clamp_flags || !err_word)
+        return SDTW_EINVAL;
+    if (reinterpret_cast<uintptr_t>(R_tiles) % 16 != 0 || reinterpret_cast<uintptr_t>(X) % 16 != 0 ||
+        reinterpret_cast<uintptr_t>(Y) % 16 != 0)
+        return SDTW_EINVAL;
+    if (!workspace || workspace_bytes < sdtw_forward_workspace_bytes(B, N, M, SDTW_F32)) return SDTW_EWORKSPACE;
+    const DeviceInfo* di = nullptr;
+    cudaError_t e = device_info(di);
+    if (e != cudaSuccess) return from_cuda(e);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    e = cudaMemsetAsync(costs, 0xff, static_cast<size_t>(B) * sizeof(float), s);  // NaN until the pair finishes
+    if (e == cudaSuccess) e = cudaMemsetAsync(workspace, 0, kHeader, s);
+    if (e == cudaSuccess)
+        e = cudaMemsetAsync(clamp_mask, 0, static_cast<size_t>(sdtw_clamp_mask_words(B, N, M)) * sizeof(uint32_t), s);
+    if (e == cudaSuccess) e = cudaMemsetAsync(clamp_flags, 0, static_cast<size_t>(B) * sizeof(int), s);
+    if (e != cudaSuccess) return from_cuda(e);
+    const int W = choose_pair_warps<float>(*di, false, B, N, M);
+    return from_cuda(pair_forward_fused(X, Y, d, static_cast<float*>(R_tiles), costs, clamp_mask, clamp_flags,
+                                        lengths_x, lengths_y, lengths_int32, B, N, M, clamp_bw(bandwidth, N, M), gamma,
+                                        W, make_sync(workspace, err_word), g_inject_skip, s));
+}
+
+sdtw_status sdtw_apply_clamp_mask(float* E, const uint32_t* clamp_mask, const int* clamp_flags, int64_t B, int64_t N,
+                                  int64_t M, void* stream)
+{
+    if (B < 0 || N < 0 || M < 0 || B > 0x7fffffff) return SDTW_EINVAL;
+    if (B == 0 || N == 0 || M == 0) return SDTW_OK;
+    if (!E || !clamp_mask || !clamp_flags) return SDTW_EINVAL;
+    count_launch();
+    sdtw_clamp_mask_kernel<<<static_cast<unsigned>(B), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+        E, clamp_mask, clamp_flags, N, M);
+    return from_cuda(cudaGetLastError());
 }
 
 sdtw_status sdtw_backward_tiles(sdtw_dtype dtype, const void* R_tiles, int64_t B, int64_t N, int64_t M,

@@ -262,8 +262,26 @@ Tensor run_backward_module(const Tensor& Racc, const Tensor& lx, const Tensor& l
     return E;
 }
 
+// True when the fused forward (cost tiles computed inside the wavefront, sdtw_forward_l2_tiles) runs this
+// problem: TORCHSOFTDTW_B200_FUSED_COST=1 in the environment (read on every call, as the FakeTensor kernel
+// does), fp32 arithmetic and a shape the library accepts (sdtw_forward_l2_fused_ok). It trades the cost
+// matrix's memory (B N M values) for in-wavefront products on the warp tensor-core path, which at d = 64
+// makes the forward slower than the stored-D pair of kernels; hence off by default. The operands are
+// contiguous accumulation-type copies, so their alignment is the allocator's (checked anyway).
+bool l2_fused(const Tensor& Xc, const Tensor& Yc)
+{
+    const char* env = std::getenv("TORCHSOFTDTW_B200_FUSED_COST");
+    if (!env || !env[0] || env[0] == '0') return false;
+    const int64_t B = Xc.size(0), N = Xc.size(1), M = Yc.size(1), d = Xc.size(2);
+    return Xc.scalar_type() == at::kFloat && sdtw_forward_l2_fused_ok(B, N, M, d) &&
+           reinterpret_cast<uintptr_t>(Xc.data_ptr()) % 16 == 0 && reinterpret_cast<uintptr_t>(Yc.data_ptr()) % 16 == 0;
+}
+
 // Returns (costs, R, D, clamp_flags): R as run_forward_module returns it; D is the clamped cost matrix with
 // the clamp recorded in its sign bit; clamp_flags (B,) int32 marks the pairs that have a clamped cell.
+// When the fused forward runs (l2_fused), D is never formed: the third output is instead the clamp mask
+// (B, N, ceil(M / 32)) int32, bit c % 32 of word c / 32 set where cell (i, c) was clamped, and R is the
+// strip tiles.
 std::tuple<Tensor, Tensor, Tensor, Tensor> l2_forward_cuda(const Tensor& X, const Tensor& Y,
                                                            const Tensor& lengths_x, const Tensor& lengths_y,
                                                            double gamma, int64_t bandwidth)
@@ -273,6 +291,26 @@ std::tuple<Tensor, Tensor, Tensor, Tensor> l2_forward_cuda(const Tensor& X, cons
     const auto acc = acc_type(X.scalar_type());
     const Tensor Xc = X.to(acc).contiguous(), Yc = Y.to(acc).contiguous();
     const int64_t B = Xc.size(0), N = Xc.size(1), M = Yc.size(1), d = Xc.size(2);
+    if (B > 0 && N > 0 && M > 0 && l2_fused(Xc, Yc)) {
+        const Tensor lx = prep_lengths(lengths_x), ly = prep_lengths(lengths_y);
+        auto opts = Xc.options();
+        const int64_t S = (N + 31) / 32, NBt = sdtw_r_tiles_elems(1, 32, M) / 1024;
+        Tensor Rt = at::empty({B, S, NBt, 32, 32}, opts);
+        Tensor costs = at::empty({B}, opts);
+        Tensor mask = at::empty({B, N, (M + 31) / 32}, opts.dtype(at::kInt));
+        Tensor flags = at::empty({B}, opts.dtype(at::kInt));
+        const size_t wsb = sdtw_forward_workspace_bytes(B, N, M, SDTW_F32);
+        Tensor ws = at::empty({static_cast<int64_t>(wsb)}, opts.dtype(at::kByte));
+        cudaStream_t stream = at::cuda::getCurrentCUDAStream(X.get_device()).stream();
+        check_status(sdtw_forward_l2_tiles(Xc.data_ptr<float>(), Yc.data_ptr<float>(), B, N, M, d, lx.data_ptr(),
+                                           ly.data_ptr(), lx.scalar_type() == at::kInt, gamma, bandwidth,
+                                           Rt.data_ptr(), costs.data_ptr<float>(),
+                                           reinterpret_cast<uint32_t*>(mask.data_ptr<int>()), flags.data_ptr<int>(),
+                                           ws.data_ptr(), wsb, error_word(Xc), stream),
+                     "forward");
+        maybe_sync_check(Xc, stream);
+        return {costs, Rt, mask, flags};
+    }
     Tensor D = at::empty({B, N, M}, Xc.options());
     Tensor flags = at::empty({B}, Xc.options().dtype(at::kInt));
     cudaStream_t stream = at::cuda::getCurrentCUDAStream(X.get_device()).stream();
@@ -294,7 +332,11 @@ std::tuple<Tensor, Tensor> l2_backward_cuda(const Tensor& X, const Tensor& Y, co
     const auto acc = acc_type(X.scalar_type());
     const Tensor Xc = X.to(acc).contiguous(), Yc = Y.to(acc).contiguous();
     const int64_t B = Xc.size(0), N = Xc.size(1), M = Yc.size(1), d = Xc.size(2);
-    TORCH_CHECK(D.sizes() == at::IntArrayRef({B, N, M}) && D.scalar_type() == acc, "D has the wrong shape or dtype");
+    // The fused forward's clamp mask in place of D (see l2_forward_cuda).
+    const bool fused = D.scalar_type() == at::kInt;
+    TORCH_CHECK(fused ? (D.sizes() == at::IntArrayRef({B, N, (M + 31) / 32}) && acc == at::kFloat)
+                      : (D.sizes() == at::IntArrayRef({B, N, M}) && D.scalar_type() == acc),
+                "D has the wrong shape or dtype");
     const bool tiled = R.dim() == 5 &&
                        R.sizes() == at::IntArrayRef({B, (N + 31) / 32, sdtw_r_tiles_elems(1, 32, M) / 1024, 32, 32});
     TORCH_CHECK((tiled || R.sizes() == at::IntArrayRef({B, N + 2, M + 2})) && R.scalar_type() == acc,
@@ -307,8 +349,19 @@ std::tuple<Tensor, Tensor> l2_backward_cuda(const Tensor& X, const Tensor& Y, co
     Tensor gY = need_y ? at::empty({B, M, d}, Xc.options()) : at::empty({0}, Y.options());
     cudaStream_t stream = at::cuda::getCurrentCUDAStream(X.get_device()).stream();
     TORCH_CHECK(clamp_flags.numel() == B && clamp_flags.scalar_type() == at::kInt, "clamp_flags must be (B,) int32");
-    check_status(sdtw_grad_l2(code_of(acc), Xc.data_ptr(), Yc.data_ptr(), D.contiguous().data_ptr(), E.data_ptr(),
-                              g.data_ptr(), clamp_flags.contiguous().data_ptr<int>(), B, N, M, d,
+    Tensor Dg = D, flags = clamp_flags.contiguous();
+    if (fused) {
+        // Fold the clamp into E; the gradient kernels then see no clamped pair (all-zero flags, so they never
+        // read their D argument, here E itself, whose sign bits are clear anyway: E >= 0).
+        const Tensor mask = D.contiguous();
+        check_status(sdtw_apply_clamp_mask(E.data_ptr<float>(), reinterpret_cast<const uint32_t*>(mask.data_ptr<int>()),
+                                           flags.data_ptr<int>(), B, N, M, stream),
+                     "apply_clamp_mask");
+        Dg = E;
+        flags = at::zeros({B}, flags.options());
+    }
+    check_status(sdtw_grad_l2(code_of(acc), Xc.data_ptr(), Yc.data_ptr(), Dg.contiguous().data_ptr(), E.data_ptr(),
+                              g.data_ptr(), flags.data_ptr<int>(), B, N, M, d,
                               need_x ? gX.data_ptr() : nullptr,
                               need_y ? gY.data_ptr() : nullptr, stream),
                  "grad_l2");

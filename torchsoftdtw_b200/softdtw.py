@@ -58,8 +58,12 @@ def _l2_forward_fake(X, Y, lengths_x, lengths_y, gamma, bandwidth):
         R = X.new_empty((B, (N + 31) // 32, (M + 31) // 32 + 1, 32, 32), dtype=acc_dt)
     else:
         R = X.new_empty((B, N + 2, M + 2), dtype=acc_dt)
-    return (X.new_empty((B,), dtype=acc_dt), R, X.new_empty((B, N, M), dtype=acc_dt),
-            X.new_empty((B,), dtype=torch.int32))
+    if _ext.l2_fused(int(B), int(N), int(M), int(X.shape[2]), acc_dt, X.device):
+        # The cost matrix stays inside the forward: the third output is its clamp mask (one bit per cell).
+        Dout = X.new_empty((B, N, (M + 31) // 32), dtype=torch.int32)
+    else:
+        Dout = X.new_empty((B, N, M), dtype=acc_dt)
+    return (X.new_empty((B,), dtype=acc_dt), R, Dout, X.new_empty((B,), dtype=torch.int32))
 
 
 @torch.library.register_fake("torchsoftdtw_b200::forward_x2")
