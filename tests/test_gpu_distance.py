@@ -127,6 +127,34 @@ def test_grad_matches_fp64(cuda, distance_path, B, N, M, d, force_mask):
     assert np.max(np.abs(gX2.cpu().numpy() - ex)) / scale_x < 2e-6
 
 
+@pytest.mark.parametrize("B,N,M,d", [(8, 512, 512, 64), (3, 300, 200, 32), (2, 37, 260, 128), (2, 64, 4, 16)])
+@pytest.mark.parametrize("masked", [False, True])
+def test_grad_y_tensor_cores(cuda, B, N, M, d, masked):
+    """grad_Y on the tcgen05 kernel (E read transposed: output rows are E's columns, K runs over its rows, in
+    chunks whose last one is ragged) against the fp64 contraction, and against the CUDA-core kernel."""
+    gen = torch.Generator().manual_seed(B * N + M + d)
+    X = torch.randn(B, N, d, generator=gen)
+    Y = torch.randn(B, M, d, generator=gen)
+    E = torch.rand(B, N, M, generator=gen)
+    D = torch.rand(B, N, M, generator=gen) + 0.1
+    if masked:
+        D[torch.rand(B, N, M, generator=gen) < 0.1] = -0.0
+    gvec = torch.rand(B, generator=gen) + 0.5
+    flags = torch.tensor([1 if masked else 0] * B, dtype=torch.int32)
+    Xc, Yc, Dc, Ec, gc, fc = (t.to(cuda) for t in (X, Y, D, E, gvec, flags))
+    _, gY = grad(Xc, Yc, Dc, Ec, gc, fc, need_x=False)
+    _, ey = reference_grads(X, Y, D, E, gvec)
+    scale = np.max(np.abs(ey)) + 1e-30
+    assert np.max(np.abs(gY.cpu().numpy() - ey)) / scale < 2e-6
+    lib = _ext.capi()
+    try:
+        lib.sdtw_debug_force_distance_path(2)
+        _, gY_cc = grad(Xc, Yc, Dc, Ec, gc, fc, need_x=False)
+    finally:
+        lib.sdtw_debug_force_distance_path(0)
+    assert float((gY - gY_cc).abs().max()) / scale < 4e-6
+
+
 def test_tensor_core_paths_agree(cuda):
     """tcgen05 and mma.sync cost matrices of the headline shape agree to fp32 rounding."""
     lib = _ext.capi()

@@ -530,7 +530,7 @@ sdtw_status launch_grad(const void* X, const void* Y, const void* D, const void*
                         cudaStream_t s)
 {
     const unsigned cblocks = static_cast<unsigned>((d + kTile - 1) / kTile);
-    bool gx_done = false;
+    bool gx_done = false, gy_done = false;
     if constexpr (sizeof(T) == 4) {
         if (g_distance_path == 0 && gX && grad_tc_supported(X, Y, D, E, gX, B, N, M, d)) {
             const cudaError_t e = grad_x_tc_launch(static_cast<const float*>(X), static_cast<const float*>(Y),
@@ -540,14 +540,25 @@ sdtw_status launch_grad(const void* X, const void* Y, const void* D, const void*
             if (e != cudaSuccess) return static_cast<sdtw_status>(e);
             gx_done = true;
         }
+        // grad_Y: the same tensor-core kernel with E read transposed (autograd's G^T X bmm of the reference).
+        if (g_distance_path == 0 && gY && grad_tc_supported(X, Y, D, E, gY, B, N, M, d)) {
+            const cudaError_t e = grad_y_tc_launch(static_cast<const float*>(X), static_cast<const float*>(Y),
+                                                   static_cast<const float*>(D), static_cast<const float*>(E),
+                                                   static_cast<const float*>(g), clamp_flags, static_cast<float*>(gY),
+                                                   B, N, M, d, wait_timeout_s(), s);
+            if (e != cudaSuccess) return static_cast<sdtw_status>(e);
+            gy_done = true;
+        }
     }
+    if (gx_done) gX = nullptr;
+    if (gy_done) gY = nullptr;
+    if (!gX && !gY) return SDTW_OK;
     if ((g_distance_path == 0 || g_distance_path == 3) && narrow_supported(B, N, M, d)) {
-        // grad_X (unless the tensor cores took it) and grad_Y
+        // grad_X and grad_Y, each unless the tensor cores took it
         const cudaError_t e = narrow_grad_l2<T>(static_cast<const T*>(X), static_cast<const T*>(Y),
                                                 static_cast<const T*>(D), static_cast<const T*>(E),
-                                                static_cast<const T*>(g), clamp_flags,
-                                                gx_done ? nullptr : static_cast<T*>(gX), static_cast<T*>(gY), B, N, M,
-                                                d, s);
+                                                static_cast<const T*>(g), clamp_flags, static_cast<T*>(gX),
+                                                static_cast<T*>(gY), B, N, M, d, s);
         return e == cudaSuccess ? SDTW_OK : static_cast<sdtw_status>(e);
     }
     if constexpr (sizeof(T) == 4) {

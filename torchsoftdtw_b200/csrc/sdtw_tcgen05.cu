@@ -173,6 +173,13 @@ __device__ __forceinline__ float split_row(unsigned char* head, unsigned char* t
 // role polls, sets bit 1 of the library's distance error word, and the epilogue writes NaN into the rows
 // it has not finished; the TMA and MMA warps wait (bounded) for their own operations before the CTA
 // releases its tensor memory.
+//
+// TRANS: the same kernel computes grad_Y = 2 g[b] (colsum(G) Y - G^T X), the contraction of E over its
+// rows. The roles swap (output rows are the columns of E; B operand [X | 1]; the epilogue reads Y), and E
+// is read transposed: the TMA warp loads E[32 rows x 128 columns] (unswizzled) and the split threads
+// gather each output row's 32 K values from that box's column, so the A operand is Gᵀ in the same
+// 128-byte swizzled K-major layout. GradTcArgs then describes the transposed problem: N = output rows
+// (the columns of E), M = the K extent (the rows of E); E and D are (B, M, N) in memory.
 // ==================================================================================================
 constexpr int kGT = 128;                    // grad_X rows per tile (UMMA M)
 constexpr int kGKC = 32;                    // columns of E per chunk (one 128-byte swizzle atom of fp32)
@@ -289,7 +296,7 @@ struct GradTcArgs {
     unsigned long long timeout_ns;
 };
 
-template <int DPAD>
+template <int DPAD, bool TRANS>
 __global__ void __launch_bounds__(kGradThreads, 1) grad_x_tc_kernel(const __grid_constant__ CUtensorMap me,
                                                                     const __grid_constant__ CUtensorMap my,
                                                                     GradTcArgs a)
@@ -360,7 +367,10 @@ __global__ void __launch_bounds__(kGradThreads, 1) grad_x_tc_kernel(const __grid
                 const int b = t / a.nrt, rt = t % a.nrt, kc = q % a.nk;
                 const uint32_t dst = base + s * G::RAW;
                 mbar_expect_tx(raw_full + 8 * s, G::RAW);
-                tma_load_3d(dst, &me, raw_full + 8 * s, kc * kGKC, rt * kGT, b);
+                if constexpr (TRANS)
+                    tma_load_3d(dst, &me, raw_full + 8 * s, rt * kGT, kc * kGKC, b);  // E rows kc*32.., columns rt*128..
+                else
+                    tma_load_3d(dst, &me, raw_full + 8 * s, kc * kGKC, rt * kGT, b);
 #pragma unroll
                 for (int bx = 0; bx < G::NBOX; ++bx)
                     tma_load_3d(dst + kEChunk + bx * (kGKC * G::YB * 4), &my, raw_full + 8 * s, bx * G::YB,
@@ -451,6 +461,26 @@ __global__ void __launch_bounds__(kGradThreads, 1) grad_x_tc_kernel(const __grid
                 for (int w = 0; w < EU; ++w) {
                     const int lu = eu0 + w;
                     const int off = 128 * er + 16 * (lu ^ (er & 7));
+                    if constexpr (TRANS) {
+                        // Output row er's K values 4 lu .. 4 lu + 3: column er of E's rows j0 + 4 lu + t (the
+                        // raw box is [32 rows][128 columns]; a warp reads 32 consecutive columns per row).
+                        const float* rc = reinterpret_cast<const float*>(raw) + er;
+                        float4 v = make_float4(rc[128 * (4 * lu)], rc[128 * (4 * lu + 1)], rc[128 * (4 * lu + 2)],
+                                               rc[128 * (4 * lu + 3)]);
+                        if (masked) {
+                            // D is (B, M, N) here: D[b][j][i_e]; rows j past the K extent read zero E anyway.
+                            const float* Dc = a.D + static_cast<int64_t>(b) * a.M * a.N + i_e;
+                            const int j = j0 + 4 * lu;
+                            if (j < a.M && signbit(__ldg(Dc + static_cast<int64_t>(j) * a.N))) v.x = 0.f;
+                            if (j + 1 < a.M && signbit(__ldg(Dc + static_cast<int64_t>(j + 1) * a.N))) v.y = 0.f;
+                            if (j + 2 < a.M && signbit(__ldg(Dc + static_cast<int64_t>(j + 2) * a.N))) v.z = 0.f;
+                            if (j + 3 < a.M && signbit(__ldg(Dc + static_cast<int64_t>(j + 3) * a.N))) v.w = 0.f;
+                        }
+                        const float4 h = split_hi(v);
+                        *reinterpret_cast<float4*>(spl + off) = h;
+                        *reinterpret_cast<float4*>(spl + kEChunk + off) = split_lo(v, h);
+                        continue;
+                    }
                     float4 v = *reinterpret_cast<const float4*>(raw + off);
                     if (masked) {
                         const int j = j0 + 4 * lu;  // M % 4 == 0: the four columns are all in or all out
@@ -968,9 +998,12 @@ bool make_map(PFN_cuTensorMapEncodeTiled_v12000 encode, CUtensorMap* map, const 
 }
 
 int g_sm_count[128] = {};
-bool g_grad_attr_set[128][5] = {};
+bool g_grad_attr_set[128][10] = {};
 
-template <int DPAD>
+// TRANS == false: grad_X of E (B, N, M) against Y (B, M, d), rows of X. TRANS == true: the caller passes the
+// transposed problem (X := Y, Y := X, N := M, M := N, out := grad_Y, ry := the inverse norms of X's rows),
+// and E, D stay the (B, M, N) arrays they are in memory.
+template <int DPAD, bool TRANS>
 cudaError_t grad_tc_launch_t(const float* X, const float* Y, const float* D, const float* E, const float* g,
                              const int* clamp_flags, float* gX, int64_t B, int64_t N, int64_t M, int64_t d,
                              double timeout_s, cudaStream_t s, int dev, int slot,
@@ -979,16 +1012,20 @@ cudaError_t grad_tc_launch_t(const float* X, const float* Y, const float* D, con
     using G = GradGeom<DPAD>;
     {
         std::lock_guard<std::mutex> lock(g_tc_mu);
-        if (!g_grad_attr_set[dev][slot]) {
-            const cudaError_t e = cudaFuncSetAttribute(grad_x_tc_kernel<DPAD>,
+        const int sl = slot + (TRANS ? 5 : 0);
+        if (!g_grad_attr_set[dev][sl]) {
+            const cudaError_t e = cudaFuncSetAttribute(grad_x_tc_kernel<DPAD, TRANS>,
                                                        cudaFuncAttributeMaxDynamicSharedMemorySize, G::BYTES);
             if (e != cudaSuccess) return e;
-            g_grad_attr_set[dev][slot] = true;
+            g_grad_attr_set[dev][sl] = true;
         }
     }
     CUtensorMap me, my;
-    if (!make_map(encode, &me, E, B, N, M) ||
-        !make_map_box(encode, &my, Y, B, M, d, G::YB, kGKC, CU_TENSOR_MAP_SWIZZLE_NONE))
+    // E's box: 32 columns x 128 rows, 128-byte swizzled (grad_X), or 128 columns x 32 rows, unswizzled
+    // (grad_Y, from the (B, M, N) array: rows are the K extent).
+    const bool me_ok = TRANS ? make_map_box(encode, &me, E, B, M, N, kGT, kGKC, CU_TENSOR_MAP_SWIZZLE_NONE)
+                             : make_map(encode, &me, E, B, N, M);
+    if (!me_ok || !make_map_box(encode, &my, Y, B, M, d, G::YB, kGKC, CU_TENSOR_MAP_SWIZZLE_NONE))
         return cudaErrorInvalidValue;
     GradTcArgs a;
     a.X = X;
@@ -1008,7 +1045,7 @@ cudaError_t grad_tc_launch_t(const float* X, const float* Y, const float* D, con
     const int64_t tiles = B * a.nrt;
     const int grid = static_cast<int>(tiles < g_sm_count[dev] ? tiles : g_sm_count[dev]);
     count_launch();
-    grad_x_tc_kernel<DPAD><<<grid, kGradThreads, G::BYTES, s>>>(me, my, a);
+    grad_x_tc_kernel<DPAD, TRANS><<<grid, kGradThreads, G::BYTES, s>>>(me, my, a);
     return cudaGetLastError();
 }
 
@@ -1018,8 +1055,46 @@ bool grad_tc_supported(const void* X, const void* Y, const void* D, const void* 
                        int64_t N, int64_t M, int64_t d)
 {
     const auto al = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+    // (The row-tile count bounds both contractions: grad_X tiles over N, grad_Y over M.)
     return d >= 1 && d <= 128 && d % 4 == 0 && M % 4 == 0 && N >= 1 && M >= 1 && al(X) && al(Y) && al(D) &&
-           al(E) && al(gX) && N < (1 << 30) && M < (1 << 30) && B >= 1 && B * ((N + kGT - 1) / kGT) < (1ll << 31);
+           al(E) && al(gX) && N < (1 << 30) && M < (1 << 30) && B >= 1 && B * ((N + kGT - 1) / kGT) < (1ll << 31) &&
+           B * ((M + kGT - 1) / kGT) < (1ll << 31);
+}
+
+namespace {
+// The SM count and the tensor-map encoder, for the calling thread's current device.
+cudaError_t tc_prepare(PFN_cuTensorMapEncodeTiled_v12000& encode, int& dev)
+{
+    cudaError_t e = get_encode(encode);
+    if (e != cudaSuccess) return e;
+    e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= 128) return cudaErrorInvalidDevice;
+    std::lock_guard<std::mutex> lock(g_tc_mu);
+    if (g_sm_count[dev] == 0) {
+        int n = 0;
+        e = cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+        if (e != cudaSuccess) return e;
+        g_sm_count[dev] = n > 0 ? n : 1;
+    }
+    return cudaSuccess;
+}
+}  // namespace
+
+cudaError_t grad_y_tc_launch(const float* X, const float* Y, const float* D, const float* E, const float* g,
+                             const int* clamp_flags, float* gY, int64_t B, int64_t N, int64_t M, int64_t d,
+                             double timeout_s, cudaStream_t s, const float* rx, float eps)
+{
+    PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
+    int dev = 0;
+    const cudaError_t e = tc_prepare(encode, dev);
+    if (e != cudaSuccess) return e;
+    // The transposed problem: output rows are Y's (M of them), the K extent is N, B operand X.
+    if (d <= 16) return grad_tc_launch_t<16, true>(Y, X, D, E, g, clamp_flags, gY, B, M, N, d, timeout_s, s, dev, 0, encode, rx, eps);
+    if (d <= 32) return grad_tc_launch_t<32, true>(Y, X, D, E, g, clamp_flags, gY, B, M, N, d, timeout_s, s, dev, 1, encode, rx, eps);
+    if (d <= 64) return grad_tc_launch_t<64, true>(Y, X, D, E, g, clamp_flags, gY, B, M, N, d, timeout_s, s, dev, 2, encode, rx, eps);
+    if (d <= 96) return grad_tc_launch_t<96, true>(Y, X, D, E, g, clamp_flags, gY, B, M, N, d, timeout_s, s, dev, 3, encode, rx, eps);
+    return grad_tc_launch_t<128, true>(Y, X, D, E, g, clamp_flags, gY, B, M, N, d, timeout_s, s, dev, 4, encode, rx, eps);
 }
 
 cudaError_t grad_x_tc_launch(const float* X, const float* Y, const float* D, const float* E, const float* g,
@@ -1027,26 +1102,14 @@ cudaError_t grad_x_tc_launch(const float* X, const float* Y, const float* D, con
                              double timeout_s, cudaStream_t s, const float* ry, float eps)
 {
     PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
-    cudaError_t e = get_encode(encode);
-    if (e != cudaSuccess) return e;
     int dev = 0;
-    e = cudaGetDevice(&dev);
+    const cudaError_t e = tc_prepare(encode, dev);
     if (e != cudaSuccess) return e;
-    if (dev < 0 || dev >= 128) return cudaErrorInvalidDevice;
-    {
-        std::lock_guard<std::mutex> lock(g_tc_mu);
-        if (g_sm_count[dev] == 0) {
-            int n = 0;
-            e = cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-            if (e != cudaSuccess) return e;
-            g_sm_count[dev] = n > 0 ? n : 1;
-        }
-    }
-    if (d <= 16) return grad_tc_launch_t<16>(X, Y, D, E, g, clamp_flags, gX, B, N, M, d, timeout_s, s, dev, 0, encode, ry, eps);
-    if (d <= 32) return grad_tc_launch_t<32>(X, Y, D, E, g, clamp_flags, gX, B, N, M, d, timeout_s, s, dev, 1, encode, ry, eps);
-    if (d <= 64) return grad_tc_launch_t<64>(X, Y, D, E, g, clamp_flags, gX, B, N, M, d, timeout_s, s, dev, 2, encode, ry, eps);
-    if (d <= 96) return grad_tc_launch_t<96>(X, Y, D, E, g, clamp_flags, gX, B, N, M, d, timeout_s, s, dev, 3, encode, ry, eps);
-    return grad_tc_launch_t<128>(X, Y, D, E, g, clamp_flags, gX, B, N, M, d, timeout_s, s, dev, 4, encode, ry, eps);
+    if (d <= 16) return grad_tc_launch_t<16, false>(X, Y, D, E, g, clamp_flags, gX, B, N, M, d, timeout_s, s, dev, 0, encode, ry, eps);
+    if (d <= 32) return grad_tc_launch_t<32, false>(X, Y, D, E, g, clamp_flags, gX, B, N, M, d, timeout_s, s, dev, 1, encode, ry, eps);
+    if (d <= 64) return grad_tc_launch_t<64, false>(X, Y, D, E, g, clamp_flags, gX, B, N, M, d, timeout_s, s, dev, 2, encode, ry, eps);
+    if (d <= 96) return grad_tc_launch_t<96, false>(X, Y, D, E, g, clamp_flags, gX, B, N, M, d, timeout_s, s, dev, 3, encode, ry, eps);
+    return grad_tc_launch_t<128, false>(X, Y, D, E, g, clamp_flags, gX, B, N, M, d, timeout_s, s, dev, 4, encode, ry, eps);
 }
 
 bool pairwise_tc_supported(const void* X, const void* Y, const void* D, int64_t B, int64_t N, int64_t M, int64_t d)

@@ -31,6 +31,13 @@ cudaError_t grad_x_tc_launch(const float* X, const float* Y, const float* D, con
                              const int* clamp_flags, float* gX, int64_t B, int64_t N, int64_t M, int64_t d,
                              double timeout_s, cudaStream_t s, const float* ry = nullptr, float eps = 0.f);
 
+// grad_Y = 2 g[b] (colsum(G) Y - G^T X) on the same kernel, E read transposed; with rx (cosine; 1 / n(x_i) per
+// row of X, B x N, 16-byte aligned): P = G^T (X / n(X)) and the cosine form of grad_X with the roles of X and
+// Y swapped. Supported when grad_tc_supported(X, Y, D, E, gY, B, N, M, d) holds.
+cudaError_t grad_y_tc_launch(const float* X, const float* Y, const float* D, const float* E, const float* g,
+                             const int* clamp_flags, float* gY, int64_t B, int64_t N, int64_t M, int64_t d,
+                             double timeout_s, cudaStream_t s, const float* rx = nullptr, float eps = 0.f);
+
 // The distance kernel family forced by sdtw_debug_force_distance_path (0: automatic, 1: no tcgen05,
 // 2: CUDA cores only).
 int distance_path();
