@@ -122,9 +122,11 @@ sdtw_status sdtw_backward(sdtw_dtype dtype, const void* D, const void* R, int64_
  * R as strip tiles: the layout in which the module path hands R from the forward to the backward (no
  * counterpart in the reference, whose module keeps the padded R of the op; the padded R stays the layout of
  * sdtw_forward / sdtw_backward). Tile (b, s, k), s = 0 .. ceil(N/32)-1, k = 0 .. M/32 (integer division), is
- * 32 x 32 elements, contiguous: row l, element x is R[32 s + l][32 k + x - l - 1] (DP indices; +inf outside
- * the band and the lengths). Each tile row is written and read as one bulk copy, against the per-element
- * copies of the padded layout. Only available when both directions run on the pair-resident kernels for the
+ * 32 x 32 elements, contiguous: row l, element x is R[32 s + l][32 k + x - l - 1] * log2(e) / gamma (DP
+ * indices; R in units of gamma ln 2, in which the dynamic program runs with two operations fewer per cell;
+ * +inf outside the band and the lengths). The costs are returned in R's own units. Each tile row is written
+ * and read as one bulk copy, against the per-element copies of the padded layout. Only available when both
+ * directions run on the pair-resident kernels for the
  * shape: sdtw_r_tiled(...) != 0 (a property of the shape, the dtype and the current device).
  *   sdtw_r_tiles_elems: elements of the tile array (16-byte aligned device memory, any initial content).
  *   sdtw_forward_tiles / sdtw_backward_tiles: sdtw_forward / sdtw_backward with R_tiles in place of R;

@@ -11,6 +11,7 @@ concurrent streams, the C ABI called directly, and failure detection without a G
 """
 
 import ctypes
+import math
 
 import numpy as np
 import pytest
@@ -295,8 +296,11 @@ def test_bad_lengths_give_nan_and_error_bit(cuda):
 @pytest.mark.parametrize("B,N,M,bw,ragged", [(3, 100, 90, -1, False), (4, 257, 130, 20, True), (5, 64, 300, 3, True),
                                              (2, 31, 33, -1, True), (3, 450, 70, 0, False), (2, 200, 512, -1, False)])
 def test_r_tiles_match_padded_r(cuda, dtype, B, N, M, bw, ragged):
-    """The module path's R tiles (sdtw_forward_tiles / sdtw_backward_tiles, pair-resident kernels) give the same
-    costs and E as the padded R, bit for bit, and every tile row holds the padded R's values."""
+    """The module path's R tiles (sdtw_forward_tiles / sdtw_backward_tiles, pair-resident kernels) give the costs
+    and E of the padded R, and every tile row holds the padded R's values in units of gamma ln 2 (the tiles
+    path runs the dynamic program in those units, so the two agree to rounding: fp64 to 1e-10; fp32 costs to
+    1e-5 relative, E to 2e-3 absolute, the size of one ulp of R ~ 1e2 divided by gamma = 0.3 and carried
+    along a path)."""
     lib = _ext.capi()
     code = 1 if dtype == torch.float64 else 0
     g = torch.Generator().manual_seed(N * 3 + M + B)
@@ -333,11 +337,17 @@ def test_r_tiles_match_padded_r(cuda, dtype, B, N, M, bw, ragged):
         lib.sdtw_debug_force_path(0)
     assert lib.sdtw_read_error_word(p(err), stream) == 0
     T.check_errors(cuda)
-    assert torch.equal(c1, c2)
-    assert torch.equal(E1, E2)
-    # Tile rows against the padded R: tile (b, s, k)[l][x] = R[32 s + l][32 k + x - l - 1] (padded row +1, column +1)
-    # wherever the tile was written (NaN marks a tile the forward did not sweep).
-    Rt_c, R2_c = Rt.cpu().numpy(), R2.cpu().numpy()
+    if dtype == torch.float64:
+        torch.testing.assert_close(c1, c2, rtol=1e-10, atol=1e-12)
+        torch.testing.assert_close(E1, E2, rtol=1e-10, atol=1e-12)
+    else:
+        torch.testing.assert_close(c1, c2, rtol=1e-5, atol=1e-6)
+        torch.testing.assert_close(E1, E2, rtol=0, atol=2e-3)
+    # Tile rows against the padded R: tile (b, s, k)[l][x] = R[32 s + l][32 k + x - l - 1] log2(e) / gamma (padded
+    # row +1, column +1) wherever the tile was written (NaN marks a tile the forward did not sweep).
+    gl = 0.3 * math.log(2.0)
+    rtol = 1e-10 if dtype == torch.float64 else 1e-5
+    Rt_c, R2_c = Rt.cpu().double().numpy() * gl, R2.cpu().double().numpy()
     written = 0
     lgrid, xgrid = np.meshgrid(np.arange(32), np.arange(32), indexing="ij")
     for b in range(B):
@@ -351,5 +361,8 @@ def test_r_tiles_match_padded_r(cuda, dtype, B, N, M, bw, ragged):
                 c = 32 * k + xgrid - lgrid - 1
                 sel = (lgrid < rows) & (c >= 0) & (c < M)
                 want = R2_c[b, 32 * s + lgrid[sel] + 1, c[sel] + 1]
-                assert np.array_equal(tile[sel], want), (b, s, k)
+                got = tile[sel]
+                assert np.array_equal(np.isinf(got), np.isinf(want)), (b, s, k)
+                fin = np.isfinite(want)
+                np.testing.assert_allclose(got[fin], want[fin], rtol=rtol, atol=1e-9)
     assert written > 0

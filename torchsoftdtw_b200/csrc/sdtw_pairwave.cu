@@ -30,14 +30,17 @@ namespace {
 
 // ---- progress barriers between strips -----------------------------------------------------------
 // A strip publishes its boundary row (forward: its last row of R; backward: the contributions its first row
-// pushes into the row above) in groups of 8 steps, and group g (= step / 8) of the strip held by warp w
-// completes mbarrier g of warp w's array once the group's values are in shared memory. Each barrier
-// completes exactly once per non-empty strip that warp sweeps (the groups the sweep does not reach are
-// completed when the strip ends), so the consumer of the strip in round r of that warp waits for parity
-// r & 1. A round can only complete a barrier after the consumer of the previous round has passed it: the
-// strip W positions later depends, through the W-1 strips between, on that consumer being 4 groups further
-// on. An empty strip (rows past the pair's length) completes nothing, and nothing waits after it. A waiting
-// warp is suspended by mbarrier.try_wait instead of polling.
+// pushes into the row above) two groups of 8 steps at a time: after the pair of groups (g, g + 1) of the
+// strip held by warp w (forward; g + 1 and g going downwards in the backward), the 16 values are in shared
+// memory and mbarrier g + 1 (forward) / g (backward) of warp w's array completes. Only those barriers, odd
+// (forward) or even (backward), are used; a consumer waits once per pair of its own groups, on the later
+// producer group the pair needs, which costs a few steps of lag and halves the waits and the publishing.
+// Each used barrier completes exactly once per non-empty strip that warp sweeps (the groups the sweep does
+// not reach are completed when the strip ends), so the consumer of the strip in round r of that warp waits
+// for parity r & 1. A round can only complete a barrier after the consumer of the previous round has passed
+// it: the strip W positions later depends, through the W-1 strips between, on that consumer being 5 groups
+// further on. An empty forward strip (rows past the pair's length) completes nothing, and nothing waits
+// after it. A waiting warp is suspended by mbarrier.try_wait instead of polling.
 __device__ __forceinline__ bool fbar_try_wait(uint32_t bar, uint32_t parity)
 {
     uint32_t ok;
@@ -359,7 +362,9 @@ __device__ __forceinline__ void fwd_tile_store(T* tile, const T* ring, int blk, 
     }
 }
 
-template <typename T, bool MASKED>
+// SCALED: the values are R in units of gamma ln 2 (fwd_cell_scaled); D arrives in its own units and is
+// scaled here.
+template <typename T, bool MASKED, bool SCALED>
 __device__ __forceinline__ void fwd_pair_steps8(T* cell, const T* top, int tau0, int A, int Z, T k, T gl,
                                                 int src_lane, bool lane0, T& outp, T& upp)
 {
@@ -371,7 +376,7 @@ __device__ __forceinline__ void fwd_pair_steps8(T* cell, const T* top, int tau0,
     for (int j = 0; j < 8; ++j) {
         const T upw = __shfl_sync(kFull, outp, src_lane);
         const T up = lane0 ? tv[j] : upw;
-        T r = fwd_cell<T>(dv[j], upp, up, outp, k, gl);
+        T r = SCALED ? fwd_cell_scaled<T>(dv[j] * k, upp, up, outp) : fwd_cell<T>(dv[j], upp, up, outp, k, gl);
         if (MASKED) {
             const int tau = tau0 + j;
             r = (tau >= A && tau <= Z) ? r : INF;
@@ -383,27 +388,38 @@ __device__ __forceinline__ void fwd_pair_steps8(T* cell, const T* top, int tau0,
     sts8(cell, dv);
 }
 
-// Groups Q0 .. Q1 of the 32 steps of block `tau0 / 32` (four groups of 8): wait for the strip above (group g of this strip
-// reads columns up to 8g + 7 of the row above, complete with the group g + 4 of the strip above), sweep,
-// publish the 8 values of the last row that the group finished. Returns false if the launch aborted.
-template <typename T, bool MASKED, int Q0, int Q1>
+// Groups Q0 .. Q1 (Q0 even, Q1 odd) of the 32 steps of block `tau0 / 32` (four groups of 8), in pairs: before
+// an even group q, wait for the strip above to have published its group g + 5 (group g of this strip reads
+// columns up to 8g + 7 of the row above, complete with the group g + 4 of the strip above; g + 5 covers
+// groups q and q + 1 with one wait); sweep the two groups; publish the 16 values of the last row that they
+// finished, completing the barrier of the odd group. Only odd barriers are used. Returns false if the
+// launch aborted.
+template <typename T, bool MASKED, int Q0, int Q1, bool SCALED>
 __device__ __forceinline__ bool fwd_pair_block(T* cell, const T* top, const T* last, T* bout, int tau0, int A, int Z,
                                                T k, T gl, bool wait_in, uint32_t bars_in, uint32_t par_in, int glast,
                                                bool publish, bool has_consumer, uint32_t bars_out, const Sync& sy,
                                                int src_lane, int lane, T& outp, T& upp)
 {
+    static_assert(Q0 % 2 == 0 && Q1 % 2 == 1, "groups come in pairs");
     const bool lane0 = lane == 0;
     const bool pub_lane = lane < kPubLanes;
     const int g0 = tau0 / 8;
 #pragma unroll
     for (int q = Q0; q <= Q1; ++q) {
-        if (wait_in && !fbar_wait_fast(bars_in + 8 * min(g0 + q + 4, glast), par_in, sy, lane)) return false;
-        fwd_pair_steps8<T, MASKED>(cell + 8 * q, top + 8 * q, tau0 + 8 * q, A, Z, k, gl, src_lane, lane0, outp, upp);
-        if (publish) {
-            // Columns tau0 + 8q - 31 .. tau0 + 8q - 24 of the last row, written by lane 31 above.
+        if ((q & 1) == 0 && wait_in && !fbar_wait_fast(bars_in + 8 * min(g0 + q + 5, glast), par_in, sy, lane))
+            return false;
+        fwd_pair_steps8<T, MASKED, SCALED>(cell + 8 * q, top + 8 * q, tau0 + 8 * q, A, Z, k, gl, src_lane, lane0, outp,
+                                           upp);
+        if (publish && (q & 1) == 1) {
+            // Columns tau0 + 8(q-1) - 31 .. tau0 + 8q - 24 of the last row (groups q - 1 and q), written by lane
+            // 31 above: 8 lanes, 2 values each, then each arrives once.
             __syncwarp();
-            const T v = last[8 * q + (lane & (kPubLanes - 1))];
-            if (pub_lane && has_consumer) bout[tau0 + 8 * q + lane - 31 + kBufPad] = v;
+            const T v0 = last[8 * (q - 1) + (lane & (kPubLanes - 1))];
+            const T v1 = last[8 * q + (lane & (kPubLanes - 1))];
+            if (pub_lane && has_consumer) {
+                bout[tau0 + 8 * (q - 1) + lane - 31 + kBufPad] = v0;
+                bout[tau0 + 8 * q + lane - 31 + kBufPad] = v1;
+            }
             fbar_arrive_n_if(bars_out + 8 * (g0 + q), 1, pub_lane);
         }
     }
@@ -421,7 +437,10 @@ __device__ __forceinline__ bool fwd_pair_block(T* cell, const T* top, const T* l
 // FUSED (float only, tiles only): D comes from fused_rect instead of a.D. Rectangle K lands in the slots of
 // blocks K and K + 1, so it is computed after block K - 1 has written back its slot and before block K starts
 // (rectangles k0 - 1 and k0 before the first block).
-template <typename T, int MC, bool FUSED>
+//
+// SCALED (tiles only): R is kept, and written to the tiles, in units of gamma ln 2 (k R, k = log2(e) / gamma);
+// the cost is converted back (times gamma ln 2) when the terminal cell writes it.
+template <typename T, int MC, bool FUSED, bool SCALED>
 __device__ bool fwd_pair_strip(const PairFwdArgs<T>& a, T* ring, const T* bin, uint32_t bars_in, uint32_t par_in,
                                T* bout, uint32_t bars_out, const float* y2, int64_t b, int s, int lane)
 {
@@ -514,7 +533,9 @@ __device__ bool fwd_pair_strip(const PairFwdArgs<T>& a, T* ring, const T* bin, u
 
     const int glast = a.G - 1;
     const bool wait_in = s > 0;
-    if (wait_in && !fbar_wait(bars_in + 8 * min(4 * k0 + 4, glast), par_in, a.sy, lane)) return false;
+    // (Group 4 k0 + 4 of the strip above holds the values the first group reads; its barriers complete in
+    // pairs, on the odd group.)
+    if (wait_in && !fbar_wait(bars_in + 8 * min(4 * k0 + 5, glast), par_in, a.sy, lane)) return false;
     T upp = lane == 0 ? bin[32 * k0 - 1 + kBufPad] : INF;  // lane 0's diagonal predecessor (column 32*k0 - 2)
     T outp = INF;
     const int src_lane = (lane + 31) & 31;
@@ -534,10 +555,10 @@ __device__ bool fwd_pair_strip(const PairFwdArgs<T>& a, T* ring, const T* bin, u
         const T* top = bin + tau0 + kBufPad;
         const T* last = ring + 31 * RS + (blk & 1) * 32;  // the strip's last row, positions tau0 ..
         const bool ok = (tau0 >= Amax && tau0 + 31 <= Zmin)
-                            ? fwd_pair_block<T, false, 0, 3>(cell, top, last, bout, tau0, A, Z, a.k, a.gl, wait_in,
+                            ? fwd_pair_block<T, false, 0, 3, SCALED>(cell, top, last, bout, tau0, A, Z, a.k, a.gl, wait_in,
                                                              bars_in, par_in, glast, !skip, has_consumer, bars_out,
                                                              a.sy, src_lane, lane, outp, upp)
-                            : fwd_pair_block<T, true, 0, 3>(cell, top, last, bout, tau0, A, Z, a.k, a.gl, wait_in,
+                            : fwd_pair_block<T, true, 0, 3, SCALED>(cell, top, last, bout, tau0, A, Z, a.k, a.gl, wait_in,
                                                             bars_in, par_in, glast, !skip, has_consumer, bars_out,
                                                             a.sy, src_lane, lane, outp, upp);
         if (!ok) return false;
@@ -547,7 +568,7 @@ __device__ bool fwd_pair_strip(const PairFwdArgs<T>& a, T* ring, const T* bin, u
         else
             fwd_pair_store<T>(Rrow, pitch, M, ring, blk, nmat, lane, a.xR, a.sy.err);
         if (blk == bstar && lane == lstar && SDTW_IN_BOUNDS(a.xC, a.costs + b, sizeof(T), a.sy.err))
-            a.costs[b] = cell[tstar - tau0];
+            a.costs[b] = SCALED ? cell[tstar - tau0] * a.gl : cell[tstar - tau0];
         __syncwarp();
         if constexpr (FUSED) {
             if (blk + 1 <= k1) {
@@ -561,15 +582,15 @@ __device__ bool fwd_pair_strip(const PairFwdArgs<T>& a, T* ring, const T* bin, u
         if (has_consumer)
             for (int c = 32 * k1 + 1 + lane; c + kBufPad < a.BL; c += 32) bout[c + kBufPad] = INF;
         __syncwarp();
-        // Complete the barriers of the groups this sweep did not reach (every barrier once per strip; each
+        // Complete the barriers of the groups this sweep did not reach (every odd barrier once per strip; each
         // phase expects kPubLanes arrivals).
         for (int g = lane; g < a.G; g += 32)
-            if (g < 4 * k0 || g > 4 * k1 + 3) fbar_arrive_n_if(bars_out + 8 * g, kPubLanes, true);
+            if ((g & 1) == 1 && (g < 4 * k0 || g > 4 * k1 + 3)) fbar_arrive_n_if(bars_out + 8 * g, kPubLanes, true);
     }
     return true;
 }
 
-template <typename T, int MC, bool FUSED>
+template <typename T, int MC, bool FUSED, bool SCALED>
 __global__ void __launch_bounds__(SDTW_PAIR_THREADS, SDTW_PAIR_MIN_CTAS) sdtw_fwd_pair_kernel(PairFwdArgs<T> a)
 {
     extern __shared__ __align__(16) unsigned char smem[];
@@ -629,7 +650,7 @@ __global__ void __launch_bounds__(SDTW_PAIR_THREADS, SDTW_PAIR_MIN_CTAS) sdtw_fw
         const int wp = (s + W - 1) % W;
         const T* bin = s > 0 ? bufs + static_cast<size_t>(wp) * a.BL : crow;
         const uint32_t par_in = static_cast<uint32_t>(((s - 1) / W) & 1);  // round of the strip above in its warp
-        if (!fwd_pair_strip<T, MC, FUSED>(a, ring, bin, bars + 8 * wp * a.G, par_in,
+        if (!fwd_pair_strip<T, MC, FUSED, SCALED>(a, ring, bin, bars + 8 * wp * a.G, par_in,
                                           bufs + static_cast<size_t>(warp) * a.BL, bars + 8 * warp * a.G, y2, b, s,
                                           lane))
             break;
@@ -760,7 +781,8 @@ __device__ __forceinline__ void bwd_pair_store(T* Erow, int64_t M, const T* ring
 // 8 backward steps tau = t8+7 .. t8 of one warp. A: ring row l at positions t8 .. t8+7, am1: position t8-1;
 // Bv: ring row l+1 at positions t8 .. t8+7 (R in, E out); bvv: lane 31's contributions from the strip below
 // (columns t8-31 .. t8-24); sv: the values lane 0 pushes into the row above (columns t8 .. t8+7).
-template <typename T, bool MASKED>
+// SCALED: R arrives in units of gamma ln 2 (the forward's tiles), so the weights need no product with k.
+template <typename T, bool MASKED, bool SCALED>
 __device__ __forceinline__ void bwd_pair_steps8(const T (&A)[8], T am1, T (&Bv)[8], const T (&bvv)[8], T (&sv)[8],
                                                 int t8, int Av, int Zv, T k, T seed, int src_lane, bool lane31,
                                                 T& sendv, T& pend, T& acc)
@@ -776,9 +798,9 @@ __device__ __forceinline__ void bwd_pair_steps8(const T (&A)[8], T am1, T (&Bv)[
         const T Es = acc + recv;
         const T m = Num<T>::mn(Num<T>::mn(rd, ru), rl);
         const T mc = Num<T>::mn(m, big);
-        const T ed = Num<T>::exp2_((mc - rd) * k);
-        const T eu = Num<T>::exp2_((mc - ru) * k);
-        const T el = Num<T>::exp2_((mc - rl) * k);
+        const T ed = Num<T>::exp2_(SCALED ? mc - rd : (mc - rd) * k);
+        const T eu = Num<T>::exp2_(SCALED ? mc - ru : (mc - ru) * k);
+        const T el = Num<T>::exp2_(SCALED ? mc - rl : (mc - rl) * k);
         T q = Es * Num<T>::rcp_((ed + eu) + el);
         T Eo = Es;
         if (MASKED) {
@@ -800,9 +822,11 @@ __device__ __forceinline__ void bwd_pair_steps8(const T (&A)[8], T am1, T (&Bv)[
 // The 32 steps of block tau0 / 32 as four groups of 8, top group first. Before group g (steps 8g .. 8g+7)
 // the strip below must have completed its group g - 4: lane 31 reads the contributions into columns
 // 8g - 31 .. 8g - 24, pushed by the strip below at its steps 8g - 31 .. 8g - 24 (groups g - 4 and g - 3; the
-// strip below sweeps downwards, so g - 3 completes first). `bcar` carries the contribution at column
-// 8g - 24, loaded with the group above. Returns false if the launch aborted.
-template <typename T, bool MASKED>
+// strip below sweeps downwards, so g - 3 completes first). The groups go in pairs: before an odd group g, one
+// wait on group g - 5 of the strip below covers g and g - 1; after the even group, the 16 pushes of the pair
+// are published and the even group's barrier completes (only even barriers are used). `bcar` carries the
+// contribution at column 8g - 24, loaded with the group above. Returns false if the launch aborted.
+template <typename T, bool MASKED, bool SCALED>
 __device__ __forceinline__ bool bwd_pair_block(T* ring, const T* bin, T* bout, int tau0, const Strip& st, T k, T seed,
                                                bool wait_in, uint32_t bars_in, uint32_t par_in, bool publish,
                                                uint32_t bars_out, bool slot_below_pending, const Sync& sy,
@@ -813,10 +837,12 @@ __device__ __forceinline__ bool bwd_pair_block(T* ring, const T* bin, T* bout, i
     T* rowA = ring + lane * RS + (tau0 & 32);  // ring row l, positions tau0 .. (slot of this block)
     T* rowB = rowA + RS;                       // ring row l + 1
     const int g0 = tau0 / 8;
+    T svp[8];  // the pushes of the odd group, published with the even group below it
 #pragma unroll
     for (int q = 3; q >= 0; --q) {
         const int t8 = tau0 + 8 * q;
-        if (wait_in && !fbar_wait_fast(bars_in + 8 * max(g0 + q - 4, 0), par_in, sy, lane)) return false;
+        if ((q & 1) == 1 && wait_in && !fbar_wait_fast(bars_in + 8 * max(g0 + q - 5, 0), par_in, sy, lane))
+            return false;
         if (q == 0 && slot_below_pending) {  // position tau0 - 1 lies in the slot of the block below
             cp_async_wait<0>();
             __syncwarp();
@@ -834,12 +860,21 @@ __device__ __forceinline__ bool bwd_pair_block(T* ring, const T* bin, T* bout, i
             bvv[7] = bcar;
             bcar = v[0];
         }
-        bwd_pair_steps8<T, MASKED>(A, am1, Bv, bvv, sv, t8, st.A, st.Z, k, seed, src_lane, lane31, sendv, pend, acc);
+        bwd_pair_steps8<T, MASKED, SCALED>(A, am1, Bv, bvv, sv, t8, st.A, st.Z, k, seed, src_lane, lane31, sendv, pend,
+                                           acc);
         __syncwarp();  // every lane has read ring row l+1 [t8, t8+8) (its A) before lane l overwrites it
         sts8(rowB + 8 * q, Bv);
         if (publish) {
-            if (lane == 0) sts8(bout + t8 + kBufPad, sv);
-            fbar_arrive_n_if(bars_out + 8 * (g0 + q), 1, lane == 0);
+            if (q & 1) {
+#pragma unroll
+                for (int j = 0; j < 8; ++j) svp[j] = sv[j];
+            } else {
+                if (lane == 0) {
+                    sts8(bout + t8 + 8 + kBufPad, svp);
+                    sts8(bout + t8 + kBufPad, sv);
+                }
+                fbar_arrive_n_if(bars_out + 8 * (g0 + q), 1, lane == 0);
+            }
         }
     }
     return true;
@@ -847,7 +882,7 @@ __device__ __forceinline__ bool bwd_pair_block(T* ring, const T* bin, T* bout, i
 
 // One strip of the backward; `t` is its position in sweep order (strip S-1-t). Returns false if the
 // launch aborted.
-template <typename T, int MC>
+template <typename T, int MC, bool SCALED>
 __device__ bool bwd_pair_strip(const PairBwdArgs<T>& a, T* ring, const T* bin, uint32_t bars_in, uint32_t par_in,
                                const T* zrow, T* bout, uint32_t bars_out, int64_t b, int s, int lane)
 {
@@ -865,7 +900,8 @@ __device__ bool bwd_pair_strip(const PairBwdArgs<T>& a, T* ring, const T* bin, u
         // non-empty strips in later rounds: complete every barrier once here too, so that a warp's barrier
         // phases keep counting its rounds (nothing waits on these arrivals: the strip above an empty strip
         // has no producer).
-        for (int g = lane; g < a.G; g += 32) fbar_arrive_n_if(bars_out + 8 * g, 1, true);
+        for (int g = lane; g < a.G; g += 32)
+            if ((g & 1) == 0) fbar_arrive_n_if(bars_out + 8 * g, 1, true);
         return true;
     }
     const int k0 = st.c_begin >> 5;
@@ -930,17 +966,19 @@ __device__ bool bwd_pair_strip(const PairBwdArgs<T>& a, T* ring, const T* bin, u
         __syncwarp();
         const int tau0 = 32 * blk;
         if (first) {
-            if (has_producer && !fbar_wait_fast(bars_in + 8 * max(4 * k1 + 3 - 4, 0), par_in, a.sy, lane))
+            // Group 4 k1 - 1 of the strip below holds the carry; its barrier completes with the pair's even
+            // group 4 k1 - 2.
+            if (has_producer && !fbar_wait_fast(bars_in + 8 * max(4 * k1 - 2, 0), par_in, a.sy, lane))
                 return false;
             bcar = bin[32 * k1 + kBufPad];
             first = false;
         }
         const bool below = blk - 1 >= kmin;
         const bool ok = (tau0 >= st.Amax && tau0 + 31 <= st.Zmin)
-                            ? bwd_pair_block<T, false>(ring, bin, bout, tau0, st, a.k, seed, has_producer, bars_in,
+                            ? bwd_pair_block<T, false, SCALED>(ring, bin, bout, tau0, st, a.k, seed, has_producer, bars_in,
                                                        par_in, publish, bars_out, below, a.sy, src_lane, lane, sendv,
                                                        pend, acc, bcar)
-                            : bwd_pair_block<T, true>(ring, bin, bout, tau0, st, a.k, seed, has_producer, bars_in,
+                            : bwd_pair_block<T, true, SCALED>(ring, bin, bout, tau0, st, a.k, seed, has_producer, bars_in,
                                                       par_in, publish, bars_out, below, a.sy, src_lane, lane, sendv,
                                                       pend, acc, bcar);
         if (!ok) return false;
@@ -963,13 +1001,14 @@ __device__ bool bwd_pair_strip(const PairBwdArgs<T>& a, T* ring, const T* bin, u
         if (lane == 0) bout[32 * k0 - 1 + kBufPad] = pend;
         for (int c = -kBufPad + lane; c <= 32 * k0 - 2; c += 32) bout[c + kBufPad] = T(0);
         __syncwarp();
-        for (int g = lane; g < 4 * k0; g += 32) fbar_arrive_n_if(bars_out + 8 * g, 1, true);
+        for (int g = lane; g < 4 * k0; g += 32)
+            if ((g & 1) == 0) fbar_arrive_n_if(bars_out + 8 * g, 1, true);
     }
     __syncwarp();
     return true;
 }
 
-template <typename T, int MC>
+template <typename T, int MC, bool SCALED>
 __global__ void __launch_bounds__(SDTW_PAIR_THREADS, SDTW_PAIR_MIN_CTAS) sdtw_bwd_pair_kernel(PairBwdArgs<T> a)
 {
     extern __shared__ __align__(16) unsigned char smem[];
@@ -991,7 +1030,7 @@ __global__ void __launch_bounds__(SDTW_PAIR_THREADS, SDTW_PAIR_MIN_CTAS) sdtw_bw
     for (int t = warp; t < a.S; t += W) {
         const int wp = (t + W - 1) % W;
         const uint32_t par_in = static_cast<uint32_t>(((t - 1) / W) & 1);  // round of the strip below in its warp
-        if (!bwd_pair_strip<T, MC>(a, ring, bufs + static_cast<size_t>(wp) * a.BL, bars + 8 * wp * a.G, par_in, zrow,
+        if (!bwd_pair_strip<T, MC, SCALED>(a, ring, bufs + static_cast<size_t>(wp) * a.BL, bars + 8 * wp * a.G, par_in, zrow,
                                    bufs + static_cast<size_t>(warp) * a.BL, bars + 8 * warp * a.G, b, a.S - 1 - t,
                                    lane))
             break;
@@ -1015,25 +1054,34 @@ size_t pair_bwd_smem_bytes(int W, int64_t M)
            static_cast<size_t>(W) * fwd_groups(M) * 8;
 }
 
+// The kernel instantiations: M specialized (MC = kPairSpecialM) or not; R in its own units (padded R) or in
+// units of gamma ln 2 (R tiles, SCALED); the fused cost forward (float, tiles).
 template <typename T>
 cudaError_t pair_init_attrs(int max_smem)
 {
-    cudaError_t e = cudaFuncSetAttribute(sdtw_fwd_pair_kernel<T, 0, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
-    if (e != cudaSuccess) return e;
-    e = cudaFuncSetAttribute(sdtw_fwd_pair_kernel<T, kPairSpecialM, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
-    if (e != cudaSuccess) return e;
-    e = cudaFuncSetAttribute(sdtw_bwd_pair_kernel<T, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
-    if (e != cudaSuccess) return e;
-    if constexpr (sizeof(T) == 4) {
-        e = cudaFuncSetAttribute(sdtw_fwd_pair_kernel<float, 0, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 max_smem);
-        if (e != cudaSuccess) return e;
-        e = cudaFuncSetAttribute(sdtw_fwd_pair_kernel<float, kPairSpecialM, true>,
-                                 cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
+    const auto set = [max_smem](const void* f) {
+        return cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
+    };
+    const void* kernels[] = {
+        reinterpret_cast<const void*>(sdtw_fwd_pair_kernel<T, 0, false, false>),
+        reinterpret_cast<const void*>(sdtw_fwd_pair_kernel<T, kPairSpecialM, false, false>),
+        reinterpret_cast<const void*>(sdtw_fwd_pair_kernel<T, 0, false, true>),
+        reinterpret_cast<const void*>(sdtw_fwd_pair_kernel<T, kPairSpecialM, false, true>),
+        reinterpret_cast<const void*>(sdtw_bwd_pair_kernel<T, 0, false>),
+        reinterpret_cast<const void*>(sdtw_bwd_pair_kernel<T, kPairSpecialM, false>),
+        reinterpret_cast<const void*>(sdtw_bwd_pair_kernel<T, 0, true>),
+        reinterpret_cast<const void*>(sdtw_bwd_pair_kernel<T, kPairSpecialM, true>),
+    };
+    for (const void* f : kernels) {
+        const cudaError_t e = set(f);
         if (e != cudaSuccess) return e;
     }
-    return cudaFuncSetAttribute(sdtw_bwd_pair_kernel<T, kPairSpecialM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                max_smem);
+    if constexpr (sizeof(T) == 4) {
+        cudaError_t e = set(reinterpret_cast<const void*>(sdtw_fwd_pair_kernel<float, 0, true, true>));
+        if (e == cudaSuccess) e = set(reinterpret_cast<const void*>(sdtw_fwd_pair_kernel<float, kPairSpecialM, true, true>));
+        return e;
+    }
+    return cudaSuccess;
 }
 template cudaError_t pair_init_attrs<float>(int);
 template cudaError_t pair_init_attrs<double>(int);
@@ -1041,15 +1089,26 @@ template cudaError_t pair_init_attrs<double>(int);
 template <typename T>
 cudaError_t pair_regs(bool backward, int& regs)
 {
-    // The largest count over the kernel's instantiations (the one specialized on M can need more).
-    cudaFuncAttributes fa, fb;
-    cudaError_t e = backward ? cudaFuncGetAttributes(&fa, sdtw_bwd_pair_kernel<T, 0>)
-                             : cudaFuncGetAttributes(&fa, sdtw_fwd_pair_kernel<T, 0, false>);
-    if (e == cudaSuccess)
-        e = backward ? cudaFuncGetAttributes(&fb, sdtw_bwd_pair_kernel<T, kPairSpecialM>)
-                     : cudaFuncGetAttributes(&fb, sdtw_fwd_pair_kernel<T, kPairSpecialM, false>);
-    regs = e == cudaSuccess ? (fa.numRegs > fb.numRegs ? fa.numRegs : fb.numRegs) : 0;
-    return e;
+    // The largest count over the direction's instantiations (the ones specialized on M can need more).
+    const void* fwd[] = {reinterpret_cast<const void*>(sdtw_fwd_pair_kernel<T, 0, false, false>),
+                         reinterpret_cast<const void*>(sdtw_fwd_pair_kernel<T, kPairSpecialM, false, false>),
+                         reinterpret_cast<const void*>(sdtw_fwd_pair_kernel<T, 0, false, true>),
+                         reinterpret_cast<const void*>(sdtw_fwd_pair_kernel<T, kPairSpecialM, false, true>)};
+    const void* bwd[] = {reinterpret_cast<const void*>(sdtw_bwd_pair_kernel<T, 0, false>),
+                         reinterpret_cast<const void*>(sdtw_bwd_pair_kernel<T, kPairSpecialM, false>),
+                         reinterpret_cast<const void*>(sdtw_bwd_pair_kernel<T, 0, true>),
+                         reinterpret_cast<const void*>(sdtw_bwd_pair_kernel<T, kPairSpecialM, true>)};
+    regs = 0;
+    for (const void* f : backward ? bwd : fwd) {
+        cudaFuncAttributes fa;
+        const cudaError_t e = cudaFuncGetAttributes(&fa, f);
+        if (e != cudaSuccess) {
+            regs = 0;
+            return e;
+        }
+        regs = fa.numRegs > regs ? fa.numRegs : regs;
+    }
+    return cudaSuccess;
 }
 template cudaError_t pair_regs<float>(bool, int&);
 template cudaError_t pair_regs<double>(bool, int&);
@@ -1059,8 +1118,8 @@ size_t pair_fused_smem_bytes(int W, int64_t M) { return fused_smem_bytes(W, M); 
 cudaError_t pair_fused_regs(int& regs)
 {
     cudaFuncAttributes fa, fb;
-    cudaError_t e = cudaFuncGetAttributes(&fa, sdtw_fwd_pair_kernel<float, 0, true>);
-    if (e == cudaSuccess) e = cudaFuncGetAttributes(&fb, sdtw_fwd_pair_kernel<float, kPairSpecialM, true>);
+    cudaError_t e = cudaFuncGetAttributes(&fa, sdtw_fwd_pair_kernel<float, 0, true, true>);
+    if (e == cudaSuccess) e = cudaFuncGetAttributes(&fb, sdtw_fwd_pair_kernel<float, kPairSpecialM, true, true>);
     regs = e == cudaSuccess ? (fa.numRegs > fb.numRegs ? fa.numRegs : fb.numRegs) : 0;
     return e;
 }
@@ -1124,10 +1183,19 @@ cudaError_t pair_forward(const T* D, T* R, T* Rt, T* costs, const void* lx, cons
     a.sy = sy;
     a.inject = inject;
     count_launch();
-    if (M == kPairSpecialM)
-        sdtw_fwd_pair_kernel<T, kPairSpecialM, false><<<static_cast<unsigned>(B), W * 32, pair_fwd_smem_bytes<T>(W, M), stream>>>(a);
-    else
-        sdtw_fwd_pair_kernel<T, 0, false><<<static_cast<unsigned>(B), W * 32, pair_fwd_smem_bytes<T>(W, M), stream>>>(a);
+    const dim3 grid(static_cast<unsigned>(B)), block(static_cast<unsigned>(W * 32));
+    const size_t smem = pair_fwd_smem_bytes<T>(W, M);
+    if (Rt != nullptr) {  // R stays in the library: units of gamma ln 2
+        if (M == kPairSpecialM)
+            sdtw_fwd_pair_kernel<T, kPairSpecialM, false, true><<<grid, block, smem, stream>>>(a);
+        else
+            sdtw_fwd_pair_kernel<T, 0, false, true><<<grid, block, smem, stream>>>(a);
+    } else {
+        if (M == kPairSpecialM)
+            sdtw_fwd_pair_kernel<T, kPairSpecialM, false, false><<<grid, block, smem, stream>>>(a);
+        else
+            sdtw_fwd_pair_kernel<T, 0, false, false><<<grid, block, smem, stream>>>(a);
+    }
     return cudaGetLastError();
 }
 cudaError_t pair_forward_fused(const float* X, const float* Y, int64_t d, float* Rt, float* costs, uint32_t* cmask,
@@ -1170,9 +1238,9 @@ cudaError_t pair_forward_fused(const float* X, const float* Y, int64_t d, float*
     a.f.xFlags = Extent{cflags, static_cast<size_t>(B) * sizeof(int)};
     count_launch();
     if (M == kPairSpecialM)
-        sdtw_fwd_pair_kernel<float, kPairSpecialM, true><<<static_cast<unsigned>(B), W * 32, fused_smem_bytes(W, M), stream>>>(a);
+        sdtw_fwd_pair_kernel<float, kPairSpecialM, true, true><<<static_cast<unsigned>(B), W * 32, fused_smem_bytes(W, M), stream>>>(a);
     else
-        sdtw_fwd_pair_kernel<float, 0, true><<<static_cast<unsigned>(B), W * 32, fused_smem_bytes(W, M), stream>>>(a);
+        sdtw_fwd_pair_kernel<float, 0, true, true><<<static_cast<unsigned>(B), W * 32, fused_smem_bytes(W, M), stream>>>(a);
     return cudaGetLastError();
 }
 
@@ -1210,10 +1278,19 @@ cudaError_t pair_backward(const T* R, const T* Rt, T* E, const void* lx, const v
     a.sy = sy;
     a.inject = inject;
     count_launch();
-    if (M == kPairSpecialM)
-        sdtw_bwd_pair_kernel<T, kPairSpecialM><<<static_cast<unsigned>(B), W * 32, pair_bwd_smem_bytes<T>(W, M), stream>>>(a);
-    else
-        sdtw_bwd_pair_kernel<T, 0><<<static_cast<unsigned>(B), W * 32, pair_bwd_smem_bytes<T>(W, M), stream>>>(a);
+    const dim3 grid(static_cast<unsigned>(B)), block(static_cast<unsigned>(W * 32));
+    const size_t smem = pair_bwd_smem_bytes<T>(W, M);
+    if (Rt != nullptr) {  // the forward's tiles, in units of gamma ln 2
+        if (M == kPairSpecialM)
+            sdtw_bwd_pair_kernel<T, kPairSpecialM, true><<<grid, block, smem, stream>>>(a);
+        else
+            sdtw_bwd_pair_kernel<T, 0, true><<<grid, block, smem, stream>>>(a);
+    } else {
+        if (M == kPairSpecialM)
+            sdtw_bwd_pair_kernel<T, kPairSpecialM, false><<<grid, block, smem, stream>>>(a);
+        else
+            sdtw_bwd_pair_kernel<T, 0, false><<<grid, block, smem, stream>>>(a);
+    }
     return cudaGetLastError();
 }
 template cudaError_t pair_backward<float>(const float*, const float*, float*, const void*, const void*, int, int64_t,

@@ -47,8 +47,9 @@ int pair_warps(bool backward, int64_t N, int64_t M, int cap, size_t budget);
 bool pair_keys_fit(int64_t N, int64_t M);
 
 // R as strip tiles (the module path's layout between the pair-resident forward and backward): tile (b, s, k)
-// is 32 x 32 elements, row l holding R[32 s + l][32 k + x - l - 1] at x = 0..31 (+inf outside the band and the
-// lengths); tiles of blocks a strip does not sweep are never written. Blocks per strip: pair_tile_blocks(M).
+// is 32 x 32 elements, row l holding R[32 s + l][32 k + x - l - 1] log2(e) / gamma at x = 0..31 (R in units of
+// gamma ln 2; +inf outside the band and the lengths); tiles of blocks a strip does not sweep are never
+// written. Blocks per strip: pair_tile_blocks(M).
 inline int pair_tile_blocks(int64_t M) { return static_cast<int>((M + 31) / 32) + 1; }
 
 // Fused squared-L2 forward (fp32, R as strip tiles): the cost matrix D = (|x|^2 + |y|^2) - 2 x.y, clamped

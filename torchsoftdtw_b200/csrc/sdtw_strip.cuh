@@ -86,4 +86,22 @@ __device__ __forceinline__ T fwd_cell(T d, T diag, T up, T left, T k, T gl)
     return fma(-gl, Num<T>::log2_(sum), m) + d;
 }
 
+// The same cell with every R and D value in units of gamma ln 2 (u = R log2(e) / gamma, d = D log2(e) /
+// gamma): u = (m + d) - log2(1 + 2^(m - x) + 2^(m - y)). The exponents need no product with 1 / gamma and
+// m + d is formed beside the exponentials, so the step's dependency chain is two operations shorter. Used
+// where R stays inside the library (the R tiles between the pair-resident forward and backward).
+template <typename T>
+__device__ __forceinline__ T fwd_cell_scaled(T d, T diag, T up, T left)
+{
+    const T a = Num<T>::mn(up, left);
+    const T y = Num<T>::mx(up, left);
+    const T m = Num<T>::mn(a, diag);
+    const T x = Num<T>::mx(a, diag);
+    const T mc = Num<T>::mn(m, Num<T>::big());
+    const T e1 = Num<T>::exp2_(mc - x);
+    const T e2 = Num<T>::exp2_(mc - y);
+    const T sum = (T(1) + e1) + e2;
+    return (m + d) - Num<T>::log2_(sum);
+}
+
 }  // namespace sdtw
