@@ -38,6 +38,11 @@ import sys
 import tempfile
 import time
 
+# NCCL prints its version banner on stdout when NCCL_DEBUG=VERSION (the default of some images), and it reads
+# the variable when torch loads it; the bench prints one JSON line on stdout.
+if os.environ.get("NCCL_DEBUG", "").upper() == "VERSION":
+    os.environ["NCCL_DEBUG"] = "WARN"
+
 import torch
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
@@ -373,14 +378,25 @@ def main():
     result["step_roofline"] = step_roofline(w, value, "fwd+bwd", sms)
 
     if world > 1 and args.loss_allreduce:
-        # The same steps, each followed by the global loss sum (sharding.all_reduce_loss: one fp32 scalar,
-        # all_reduce(SUM) over NCCL); the end event follows the collective on the step's stream.
+        # The same steps with the global loss sum (sharding.all_reduce_loss: one fp32 scalar, all_reduce(SUM)
+        # over NCCL). after_backward: the collective follows the step; overlapped: it starts when the forward
+        # has produced the loss and runs beside the backward, joined before the step's end event.
         def step_global():
             return sharding.all_reduce_loss(step())
 
+        def step_global_overlapped():
+            Xd.grad = None
+            loss = module(Xd, Yd, lxd, lyd).sum()
+            pending = sharding.all_reduce_loss(loss, async_op=True)
+            loss.backward()
+            return pending.wait()
+
         ms2, _ = timed(step_global, steps, 2)
+        ms3, _ = timed(step_global_overlapped, steps, 2)
         result["with_loss_allreduce"] = {"value": cells_global * steps / (ms2 / 1e3), "unit": "cells/s",
-                                         "ms_per_step": ms2 / steps}
+                                         "ms_per_step": ms2 / steps,
+                                         "overlapped": {"value": cells_global * steps / (ms3 / 1e3),
+                                                        "ms_per_step": ms3 / steps}}
 
     if world > 1 and not args.no_weak:
         # Secondary: weak scaling, every rank a full batch of B pairs of its own (seed = rank).

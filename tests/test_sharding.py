@@ -40,8 +40,10 @@ def _worker(rank, world, port, B, out):
         global_costs = torch.rand(B, generator=g, dtype=torch.float64)
         local = sharding.shard(global_costs, world, rank)
         total = sharding.all_reduce_loss(local.sum())
+        pending = sharding.all_reduce_loss(local.sum(), async_op=True)  # the overlapped form of the bench
+        total_async = pending.wait()
         gathered = sharding.gather_costs(local, B)
-        out[rank] = (float(total), torch.equal(gathered, global_costs), float(global_costs.sum()))
+        out[rank] = (float(total), torch.equal(gathered, global_costs), float(global_costs.sum()), float(total_async))
     finally:
         dist.destroy_process_group()
 
@@ -59,9 +61,10 @@ def test_two_rank_loss_and_gather(B):
         p.join(timeout=120)
         assert p.exitcode == 0
     for r in range(2):
-        total, same, expected = out[r]
+        total, same, expected, total_async = out[r]
         assert same
         assert abs(total - expected) < 1e-12
+        assert total_async == total
 
 
 def _lonely(port, q):

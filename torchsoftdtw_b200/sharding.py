@@ -5,7 +5,8 @@ rank runs the operator on its own slice with its inputs resident in its own HBM:
 collective at all. Two optional collectives exist for callers that want global results:
 
 * :func:`all_reduce_loss` — the global loss sum (one scalar, ``all_reduce(SUM)``; NCCL over NVLink on
-  CUDA, gloo on CPU);
+  CUDA, gloo on CPU); with ``async_op=True`` it returns at once with a handle, so the collective can run
+  while the backward's kernels do (start it after the forward, wait on the handle after the backward);
 * :func:`gather_costs` — every pair's cost on every rank (``all_gather`` of padded slices).
 """
 
@@ -30,11 +31,27 @@ def shard(t: torch.Tensor, world: int, rank: int) -> torch.Tensor:
     return t[b:e]
 
 
-def all_reduce_loss(local_sum: torch.Tensor, group=None) -> torch.Tensor:
-    """Sum of every rank's local loss (in place on a clone; the input is left as it was)."""
+class PendingSum:
+    """An all-reduce in flight: :meth:`wait` makes the current stream wait for it and returns the sum."""
+
+    def __init__(self, out: torch.Tensor, work):
+        self._out = out
+        self._work = work
+
+    def wait(self) -> torch.Tensor:
+        self._work.wait()
+        return self._out
+
+
+def all_reduce_loss(local_sum: torch.Tensor, group=None, async_op: bool = False):
+    """Sum of every rank's local loss (in place on a clone; the input is left as it was).
+
+    async_op=True returns a :class:`PendingSum` instead: the collective is enqueued behind the work already
+    on the current stream (the forward that produced ``local_sum``) and runs beside whatever is enqueued
+    next (the backward), until ``wait()`` joins it."""
     out = local_sum.detach().clone()
-    dist.all_reduce(out, op=dist.ReduceOp.SUM, group=group)
-    return out
+    work = dist.all_reduce(out, op=dist.ReduceOp.SUM, group=group, async_op=async_op)
+    return PendingSum(out, work) if async_op else out
 
 
 def gather_costs(local_costs: torch.Tensor, B: int, group=None) -> torch.Tensor:
