@@ -123,6 +123,36 @@ def test_c_abi_rejects_bad_arguments_before_launching(lib):
     assert lib.sdtw_grad_dist_workspace_bytes(256, 512, 1) >= 256 * 512 * 8
 
 
+def test_fused_cost_forward_arguments(lib):
+    """The fused cost forward's helpers and argument checks (no device needed: nothing is launched)."""
+    null = None
+    assert lib.sdtw_clamp_mask_words(256, 512, 512) == 256 * 512 * 16
+    assert lib.sdtw_clamp_mask_words(2, 3, 33) == 2 * 3 * 2
+    assert lib.sdtw_clamp_mask_words(-1, 3, 3) == 0
+    # d must be a positive multiple of 16, and without a device no shape is accepted
+    assert lib.sdtw_forward_l2_fused_ok(256, 512, 512, 8) == 0
+    assert lib.sdtw_forward_l2_fused_ok(256, 512, 512, 0) == 0
+    assert lib.sdtw_forward_l2_tiles(null, null, 1, 4, 4, 16, null, null, 0, 0.0, -1, null, null, null, null, null, 0,
+                                     null, null) == -1  # gamma
+    assert lib.sdtw_forward_l2_tiles(null, null, 0, 4, 4, 16, null, null, 0, 1.0, -1, null, null, null, null, null, 0,
+                                     null, null) == 0  # empty batch
+    assert lib.sdtw_apply_clamp_mask(null, null, null, -1, 4, 4, null) == -1
+    assert lib.sdtw_apply_clamp_mask(null, null, null, 0, 4, 4, null) == 0
+    assert lib.sdtw_apply_clamp_mask(null, null, null, 2, 4, 4, null) == -1  # missing buffers
+
+
+def test_fused_cost_policy_is_opt_in(monkeypatch):
+    import torch
+
+    from torchsoftdtw_b200 import _ext
+
+    monkeypatch.delenv(_ext.FUSED_COST_ENV, raising=False)
+    assert not _ext.l2_fused(256, 512, 512, 64, torch.float32, "cuda")
+    monkeypatch.setenv(_ext.FUSED_COST_ENV, "1")
+    assert not _ext.l2_fused(256, 512, 512, 64, torch.float64, "cuda")  # fp32 only
+    assert not _ext.l2_fused(256, 512, 512, 64, torch.float32, "cpu")
+
+
 def test_workspace_sizes(lib):
     f = lib.sdtw_forward_workspace_bytes(256, 512, 512, 0)
     b = lib.sdtw_backward_workspace_bytes(256, 512, 512, 0)
