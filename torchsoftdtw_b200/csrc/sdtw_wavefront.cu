@@ -670,7 +670,16 @@ int choose_pair_warps(const DeviceInfo& di, bool backward, int64_t B, int64_t N,
     // strips): every strip of a pair then runs at once and a pair takes its dependency chain's time, where the
     // strip-ticket kernels' coarser hand-over through L2 makes the chain longer (128 x 512 x 512 forward:
     // strip-ticket 0.233 ms).
-    if (g_force_path != 2 && ((B < di.sms && strips_of(N) > kPairMaxWarps) || strips_of(N) < 6)) return 0;
+    // Pairs of more than 16 strips in batches smaller than the SM count: the pair-resident kernels sweep the
+    // strips in rounds on one SM per pair and still win while the boundary rows leave room for enough warps
+    // (fp32, forward / backward, pair-resident against strip-ticket: 64 x 768 x 768 0.258 / 0.231 against
+    // 0.326 / 0.326 ms; 16 x 2048 x 2048 band 128 0.613 / 0.590 against 0.736 / 0.743; 32 x 1024 x 1024
+    // 0.412 / 0.378 against 0.389 / 0.395); with 128 strips of 4096 columns the strip-ticket kernels spread
+    // the work over every SM and are faster (16 x 4096 x 4096 band 256: 2.20 / 2.64 against 1.63 / 1.59 ms).
+    // (fp64 rings and rows are twice the size: those batches stay on the strip-ticket kernels.)
+    const bool many_strips =
+        B < di.sms && strips_of(N) > kPairMaxWarps && (strips_of(N) > 64 || M > 2048 || sizeof(T) == 8);
+    if (g_force_path != 2 && (many_strips || strips_of(N) < 6)) return 0;
     if (B > 0x7fffffff || !pair_keys_fit(N, M)) return 0;
     // Enough CTAs per SM for the whole batch to be resident at once (up to 8), each as wide as its
     // share of the SM's shared memory and registers allows.
