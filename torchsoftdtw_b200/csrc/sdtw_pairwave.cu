@@ -4,10 +4,11 @@
 // w, w+W, ...; the backward walks the strips bottom-up), and consecutive strips hand their boundary
 // row to each other through shared memory:
 //   * every warp owns a full-width boundary row in shared memory (forward: the last row of R of its
-//     current strip; backward: the contributions its first row pushes into the row above) and a
-//     progress counter. The producing lane writes a value per step; after every 8 steps the counter is
-//     raised with st.release.cta, and the consuming warp reads it with ld.acquire.cta before it reads
-//     the 8 values it needs. A strip therefore starts 40 steps after the strip it depends on.
+//     current strip; backward: the contributions its first row pushes into the row above) and one
+//     mbarrier per group of 8 steps. After every second group the 16 new values are copied into the row
+//     and the group's barrier completes; the consuming warp waits on it (mbarrier.try_wait, bounded)
+//     once per pair of its own groups. A strip therefore starts about 48 steps after the strip it
+//     depends on.
 //   * A warp only ever waits on a strip with a smaller index in sweep order, which is always held by a
 //     running warp of the same CTA, so the CTA cannot deadlock. A boundary row is rewritten (by the
 //     strip W positions later) only after a chain of acquires through every warp in between, so each
