@@ -12,8 +12,11 @@
 //     forward passes each strip's last row of R down, the backward passes the contributions pushed
 //     from a strip's first row up. The buffer starts as an all-ones NaN pattern and every value is
 //     written once with st.relaxed, so a consumer knows a value has arrived when it is no longer the
-//     pattern: no flags, no fences. Consumers prefetch the next block's boundary values one block
-//     ahead; every wait is bounded in time (the launch aborts with SDTW_ERR_TIMEOUT, never hangs).
+//     pattern: no flags, no fences. Values are handed over per group of steps (8 steps in the backward
+//     and the fp64 forward, a 32-step block in the fp32 forward): after each group the producer publishes
+//     the boundary values it finished, and before each group the consumer waits for the ones that group
+//     reads, having read them from L2 ahead of time; every wait is bounded in time (the launch aborts with
+//     SDTW_ERR_TIMEOUT, never hangs).
 //   * Per warp, a shared-memory ring of 4 chunks x 32 columns holds the operands of the swept rows
 //     (forward: D, overwritten in place by R; backward: R, overwritten in place by E); chunks are
 //     prefetched two blocks ahead with cp.async and written back with coalesced row stores.
@@ -61,9 +64,9 @@ struct FwdArgs {
     int vec;          // D rows are 16-byte aligned: 16-byte cp.async
 };
 
-// 32 forward steps tau = tau0 .. tau0+31 of one warp.
-template <typename T, bool MASKED>
-__device__ __forceinline__ void fwd_block(T* myrow, const T* top, int tau0, int lane, int A, int Z, T k, T gl,
+// The G forward steps tau = tau0 + GQ .. tau0 + GQ + G - 1 of one warp (group Q of the block at tau0).
+template <typename T, bool MASKED, int G, int Q>
+__device__ __forceinline__ void fwd_group(T* myrow, const T* top, int tau0, int lane, int A, int Z, T k, T gl,
                                           T& outp, T& upp)
 {
     const T INF = Num<T>::inf();
@@ -72,7 +75,7 @@ __device__ __forceinline__ void fwd_block(T* myrow, const T* top, int tau0, int 
     const int base = tau0 - lane;
     const T* topb = top + (tau0 & kSideMask);
 #pragma unroll
-    for (int u = 0; u < 32; ++u) {
+    for (int u = G * Q; u < G * Q + G; ++u) {
         T* cell = myrow + ((base + u) & kRingMask);
         const T d = *cell;
         const T upw = __shfl_sync(kFull, outp, src);
@@ -129,6 +132,70 @@ __device__ __forceinline__ void fwd_store_chunk(const FwdArgs<T>& a, T* Rb, cons
     T* dst = Rb + static_cast<int64_t>(st.r0 + 1) * pitch + col + 1;
     const T* srcp = ring + (col & kRingMask);
     for (int r = 0; r < st.rows; ++r) dst[r * pitch] = srcp[r * kRing];
+}
+
+// Steps per boundary hand-over in the strip-ticket forward. Groups of 8 steps cut the lag between strips
+// from 64 steps to 40 but cost each group a wait and a publish, which the short fp32 steps do not earn back.
+// Measured on one B200: fp32, 16 pairs of 4096 x 4096, band 256: 1.60 ms with whole blocks, 1.61 with groups
+// of 16, 1.68 with groups of 8; fp64, 4 pairs of 2048 x 2048: 3.99 ms with groups of 8, 4.46 with blocks.
+template <typename T>
+struct FwdGroup {
+    static constexpr int value = sizeof(T) == 8 ? 8 : 32;
+};
+
+// One block of 32 steps as 32 / G groups of G. Lane l holds in `nv` the value of the row above at column
+// tau0 + l (read from L2 ahead of time, possibly before the strip above wrote it). Group q reads columns
+// tau0 + Gq .. tau0 + Gq + G - 1 of the row above (through lane 0), complete once the strip above finished the
+// same group of the next block. Before group q the G lanes that hold them wait for their values, hand them to
+// the side ring and read the next block's value of their column ahead, and the lanes of group q + 1 re-read
+// theirs; after the group, G lanes publish the G values of the last row it finished. Returns false if the
+// launch aborted.
+template <typename T, bool MASKED, int G, int Q>
+__device__ __forceinline__ bool fwd_group_step(const FwdArgs<T>& a, T* ring, T* top, const T* bnd_in, T* bnd_out, int tau0,
+                                               const Strip& st, int plo, int phi, bool has_above, bool has_consumer,
+                                               int lane, T& nv, T& outp, T& upp)
+{
+    constexpr int NG = 32 / G;
+    const T INF = Num<T>::inf();
+    const int grp = lane / G;
+    if (has_above) {
+        const int c = tau0 + lane;
+        const bool need = c >= plo && c <= phi;
+        if (!await_boundary(nv, bnd_in + c, need && grp == Q, a.sy, lane)) return false;
+        if (grp == Q) {
+            top[c & kSideMask] = need ? nv : INF;
+            const int cn = c + 32;
+            nv = (cn >= plo && cn <= phi) ? ld_relaxed(bnd_in + cn) : INF;
+        } else if (NG > 1 && grp == (Q + 1) % NG) {
+            const int cr = Q == NG - 1 ? c + 32 : c;  // after the last group: the next block's first group
+            if (cr >= plo && cr <= phi) nv = ld_relaxed(bnd_in + cr);
+        }
+    } else if (grp == Q) {
+        top[(tau0 + lane) & kSideMask] = INF;
+    }
+    __syncwarp();
+    fwd_group<T, MASKED, G, Q>(ring + lane * kRing, top, tau0, lane, st.A, st.Z, a.k, a.gl, outp, upp);
+    __syncwarp();
+    if (has_consumer && lane < G) {
+        // Last row (lane 31) finished columns [tau0 + GQ - 31, tau0 + GQ + G - 32] in this group.
+        const int c = tau0 + G * Q - 31 + lane;
+        if (c >= st.c_begin && c <= st.c_end) st_relaxed(bnd_out + c, ring[31 * kRing + (c & kRingMask)]);
+    }
+    return true;
+}
+template <typename T, bool MASKED, int G, int Q = 0>
+__device__ __forceinline__ bool fwd_block_groups(const FwdArgs<T>& a, T* ring, T* top, const T* bnd_in, T* bnd_out,
+                                                 int tau0, const Strip& st, int plo, int phi, bool has_above,
+                                                 bool has_consumer, int lane, T& nv, T& outp, T& upp)
+{
+    if (!fwd_group_step<T, MASKED, G, Q>(a, ring, top, bnd_in, bnd_out, tau0, st, plo, phi, has_above, has_consumer,
+                                         lane, nv, outp, upp))
+        return false;
+    if constexpr (Q + 1 < 32 / G)
+        return fwd_block_groups<T, MASKED, G, Q + 1>(a, ring, top, bnd_in, bnd_out, tau0, st, plo, phi, has_above,
+                                                     has_consumer, lane, nv, outp, upp);
+    else
+        return true;
 }
 
 template <typename T>
@@ -190,28 +257,15 @@ __device__ void fwd_strip(const FwdArgs<T>& a, T* ring, T* top, int64_t b, int s
 #pragma unroll 1
     for (int blk = k0; blk <= k1; ++blk) {
         const int tau0 = 32 * blk;
-        if (s > 0) {
-            const int c = tau0 + lane;
-            const bool need = c >= plo && c <= phi;
-            if (!await_boundary(nv, bnd_in + c, need, a.sy, lane)) return;
-            top[c & kSideMask] = need ? nv : INF;
-            const int cn = c + 32;
-            nv = (cn >= plo && cn <= phi) ? ld_relaxed(bnd_in + cn) : INF;
-        } else {
-            top[(tau0 + lane) & kSideMask] = INF;
-        }
         cp_async_wait<2>();
         __syncwarp();
-        if (tau0 >= st.Amax && tau0 + 31 <= st.Zmin)
-            fwd_block<T, false>(myrow, top, tau0, lane, st.A, st.Z, a.k, a.gl, outp, upp);
-        else
-            fwd_block<T, true>(myrow, top, tau0, lane, st.A, st.Z, a.k, a.gl, outp, upp);
-        __syncwarp();
-        if (has_consumer) {
-            // Last row (lane 31) finished columns [tau0-31, tau0] in this block.
-            const int c = tau0 - 31 + lane;
-            if (c >= st.c_begin && c <= st.c_end) st_relaxed(bnd_out + c, ring[31 * kRing + (c & kRingMask)]);
-        }
+        const bool full = tau0 >= st.Amax && tau0 + 31 <= st.Zmin;
+        constexpr int G = FwdGroup<T>::value;
+        if (!(full ? fwd_block_groups<T, false, G>(a, ring, top, bnd_in, bnd_out, tau0, st, plo, phi, s > 0,
+                                                    has_consumer, lane, nv, outp, upp)
+                   : fwd_block_groups<T, true, G>(a, ring, top, bnd_in, bnd_out, tau0, st, plo, phi, s > 0,
+                                                   has_consumer, lane, nv, outp, upp)))
+            return;
         if (blk - 1 >= k0) fwd_store_chunk<T>(a, Rb, ring, blk - 1, st, lane);
         __syncwarp();
         if (blk + 3 <= kc) fwd_load_chunk<T>(a, Db, ring, blk + 3, st.rows, lane);
@@ -280,8 +334,9 @@ struct BwdArgs {
     int inject_skip;
 };
 
-template <typename T, bool MASKED>
-__device__ __forceinline__ void bwd_block(T* rowA, T* rowB, const T* bndring, T* sendring, int tau0, int lane, int A,
+// The 8 backward steps tau = tau0 + 8Q + 7 down to tau0 + 8Q of one warp (group Q of the block at tau0).
+template <typename T, bool MASKED, int Q>
+__device__ __forceinline__ void bwd_group(T* rowA, T* rowB, const T* bndring, T* sendring, int tau0, int lane, int A,
                                           int Z, T k, T seed, T& upc, T& sendv, T& pend, T& acc)
 {
     const T big = Num<T>::big();
@@ -292,7 +347,7 @@ __device__ __forceinline__ void bwd_block(T* rowA, T* rowB, const T* bndring, T*
     // Boundary values of lane 31's column c live at (c + 31) & 63, so a block reads them without wrapping.
     const T* bndb = bndring + (tau0 & kSideMask);
 #pragma unroll
-    for (int u = 31; u >= 0; --u) {
+    for (int u = 8 * Q + 7; u >= 8 * Q; --u) {
         const int c = base + u;
         const int cm = (c - 1) & kRingMask;
         const T rd = rowA[cm];  // R[i-1][c-1]
@@ -360,6 +415,64 @@ __device__ __forceinline__ void bwd_store_chunk(int64_t M, T* Eb, const T* ring,
     }
 }
 
+// Column c of the row below's boundary (the contributions its first row pushes into this strip's last row)
+// is written by the strip below.
+__device__ __forceinline__ bool bwd_needed(int c, bool has_producer, int plo, int phi)
+{
+    return has_producer && c >= 0 && c >= plo - 1 && c <= phi;
+}
+
+// One block of 32 backward steps as four groups of 8, taken from the last (Q = 3) to the first. Lane l holds
+// in `nv` the contribution into lane 31's column tau0 - 31 + l, read from L2 ahead of time. Before group q the
+// lanes of that group wait for their values, hand them to the side ring and read their column of the next
+// block ahead, and the lanes of the group after it re-read theirs; after the group, 8 lanes publish lane 0's
+// pushes into the row above for the 8 columns the group finished (the lag between strips is 40 steps instead
+// of 64 with whole blocks: fp32, 16 pairs of 4096 x 4096, band 256, measured on one B200 at 1.35 ms against
+// 1.60). Returns false if the launch aborted.
+template <typename T, bool MASKED, int Q>
+__device__ __forceinline__ bool bwd_group_step(const BwdArgs<T>& a, T* rowA, T* rowB, T* bndring, T* sendring,
+                                               const T* bnd_in, T* bnd_out, int tau0, const Strip& st, int hi0,
+                                               bool has_producer, bool has_consumer, int plo, int phi, int lane,
+                                               T seed, T& nv, T& upc, T& sendv, T& pend, T& acc)
+{
+    const int grp = lane >> 3;
+    const int c = tau0 - 31 + lane;
+    const bool need = bwd_needed(c, has_producer, plo, phi);
+    if (!await_boundary(nv, bnd_in + c, need && grp == Q, a.sy, lane)) return false;
+    if (grp == Q) {
+        bndring[(c + 31) & kSideMask] = need ? nv : T(0);
+        const int cn = c - 32;
+        nv = bwd_needed(cn, has_producer, plo, phi) ? ld_relaxed(bnd_in + cn) : T(0);
+    } else if (grp == ((Q + 3) & 3)) {
+        const int cr = Q == 0 ? c - 32 : c;  // after the last group: the next block's first group
+        if (bwd_needed(cr, has_producer, plo, phi)) nv = ld_relaxed(bnd_in + cr);
+    }
+    __syncwarp();
+    bwd_group<T, MASKED, Q>(rowA, rowB, bndring, sendring, tau0, lane, st.A, st.Z, a.k, seed, upc, sendv, pend, acc);
+    __syncwarp();
+    if (has_consumer && lane < 8) {
+        // Lane 0 finished its pushes into row r0-1 for columns [tau0 + 8Q, tau0 + 8Q + 7].
+        const int cp = tau0 + 8 * Q + lane;
+        if (cp >= 0 && cp >= st.c_begin - 1 && cp <= hi0) st_relaxed(bnd_out + cp, sendring[cp & kSideMask]);
+    }
+    return true;
+}
+template <typename T, bool MASKED>
+__device__ __forceinline__ bool bwd_block_groups(const BwdArgs<T>& a, T* rowA, T* rowB, T* bndring, T* sendring,
+                                                 const T* bnd_in, T* bnd_out, int tau0, const Strip& st, int hi0,
+                                                 bool has_producer, bool has_consumer, int plo, int phi, int lane,
+                                                 T seed, T& nv, T& upc, T& sendv, T& pend, T& acc)
+{
+    return bwd_group_step<T, MASKED, 3>(a, rowA, rowB, bndring, sendring, bnd_in, bnd_out, tau0, st, hi0,
+                                        has_producer, has_consumer, plo, phi, lane, seed, nv, upc, sendv, pend, acc) &&
+           bwd_group_step<T, MASKED, 2>(a, rowA, rowB, bndring, sendring, bnd_in, bnd_out, tau0, st, hi0,
+                                        has_producer, has_consumer, plo, phi, lane, seed, nv, upc, sendv, pend, acc) &&
+           bwd_group_step<T, MASKED, 1>(a, rowA, rowB, bndring, sendring, bnd_in, bnd_out, tau0, st, hi0,
+                                        has_producer, has_consumer, plo, phi, lane, seed, nv, upc, sendv, pend, acc) &&
+           bwd_group_step<T, MASKED, 0>(a, rowA, rowB, bndring, sendring, bnd_in, bnd_out, tau0, st, hi0,
+                                        has_producer, has_consumer, plo, phi, lane, seed, nv, upc, sendv, pend, acc);
+}
+
 template <typename T, int MC>
 __device__ void bwd_strip(const BwdArgs<T>& a, T* ring, T* bndring, T* sendring, int64_t b, int s, int lane,
                           bool skip_publish)
@@ -415,39 +528,26 @@ __device__ void bwd_strip(const BwdArgs<T>& a, T* ring, T* bndring, T* sendring,
     T upc = T(0), sendv = T(0), pend = T(0), acc = seed;
 
     // Contributions from the row below into lane 31's columns of the next block, prefetched.
-    auto needed = [&](int c) { return has_producer && c >= 0 && c >= plo - 1 && c <= phi; };
     T nv = T(0);
     {
         const int c = 32 * k1 - 31 + lane;
-        if (needed(c)) nv = ld_relaxed(bnd_in + c);
+        if (bwd_needed(c, has_producer, plo, phi)) nv = ld_relaxed(bnd_in + c);
     }
 
 #pragma unroll 1
     for (int blk = k1; blk >= k0; --blk) {
         const int tau0 = 32 * blk;
-        {
-            const int c = tau0 - 31 + lane;
-            const bool need = needed(c);
-            if (!await_boundary(nv, bnd_in + c, need, a.sy, lane)) return;
-            bndring[(c + 31) & kSideMask] = need ? nv : T(0);
-            const int cn = c - 32;
-            nv = needed(cn) ? ld_relaxed(bnd_in + cn) : T(0);
-        }
         cp_async_wait<2>();
         __syncwarp();
         if (blk == k1) upc = rowA[(tau0 + 31 - lane) & kRingMask];
-        if (tau0 >= st.Amax && tau0 + 31 <= st.Zmin)
-            bwd_block<T, false>(rowA, rowB, bndring, sendring, tau0, lane, st.A, st.Z, a.k, seed, upc, sendv, pend,
-                                acc);
-        else
-            bwd_block<T, true>(rowA, rowB, bndring, sendring, tau0, lane, st.A, st.Z, a.k, seed, upc, sendv, pend,
-                               acc);
-        __syncwarp();
-        if (has_consumer) {
-            // Lane 0 finished its pushes into row r0-1 for columns [tau0, tau0+31].
-            const int c = tau0 + lane;
-            if (c >= 0 && c >= st.c_begin - 1 && c <= hi0) st_relaxed(bnd_out + c, sendring[c & kSideMask]);
-        }
+        const bool full = tau0 >= st.Amax && tau0 + 31 <= st.Zmin;
+        if (!(full ? bwd_block_groups<T, false>(a, rowA, rowB, bndring, sendring, bnd_in, bnd_out, tau0, st, hi0,
+                                                 has_producer, has_consumer, plo, phi, lane, seed, nv, upc, sendv,
+                                                 pend, acc)
+                   : bwd_block_groups<T, true>(a, rowA, rowB, bndring, sendring, bnd_in, bnd_out, tau0, st, hi0,
+                                                has_producer, has_consumer, plo, phi, lane, seed, nv, upc, sendv,
+                                                pend, acc)))
+            return;
         bwd_store_chunk<T>(M, Eb, ring, blk, st, lane);
         __syncwarp();
         if (blk - 4 >= kmin) bwd_load_chunk<T>(M, Rb, ring, blk - 4, st.r0, st.rows, lane);
