@@ -77,6 +77,15 @@ sdtw_status sdtw_forward(sdtw_dtype dtype, const void* D, int64_t B, int64_t N, 
                          int64_t bandwidth, void* R, void* costs, void* workspace, size_t workspace_bytes,
                          uint32_t* err_word, void* stream);
 
+/* sdtw_forward for an R that only sdtw_backward (same lengths and bandwidth) reads, as the SoftDTW module
+ * saves it: the same costs, and R identical in every cell that backward reads. Where the strip-ticket
+ * kernels run both directions, R is prefilled with +inf only over the 32-column chunks around each strip's
+ * band that the backward loads, instead of everywhere; cells outside them are left unwritten. */
+sdtw_status sdtw_forward_band_r(sdtw_dtype dtype, const void* D, int64_t B, int64_t N, int64_t M,
+                                const void* lengths_x, const void* lengths_y, int lengths_int32, double gamma,
+                                int64_t bandwidth, void* R, void* costs, void* workspace, size_t workspace_bytes,
+                                uint32_t* err_word, void* stream);
+
 /* ---------------------------------------------------------------------------------------------------
  * Forward that allocates nothing (no counterpart in the reference, which always allocates its outputs
  * and temporaries through torch).
@@ -201,6 +210,19 @@ sdtw_status sdtw_backward_x2(const float* R_hi, const float* R_lo, int64_t B, in
 sdtw_status sdtw_pairwise_l2(sdtw_dtype dtype, const void* X, const void* Y, int64_t B, int64_t N, int64_t M,
                              int64_t d, void* D, int* clamp_flags, void* stream);
 
+/* The same cost for a dynamic program that reads only part of D: the cells below the pair's lengths and
+ * inside the Sakoe-Chiba band (bandwidth < 0: no band). On the tensor-core path only the 128 x 128 tiles of
+ * D that hold such a cell are computed (a one-CTA kernel lists them first); the other cells of D are left
+ * unwritten, and clamp_flags cover the computed tiles. Elsewhere all of D is computed. For D that feeds
+ * this library's wavefronts with the same lengths and bandwidth (which read nothing else), as on the
+ * SoftDTW module path with a band; the operator contract (R and E in full) is unchanged by it.
+ * workspace: sdtw_pairwise_l2_band_workspace_bytes(B, N, M) bytes, 16-byte aligned. */
+size_t sdtw_pairwise_l2_band_workspace_bytes(int64_t B, int64_t N, int64_t M);
+sdtw_status sdtw_pairwise_l2_band(sdtw_dtype dtype, const void* X, const void* Y, int64_t B, int64_t N, int64_t M,
+                                  int64_t d, const void* lengths_x, const void* lengths_y, int lengths_are_int32,
+                                  int64_t bandwidth, void* D, int* clamp_flags, void* workspace,
+                                  size_t workspace_bytes, void* stream);
+
 /* ---------------------------------------------------------------------------------------------------
  * Gradient of sum_b g[b] * costs[b] through the squared-L2 cost (the autograd of distances.py:14-18):
  *   G = g[b] * E * [D >= 0 before the clamp]  (read from the sign bit written by sdtw_pairwise_l2)
@@ -211,6 +233,15 @@ sdtw_status sdtw_pairwise_l2(sdtw_dtype dtype, const void* X, const void* Y, int
 sdtw_status sdtw_grad_l2(sdtw_dtype dtype, const void* X, const void* Y, const void* D, const void* E,
                          const void* g, const int* clamp_flags, int64_t B, int64_t N, int64_t M, int64_t d,
                          void* grad_X, void* grad_Y, void* stream);
+
+/* The same gradient for E that is zero outside the cells below the pair's lengths and inside the band (as
+ * sdtw_backward leaves it): on the tensor-core path each 128-row tile contracts only the 32-wide chunks of
+ * E that hold such a cell (zero chunks add nothing), and reads D only there, so D may come from
+ * sdtw_pairwise_l2_band. Elsewhere it is sdtw_grad_l2. */
+sdtw_status sdtw_grad_l2_band(sdtw_dtype dtype, const void* X, const void* Y, const void* D, const void* E,
+                              const void* g, const int* clamp_flags, int64_t B, int64_t N, int64_t M, int64_t d,
+                              const void* lengths_x, const void* lengths_y, int lengths_are_int32, int64_t bandwidth,
+                              void* grad_X, void* grad_Y, void* stream);
 
 /* ---------------------------------------------------------------------------------------------------
  * L1 and cosine cost matrices (the module's distance="l1" / "cosine" path) and their gradients.

@@ -141,6 +141,24 @@ def test_fused_cost_forward_arguments(lib):
     assert lib.sdtw_apply_clamp_mask(null, null, null, 2, 4, 4, null) == -1  # missing buffers
 
 
+def test_band_cost_and_gradient_arguments(lib):
+    """The band-restricted cost and gradient: workspace size and argument checks (nothing is launched)."""
+    null = None
+    # 16 bytes of count, then one int per 128 x 128 tile
+    assert lib.sdtw_pairwise_l2_band_workspace_bytes(16, 4096, 4096) == 16 + 4 * 16 * 32 * 32
+    assert lib.sdtw_pairwise_l2_band_workspace_bytes(3, 129, 1) == 16 + 4 * 3 * 2 * 1
+    assert lib.sdtw_pairwise_l2_band_workspace_bytes(-1, 4, 4) == 0
+    buf = ctypes.c_void_p(4096)  # never dereferenced: every call below returns before any device work
+    assert lib.sdtw_pairwise_l2_band(2, null, null, 1, 4, 4, 4, buf, buf, 0, 3, buf, null, buf, 64, null) == -2  # dtype
+    assert lib.sdtw_pairwise_l2_band(0, null, null, 0, 4, 4, 4, null, null, 0, 3, null, null, null, 0, null) == 0
+    assert lib.sdtw_pairwise_l2_band(0, buf, buf, 1, 4, 4, 4, null, buf, 0, 3, buf, null, buf, 64, null) == -1
+    assert lib.sdtw_pairwise_l2_band(0, buf, buf, 1, 4, 4, 4, buf, buf, 0, 3, buf, null, buf, 8, null) == -3
+    assert lib.sdtw_pairwise_l2_band(0, buf, buf, 1, 4, 4, 4, buf, buf, 0, 3, buf, null,
+                                     ctypes.c_void_p(4100), 64, null) == -3  # workspace not 16-byte aligned
+    assert lib.sdtw_grad_l2_band(0, buf, buf, buf, buf, buf, null, 1, 4, 4, 4, null, buf, 0, 3, buf, null,
+                                 null) == -1
+
+
 def test_fused_cost_policy_is_opt_in(monkeypatch):
     import torch
 

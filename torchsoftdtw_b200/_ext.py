@@ -56,6 +56,7 @@ SIGNATURES: dict[str, tuple] = {
     "sdtw_set_wait_timeout": (None, [_d]),
     "sdtw_forward_workspace_bytes": (_sz, [_i64, _i64, _i64, _i]),
     "sdtw_forward": (_i, [_i, _p, _i64, _i64, _i64, _p, _p, _i, _d, _i64, _p, _p, _p, _sz, _p, _p]),
+    "sdtw_forward_band_r": (_i, [_i, _p, _i64, _i64, _i64, _p, _p, _i, _d, _i64, _p, _p, _p, _sz, _p, _p]),
     "sdtw_forward_noalloc": (_i, [_i, _p, _i64, _i64, _i64, _p, _p, _i, _d, _i64, _p, _p, _p, _p]),
     "sdtw_backward_workspace_bytes": (_sz, [_i64, _i64, _i64, _i]),
     "sdtw_backward": (_i, [_i, _p, _p, _i64, _i64, _i64, _p, _p, _i, _d, _i64, _p, _p, _sz, _p, _p]),
@@ -72,6 +73,9 @@ SIGNATURES: dict[str, tuple] = {
     "sdtw_backward_x2": (_i, [_p, _p, _i64, _i64, _i64, _p, _p, _i, _d, _i64, _p, _p, _p]),
     "sdtw_pairwise_l2": (_i, [_i, _p, _p, _i64, _i64, _i64, _i64, _p, _p, _p]),
     "sdtw_grad_l2": (_i, [_i, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _p, _p, _p]),
+    "sdtw_pairwise_l2_band_workspace_bytes": (_sz, [_i64, _i64, _i64]),
+    "sdtw_pairwise_l2_band": (_i, [_i, _p, _p, _i64, _i64, _i64, _i64, _p, _p, _i, _i64, _p, _p, _p, _sz, _p]),
+    "sdtw_grad_l2_band": (_i, [_i, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _p, _p, _i, _i64, _p, _p, _p]),
     "sdtw_pairwise_dist": (_i, [_i, _i, _p, _p, _i64, _i64, _i64, _i64, _d, _p, _p]),
     "sdtw_grad_dist_workspace_bytes": (_sz, [_i64, _i64, _i]),
     "sdtw_grad_dist": (_i, [_i, _i, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _d, _p, _p, _p, _p]),

@@ -480,13 +480,13 @@ namespace {
 
 template <typename T>
 sdtw_status launch_pairwise(const void* X, const void* Y, int64_t B, int64_t N, int64_t M, int64_t d, void* D,
-                            int* clamp_flags, cudaStream_t s)
+                            int* clamp_flags, cudaStream_t s, const DpRegion* region = nullptr, void* ws = nullptr)
 {
     if constexpr (sizeof(T) == 4) {
         if (g_distance_path == 0 && pairwise_tc_supported(X, Y, D, B, N, M, d)) {
             const cudaError_t e = pairwise_tc_launch(static_cast<const float*>(X), static_cast<const float*>(Y),
                                                      static_cast<float*>(D), clamp_flags, B, N, M, d,
-                                                     wait_timeout_s(), s);
+                                                     wait_timeout_s(), s, false, 0.f, region, ws);
             return e == cudaSuccess ? SDTW_OK : static_cast<sdtw_status>(e);
         }
     }
@@ -527,7 +527,7 @@ sdtw_status launch_pairwise(const void* X, const void* Y, int64_t B, int64_t N, 
 template <typename T>
 sdtw_status launch_grad(const void* X, const void* Y, const void* D, const void* E, const void* g,
                         const int* clamp_flags, int64_t B, int64_t N, int64_t M, int64_t d, void* gX, void* gY,
-                        cudaStream_t s)
+                        cudaStream_t s, const DpRegion* region = nullptr)
 {
     const unsigned cblocks = static_cast<unsigned>((d + kTile - 1) / kTile);
     bool gx_done = false, gy_done = false;
@@ -536,7 +536,7 @@ sdtw_status launch_grad(const void* X, const void* Y, const void* D, const void*
             const cudaError_t e = grad_x_tc_launch(static_cast<const float*>(X), static_cast<const float*>(Y),
                                                    static_cast<const float*>(D), static_cast<const float*>(E),
                                                    static_cast<const float*>(g), clamp_flags, static_cast<float*>(gX),
-                                                   B, N, M, d, wait_timeout_s(), s);
+                                                   B, N, M, d, wait_timeout_s(), s, nullptr, 0.f, region);
             if (e != cudaSuccess) return static_cast<sdtw_status>(e);
             gx_done = true;
         }
@@ -545,7 +545,7 @@ sdtw_status launch_grad(const void* X, const void* Y, const void* D, const void*
             const cudaError_t e = grad_y_tc_launch(static_cast<const float*>(X), static_cast<const float*>(Y),
                                                    static_cast<const float*>(D), static_cast<const float*>(E),
                                                    static_cast<const float*>(g), clamp_flags, static_cast<float*>(gY),
-                                                   B, N, M, d, wait_timeout_s(), s);
+                                                   B, N, M, d, wait_timeout_s(), s, nullptr, 0.f, region);
             if (e != cudaSuccess) return static_cast<sdtw_status>(e);
             gy_done = true;
         }
@@ -616,6 +616,51 @@ extern "C" {
  * supported), 1 forces the mma.sync kernels, 2 the CUDA-core kernels. */
 void sdtw_debug_force_distance_path(int path) { g_distance_path = (path >= 0 && path <= 3) ? path : 0; }
 
+size_t sdtw_pairwise_l2_band_workspace_bytes(int64_t B, int64_t N, int64_t M)
+{
+    if (!sizes_ok(B, N, M, 0)) return 0;
+    const int64_t nb = B < kBatchChunk ? B : kBatchChunk;
+    return pairwise_tc_region_ws_bytes(nb, N, M);
+}
+
+sdtw_status sdtw_pairwise_l2_band(sdtw_dtype dtype, const void* X, const void* Y, int64_t B, int64_t N, int64_t M,
+                                  int64_t d, const void* lengths_x, const void* lengths_y, int lengths_are_int32,
+                                  int64_t bandwidth, void* D, int* clamp_flags, void* workspace,
+                                  size_t workspace_bytes, void* stream)
+{
+    if (dtype != SDTW_F32 && dtype != SDTW_F64) return SDTW_EDTYPE;
+    if (!sizes_ok(B, N, M, d)) return SDTW_EINVAL;
+    if (B == 0) return SDTW_OK;
+    if (!lengths_x || !lengths_y) return SDTW_EINVAL;
+    if (workspace_bytes < sdtw_pairwise_l2_band_workspace_bytes(B, N, M) || !workspace ||
+        (reinterpret_cast<uintptr_t>(workspace) & 15))
+        return SDTW_EWORKSPACE;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (clamp_flags) {
+        const cudaError_t e = cudaMemsetAsync(clamp_flags, 0, static_cast<size_t>(B) * sizeof(int), s);
+        if (e != cudaSuccess) return static_cast<sdtw_status>(e);
+    }
+    if (N == 0 || M == 0) return SDTW_OK;
+    if (!D || (d > 0 && (!X || !Y))) return SDTW_EINVAL;
+    const size_t es = dtype == SDTW_F32 ? 4 : 8;
+    const size_t ls = lengths_are_int32 ? 4 : 8;
+    for (int64_t b0 = 0; b0 < B; b0 += kBatchChunk) {
+        const int64_t nb = B - b0 < kBatchChunk ? B - b0 : kBatchChunk;
+        const void* Xc = at_elem(X, b0 * N * d, es);
+        const void* Yc = at_elem(Y, b0 * M * d, es);
+        void* Dc = at_elem(D, b0 * N * M, es);
+        int* fc = clamp_flags ? clamp_flags + b0 : nullptr;
+        const DpRegion region{at_elem(lengths_x, b0, ls), at_elem(lengths_y, b0, ls), lengths_are_int32 ? 1 : 0,
+                              bandwidth};
+        // The tile list needs the tensor-core kernel; every other path computes all of D (a superset).
+        const sdtw_status st = dtype == SDTW_F32
+                                   ? launch_pairwise<float>(Xc, Yc, nb, N, M, d, Dc, fc, s, &region, workspace)
+                                   : launch_pairwise<double>(Xc, Yc, nb, N, M, d, Dc, fc, s);
+        if (st != SDTW_OK) return st;
+    }
+    return SDTW_OK;
+}
+
 sdtw_status sdtw_pairwise_l2(sdtw_dtype dtype, const void* X, const void* Y, int64_t B, int64_t N, int64_t M,
                              int64_t d, void* D, int* clamp_flags, void* stream)
 {
@@ -644,9 +689,14 @@ sdtw_status sdtw_pairwise_l2(sdtw_dtype dtype, const void* X, const void* Y, int
     return SDTW_OK;
 }
 
-sdtw_status sdtw_grad_l2(sdtw_dtype dtype, const void* X, const void* Y, const void* D, const void* E, const void* g,
+}  // extern "C"
+
+namespace sdtw {
+namespace {
+sdtw_status grad_l2_impl(sdtw_dtype dtype, const void* X, const void* Y, const void* D, const void* E, const void* g,
                          const int* clamp_flags, int64_t B, int64_t N, int64_t M, int64_t d, void* grad_X,
-                         void* grad_Y, void* stream)
+                         void* grad_Y, void* stream, const void* lengths_x, const void* lengths_y,
+                         int lengths_are_int32, int64_t bandwidth)
 {
     if (dtype != SDTW_F32 && dtype != SDTW_F64) return SDTW_EDTYPE;
     if (!sizes_ok(B, N, M, d)) return SDTW_EINVAL;
@@ -668,12 +718,38 @@ sdtw_status sdtw_grad_l2(sdtw_dtype dtype, const void* X, const void* Y, const v
         const int* fc = clamp_flags ? clamp_flags + b0 : nullptr;
         void* gXc = grad_X ? at_elem(grad_X, b0 * N * d, es) : nullptr;
         void* gYc = grad_Y ? at_elem(grad_Y, b0 * M * d, es) : nullptr;
+        const size_t ls = lengths_are_int32 ? 4 : 8;
+        const DpRegion region{lengths_x ? at_elem(lengths_x, b0, ls) : nullptr,
+                              lengths_y ? at_elem(lengths_y, b0, ls) : nullptr, lengths_are_int32 ? 1 : 0, bandwidth};
+        const DpRegion* rp = lengths_x ? &region : nullptr;
         const sdtw_status st = dtype == SDTW_F32
-                                   ? launch_grad<float>(Xc, Yc, Dc, Ec, gc, fc, nb, N, M, d, gXc, gYc, s)
+                                   ? launch_grad<float>(Xc, Yc, Dc, Ec, gc, fc, nb, N, M, d, gXc, gYc, s, rp)
                                    : launch_grad<double>(Xc, Yc, Dc, Ec, gc, fc, nb, N, M, d, gXc, gYc, s);
         if (st != SDTW_OK) return st;
     }
     return SDTW_OK;
+}
+}  // namespace
+}  // namespace sdtw
+
+extern "C" {
+
+sdtw_status sdtw_grad_l2(sdtw_dtype dtype, const void* X, const void* Y, const void* D, const void* E, const void* g,
+                         const int* clamp_flags, int64_t B, int64_t N, int64_t M, int64_t d, void* grad_X,
+                         void* grad_Y, void* stream)
+{
+    return grad_l2_impl(dtype, X, Y, D, E, g, clamp_flags, B, N, M, d, grad_X, grad_Y, stream, nullptr, nullptr, 0,
+                        -1);
+}
+
+sdtw_status sdtw_grad_l2_band(sdtw_dtype dtype, const void* X, const void* Y, const void* D, const void* E,
+                              const void* g, const int* clamp_flags, int64_t B, int64_t N, int64_t M, int64_t d,
+                              const void* lengths_x, const void* lengths_y, int lengths_are_int32, int64_t bandwidth,
+                              void* grad_X, void* grad_Y, void* stream)
+{
+    if (!lengths_x || !lengths_y) return SDTW_EINVAL;
+    return grad_l2_impl(dtype, X, Y, D, E, g, clamp_flags, B, N, M, d, grad_X, grad_Y, stream, lengths_x, lengths_y,
+                        lengths_are_int32, bandwidth);
 }
 
 }  // extern "C"

@@ -12,6 +12,7 @@
 
 #include "sdtw_b200.h"
 #include "sdtw_common.cuh"
+#include "sdtw_strip.cuh"
 #include "sdtw_tcgen05.h"
 
 namespace sdtw {
@@ -282,6 +283,81 @@ __device__ __forceinline__ bool wait_role(uint32_t bar, uint32_t parity, uint64_
     }
 }
 
+// ---- the cells a pair's dynamic program reads --------------------------------------------------------
+// Columns [c0, c1] that hold the in-band cells of rows i0 .. i1 of pair b lying below its lengths (rows
+// i < nx, columns j < ny), for E (or D) of nrows x ncols. With trans the rows are E's columns (the band is
+// symmetric in its two axes: band_row_range(j, ny, nx, bw) is the row interval of column j). Band intervals
+// are non-decreasing in the row, so the first and last rows bound them. False when no such cell exists: rows
+// past the length, an empty side, or lengths outside [0, nrows] x [0, ncols] (an empty pair for the
+// wavefront kernels).
+__device__ __forceinline__ bool dp_cols_of_rows(const Lengths& len, int64_t b, int64_t nrows, int64_t ncols,
+                                                int64_t bw, int64_t i0, int64_t i1, bool trans, int64_t& c0,
+                                                int64_t& c1)
+{
+    const int64_t nx = len.x(b), ny = len.y(b);
+    if (nx <= 0 || nx > nrows || ny <= 0 || ny > ncols) return false;
+    const int64_t nr = trans ? ny : nx, nc = trans ? nx : ny;
+    if (i0 >= nr) return false;
+    if (i1 > nr - 1) i1 = nr - 1;
+    int64_t lo, hi, lo1, hi1;
+    band_row_range(i0, nr, nc, bw, lo, hi);
+    band_row_range(i1, nr, nc, bw, lo1, hi1);
+    c0 = lo;
+    c1 = hi1;
+    return c0 <= c1;
+}
+
+// The tiles of D (B pairs of nit x njt tiles of 128 x 128) that hold a cell of the region, as tile ids
+// (b * nit + row tile) * njt + column tile in increasing order, and their count. One CTA of 1024 threads,
+// one (pair, row tile) per thread per round, an exclusive scan of the per-row counts placing the ids.
+__global__ void __launch_bounds__(1024) band_tile_list_kernel(Lengths len, int B, int N, int M, int64_t bw,
+                                                              int nit, int njt, int* count, int* list)
+{
+    __shared__ int wsum[32];
+    __shared__ int base;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    if (tid == 0) base = 0;
+    __syncthreads();
+    const int rows = B * nit;
+    for (int e0 = 0; e0 < rows; e0 += 1024) {
+        const int e = e0 + tid;
+        int ct0 = 0, n = 0;
+        if (e < rows) {
+            const int b = e / nit, rt = e % nit;
+            int64_t c0, c1;
+            if (dp_cols_of_rows(len, b, N, M, bw, static_cast<int64_t>(rt) * kT, static_cast<int64_t>(rt) * kT + kT - 1,
+                                false, c0, c1)) {
+                ct0 = static_cast<int>(c0 / kT);
+                n = static_cast<int>(c1 / kT) - ct0 + 1;
+            }
+        }
+        int v = n;  // inclusive scan within the warp
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int t = __shfl_up_sync(kFull, v, o);
+            if (lane >= o) v += t;
+        }
+        if (lane == 31) wsum[warp] = v;
+        __syncthreads();
+        if (warp == 0) {
+            int w = wsum[lane];
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int t = __shfl_up_sync(kFull, w, o);
+                if (lane >= o) w += t;
+            }
+            wsum[lane] = w;
+        }
+        __syncthreads();
+        const int at = base + (warp > 0 ? wsum[warp - 1] : 0) + v - n;
+        for (int k = 0; k < n; ++k) list[at + k] = e * njt + ct0 + k;
+        __syncthreads();
+        if (tid == 0) base += wsum[31];
+        __syncthreads();
+    }
+    if (tid == 0) *count = base;
+}
+
 struct GradTcArgs {
     const float* X;
     const float* D;
@@ -294,9 +370,32 @@ struct GradTcArgs {
     int nrt;                 // row tiles per pair
     int nk;                  // chunks per tile
     unsigned long long timeout_ns;
+    Lengths len;             // BANDED kernels: E is zero outside the region of len and bw
+    int64_t bw;
 };
 
-template <int DPAD, bool TRANS>
+// The K chunks (32 columns of E; rows of E with TRANS) a row tile contracts: with BANDED, those that hold a
+// cell of the region (one chunk of zeros where the tile holds none, so that its accumulator is written), else
+// all. BANDED is a template parameter so that the kernel without a region keeps its registers (the split
+// warps run at the 72-register cap of 832 threads).
+template <bool TRANS, bool BANDED>
+__device__ __forceinline__ void grad_chunk_range(const GradTcArgs& a, int b, int rt, int& kc0, int& nkc)
+{
+    kc0 = 0;
+    nkc = a.nk;
+    if constexpr (!BANDED) return;
+    const int64_t ne = TRANS ? a.M : a.N, me = TRANS ? a.N : a.M;  // E is (B, ne, me)
+    int64_t c0, c1;
+    if (!dp_cols_of_rows(a.len, b, ne, me, a.bw, static_cast<int64_t>(rt) * kGT,
+                         static_cast<int64_t>(rt) * kGT + kGT - 1, TRANS, c0, c1)) {
+        nkc = 1;
+        return;
+    }
+    kc0 = static_cast<int>(c0 / kGKC);
+    nkc = static_cast<int>(c1 / kGKC) - kc0 + 1;
+}
+
+template <int DPAD, bool TRANS, bool BANDED>
 __global__ void __launch_bounds__(kGradThreads, 1) grad_x_tc_kernel(const __grid_constant__ CUtensorMap me,
                                                                     const __grid_constant__ CUtensorMap my,
                                                                     GradTcArgs a)
@@ -358,24 +457,31 @@ __global__ void __launch_bounds__(kGradThreads, 1) grad_x_tc_kernel(const __grid
     if (warp == 0) {
         // ---------------- TMA producer ----------------
         if (lane == 0) {
-            const int Q = my_tiles * a.nk;  // chunks of this CTA
-            int issued = 0;
-            for (int q = 0; q < Q; ++q) {
-                const int s = q % G::S;
-                if (q >= G::S && !wait_role(raw_empty + 8 * s, ((q / G::S) - 1) & 1, a.timeout_ns, abort)) break;
-                const int t = static_cast<int>(blockIdx.x) + (q / a.nk) * static_cast<int>(gridDim.x);
-                const int b = t / a.nrt, rt = t % a.nrt, kc = q % a.nk;
-                const uint32_t dst = base + s * G::RAW;
-                mbar_expect_tx(raw_full + 8 * s, G::RAW);
-                if constexpr (TRANS)
-                    tma_load_3d(dst, &me, raw_full + 8 * s, rt * kGT, kc * kGKC, b);  // E rows kc*32.., columns rt*128..
-                else
-                    tma_load_3d(dst, &me, raw_full + 8 * s, kc * kGKC, rt * kGT, b);
+            int issued = 0, q = 0;
+            bool ok = true;
+            for (int tl = 0; tl < my_tiles && ok; ++tl) {
+                const int t = static_cast<int>(blockIdx.x) + tl * static_cast<int>(gridDim.x);
+                const int b = t / a.nrt, rt = t % a.nrt;
+                int kc0, nkc;
+                grad_chunk_range<TRANS, BANDED>(a, b, rt, kc0, nkc);
+                for (int kc = kc0; kc < kc0 + nkc; ++kc, ++q) {
+                    const int s = q % G::S;
+                    if (q >= G::S && !wait_role(raw_empty + 8 * s, ((q / G::S) - 1) & 1, a.timeout_ns, abort)) {
+                        ok = false;
+                        break;
+                    }
+                    const uint32_t dst = base + s * G::RAW;
+                    mbar_expect_tx(raw_full + 8 * s, G::RAW);
+                    if constexpr (TRANS)  // E rows kc*32.., columns rt*128..
+                        tma_load_3d(dst, &me, raw_full + 8 * s, rt * kGT, kc * kGKC, b);
+                    else
+                        tma_load_3d(dst, &me, raw_full + 8 * s, kc * kGKC, rt * kGT, b);
 #pragma unroll
-                for (int bx = 0; bx < G::NBOX; ++bx)
-                    tma_load_3d(dst + kEChunk + bx * (kGKC * G::YB * 4), &my, raw_full + 8 * s, bx * G::YB,
-                                kc * kGKC, b);
-                issued = q + 1;
+                    for (int bx = 0; bx < G::NBOX; ++bx)
+                        tma_load_3d(dst + kEChunk + bx * (kGKC * G::YB * 4), &my, raw_full + 8 * s, bx * G::YB,
+                                    kc * kGKC, b);
+                    issued = q + 1;
+                }
             }
             // Before the CTA ends: every load issued into each stage has landed (the last one per stage
             // completes after all earlier ones, which the split released).
@@ -393,7 +499,12 @@ __global__ void __launch_bounds__(kGradThreads, 1) grad_x_tc_kernel(const __grid
                 const int ab = tl & 1;
                 if (tl >= 2 && !wait_role(acc_empty + 8 * ab, ((tl >> 1) - 1) & 1, a.timeout_ns, abort)) break;
                 const uint32_t acc = tmem + static_cast<uint32_t>(ab) * G::ACC_COLS;
-                for (int kc = 0; kc < a.nk; ++kc, ++q) {
+                int kc0, nkc;
+                {
+                    const int t = static_cast<int>(blockIdx.x) + tl * static_cast<int>(gridDim.x);
+                    grad_chunk_range<TRANS, BANDED>(a, t / a.nrt, t % a.nrt, kc0, nkc);
+                }
+                for (int kc = 0; kc < nkc; ++kc, ++q) {
                     const int p = q % G::P;
                     if (!wait_role(spl_full + 8 * p, (q / G::P) & 1, a.timeout_ns, abort)) {
                         ok = false;
@@ -415,7 +526,7 @@ __global__ void __launch_bounds__(kGradThreads, 1) grad_x_tc_kernel(const __grid
                                  : "memory");
                     last_commit_bar = 0;
                     last_commit_parity = static_cast<uint32_t>((q / G::P) & 1);
-                    if (kc == a.nk - 1) {
+                    if (kc == nkc - 1) {
                         asm volatile(
                             "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
                                 acc_full + 8 * ab)
@@ -446,8 +557,10 @@ __global__ void __launch_bounds__(kGradThreads, 1) grad_x_tc_kernel(const __grid
             const int i_e = rt * kGT + er;
             const bool masked = !a.ry && (a.clamp_flags == nullptr || a.clamp_flags[b] != 0) && i_e < a.N;
             const float* Drow = a.D + (static_cast<int64_t>(b) * a.N + (i_e < a.N ? i_e : 0)) * a.M;
+            int kc0, nkc;
+            grad_chunk_range<TRANS, BANDED>(a, b, rt, kc0, nkc);
             bool ok = true;
-            for (int kc = 0; kc < a.nk; ++kc, ++q) {
+            for (int kc = kc0; kc < kc0 + nkc; ++kc, ++q) {
                 const int s = q % G::S, p = q % G::P;
                 if (!wait_role(raw_full + 8 * s, (q / G::S) & 1, a.timeout_ns, abort) ||
                     (q >= G::P && !wait_role(spl_empty + 8 * p, ((q / G::P) - 1) & 1, a.timeout_ns, abort))) {
@@ -721,6 +834,8 @@ struct PairwiseTcArgs {
     int B, N, M, d;
     int nit, njt, nk;  // row tiles, column tiles, feature chunks
     unsigned long long timeout_ns;
+    const int* tiles;    // non-null: compute only these tile ids (band_tile_list_kernel), tile_count of them
+    const int* tile_count;
 };
 
 __global__ void __launch_bounds__(kDThreads, 1) pairwise_l2_tc_kernel(const __grid_constant__ CUtensorMap mx,
@@ -745,12 +860,13 @@ __global__ void __launch_bounds__(kDThreads, 1) pairwise_l2_tc_kernel(const __gr
     float* y2s = x2s + 4 * kT;                              // [4][128]
 
     const int per_pair = a.nit * a.njt;
-    const int ntiles = a.B * per_pair;
+    const int ntiles = a.tiles ? *a.tile_count : a.B * per_pair;
     const int my_tiles = blockIdx.x < static_cast<unsigned>(ntiles)
                              ? (ntiles - 1 - static_cast<int>(blockIdx.x)) / static_cast<int>(gridDim.x) + 1
                              : 0;
     auto tile_of = [&](int tl, int& b, int& i0, int& j0) {
-        const int t = static_cast<int>(blockIdx.x) + tl * static_cast<int>(gridDim.x);
+        int t = static_cast<int>(blockIdx.x) + tl * static_cast<int>(gridDim.x);
+        if (a.tiles) t = a.tiles[t];
         b = t / per_pair;
         const int r = t % per_pair;
         i0 = (r / a.njt) * kT;
@@ -998,23 +1114,24 @@ bool make_map(PFN_cuTensorMapEncodeTiled_v12000 encode, CUtensorMap* map, const 
 }
 
 int g_sm_count[128] = {};
-bool g_grad_attr_set[128][10] = {};
+bool g_grad_attr_set[128][20] = {};
 
 // TRANS == false: grad_X of E (B, N, M) against Y (B, M, d), rows of X. TRANS == true: the caller passes the
 // transposed problem (X := Y, Y := X, N := M, M := N, out := grad_Y, ry := the inverse norms of X's rows),
 // and E, D stay the (B, M, N) arrays they are in memory.
-template <int DPAD, bool TRANS>
+template <int DPAD, bool TRANS, bool BANDED>
 cudaError_t grad_tc_launch_t(const float* X, const float* Y, const float* D, const float* E, const float* g,
                              const int* clamp_flags, float* gX, int64_t B, int64_t N, int64_t M, int64_t d,
                              double timeout_s, cudaStream_t s, int dev, int slot,
-                             PFN_cuTensorMapEncodeTiled_v12000 encode, const float* ry, float eps)
+                             PFN_cuTensorMapEncodeTiled_v12000 encode, const float* ry, float eps,
+                             const DpRegion* region)
 {
     using G = GradGeom<DPAD>;
     {
         std::lock_guard<std::mutex> lock(g_tc_mu);
-        const int sl = slot + (TRANS ? 5 : 0);
+        const int sl = slot + (TRANS ? 5 : 0) + (BANDED ? 10 : 0);
         if (!g_grad_attr_set[dev][sl]) {
-            const cudaError_t e = cudaFuncSetAttribute(grad_x_tc_kernel<DPAD, TRANS>,
+            const cudaError_t e = cudaFuncSetAttribute(grad_x_tc_kernel<DPAD, TRANS, BANDED>,
                                                        cudaFuncAttributeMaxDynamicSharedMemorySize, G::BYTES);
             if (e != cudaSuccess) return e;
             g_grad_attr_set[dev][sl] = true;
@@ -1042,10 +1159,12 @@ cudaError_t grad_tc_launch_t(const float* X, const float* Y, const float* D, con
     a.nrt = static_cast<int>((N + kGT - 1) / kGT);
     a.nk = static_cast<int>((M + kGKC - 1) / kGKC);
     a.timeout_ns = static_cast<unsigned long long>(timeout_s * 1e9);
+    a.len = Lengths{BANDED ? region->px : nullptr, BANDED ? region->py : nullptr, BANDED ? region->is32 : 0};
+    a.bw = BANDED ? (region->bw > N + M ? N + M : region->bw) : -1;
     const int64_t tiles = B * a.nrt;
     const int grid = static_cast<int>(tiles < g_sm_count[dev] ? tiles : g_sm_count[dev]);
     count_launch();
-    grad_x_tc_kernel<DPAD, TRANS><<<grid, kGradThreads, G::BYTES, s>>>(me, my, a);
+    grad_x_tc_kernel<DPAD, TRANS, BANDED><<<grid, kGradThreads, G::BYTES, s>>>(me, my, a);
     return cudaGetLastError();
 }
 
@@ -1079,37 +1198,58 @@ cudaError_t tc_prepare(PFN_cuTensorMapEncodeTiled_v12000& encode, int& dev)
     }
     return cudaSuccess;
 }
+
+// grad_tc_launch_t for d's padded width, with or without a region.
+template <bool TRANS>
+cudaError_t grad_tc_dispatch(const float* X, const float* Y, const float* D, const float* E, const float* g,
+                             const int* clamp_flags, float* out, int64_t B, int64_t N, int64_t M, int64_t d,
+                             double timeout_s, cudaStream_t s, int dev, PFN_cuTensorMapEncodeTiled_v12000 encode,
+                             const float* r, float eps, const DpRegion* region)
+{
+    if (region && region->px) {
+        if (d <= 16) return grad_tc_launch_t<16, TRANS, true>(X, Y, D, E, g, clamp_flags, out, B, N, M, d, timeout_s, s, dev, 0, encode, r, eps, region);
+        if (d <= 32) return grad_tc_launch_t<32, TRANS, true>(X, Y, D, E, g, clamp_flags, out, B, N, M, d, timeout_s, s, dev, 1, encode, r, eps, region);
+        if (d <= 64) return grad_tc_launch_t<64, TRANS, true>(X, Y, D, E, g, clamp_flags, out, B, N, M, d, timeout_s, s, dev, 2, encode, r, eps, region);
+        if (d <= 96) return grad_tc_launch_t<96, TRANS, true>(X, Y, D, E, g, clamp_flags, out, B, N, M, d, timeout_s, s, dev, 3, encode, r, eps, region);
+        return grad_tc_launch_t<128, TRANS, true>(X, Y, D, E, g, clamp_flags, out, B, N, M, d, timeout_s, s, dev, 4, encode, r, eps, region);
+    }
+    if (d <= 16) return grad_tc_launch_t<16, TRANS, false>(X, Y, D, E, g, clamp_flags, out, B, N, M, d, timeout_s, s, dev, 0, encode, r, eps, nullptr);
+    if (d <= 32) return grad_tc_launch_t<32, TRANS, false>(X, Y, D, E, g, clamp_flags, out, B, N, M, d, timeout_s, s, dev, 1, encode, r, eps, nullptr);
+    if (d <= 64) return grad_tc_launch_t<64, TRANS, false>(X, Y, D, E, g, clamp_flags, out, B, N, M, d, timeout_s, s, dev, 2, encode, r, eps, nullptr);
+    if (d <= 96) return grad_tc_launch_t<96, TRANS, false>(X, Y, D, E, g, clamp_flags, out, B, N, M, d, timeout_s, s, dev, 3, encode, r, eps, nullptr);
+    return grad_tc_launch_t<128, TRANS, false>(X, Y, D, E, g, clamp_flags, out, B, N, M, d, timeout_s, s, dev, 4, encode, r, eps, nullptr);
+}
 }  // namespace
 
 cudaError_t grad_y_tc_launch(const float* X, const float* Y, const float* D, const float* E, const float* g,
                              const int* clamp_flags, float* gY, int64_t B, int64_t N, int64_t M, int64_t d,
-                             double timeout_s, cudaStream_t s, const float* rx, float eps)
+                             double timeout_s, cudaStream_t s, const float* rx, float eps, const DpRegion* region)
 {
     PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
     int dev = 0;
     const cudaError_t e = tc_prepare(encode, dev);
     if (e != cudaSuccess) return e;
     // The transposed problem: output rows are Y's (M of them), the K extent is N, B operand X.
-    if (d <= 16) return grad_tc_launch_t<16, true>(Y, X, D, E, g, clamp_flags, gY, B, M, N, d, timeout_s, s, dev, 0, encode, rx, eps);
-    if (d <= 32) return grad_tc_launch_t<32, true>(Y, X, D, E, g, clamp_flags, gY, B, M, N, d, timeout_s, s, dev, 1, encode, rx, eps);
-    if (d <= 64) return grad_tc_launch_t<64, true>(Y, X, D, E, g, clamp_flags, gY, B, M, N, d, timeout_s, s, dev, 2, encode, rx, eps);
-    if (d <= 96) return grad_tc_launch_t<96, true>(Y, X, D, E, g, clamp_flags, gY, B, M, N, d, timeout_s, s, dev, 3, encode, rx, eps);
-    return grad_tc_launch_t<128, true>(Y, X, D, E, g, clamp_flags, gY, B, M, N, d, timeout_s, s, dev, 4, encode, rx, eps);
+    return grad_tc_dispatch<true>(Y, X, D, E, g, clamp_flags, gY, B, M, N, d, timeout_s, s, dev, encode, rx, eps,
+                                  region);
 }
 
 cudaError_t grad_x_tc_launch(const float* X, const float* Y, const float* D, const float* E, const float* g,
                              const int* clamp_flags, float* gX, int64_t B, int64_t N, int64_t M, int64_t d,
-                             double timeout_s, cudaStream_t s, const float* ry, float eps)
+                             double timeout_s, cudaStream_t s, const float* ry, float eps, const DpRegion* region)
 {
     PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
     int dev = 0;
     const cudaError_t e = tc_prepare(encode, dev);
     if (e != cudaSuccess) return e;
-    if (d <= 16) return grad_tc_launch_t<16, false>(X, Y, D, E, g, clamp_flags, gX, B, N, M, d, timeout_s, s, dev, 0, encode, ry, eps);
-    if (d <= 32) return grad_tc_launch_t<32, false>(X, Y, D, E, g, clamp_flags, gX, B, N, M, d, timeout_s, s, dev, 1, encode, ry, eps);
-    if (d <= 64) return grad_tc_launch_t<64, false>(X, Y, D, E, g, clamp_flags, gX, B, N, M, d, timeout_s, s, dev, 2, encode, ry, eps);
-    if (d <= 96) return grad_tc_launch_t<96, false>(X, Y, D, E, g, clamp_flags, gX, B, N, M, d, timeout_s, s, dev, 3, encode, ry, eps);
-    return grad_tc_launch_t<128, false>(X, Y, D, E, g, clamp_flags, gX, B, N, M, d, timeout_s, s, dev, 4, encode, ry, eps);
+    return grad_tc_dispatch<false>(X, Y, D, E, g, clamp_flags, gX, B, N, M, d, timeout_s, s, dev, encode, ry, eps,
+                                   region);
+}
+
+size_t pairwise_tc_region_ws_bytes(int64_t B, int64_t N, int64_t M)
+{
+    return 16 + 4 * static_cast<size_t>(B) * static_cast<size_t>((N + kT - 1) / kT) *
+                    static_cast<size_t>((M + kT - 1) / kT);
 }
 
 bool pairwise_tc_supported(const void* X, const void* Y, const void* D, int64_t B, int64_t N, int64_t M, int64_t d)
@@ -1120,7 +1260,8 @@ bool pairwise_tc_supported(const void* X, const void* Y, const void* D, int64_t 
 }
 
 cudaError_t pairwise_tc_launch(const float* X, const float* Y, float* D, int* clamp_flags, int64_t B, int64_t N,
-                               int64_t M, int64_t d, double timeout_s, cudaStream_t s, bool cosine, float eps)
+                               int64_t M, int64_t d, double timeout_s, cudaStream_t s, bool cosine, float eps,
+                               const DpRegion* region, void* ws)
 {
     PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
     cudaError_t e = get_encode(encode);
@@ -1159,7 +1300,19 @@ cudaError_t pairwise_tc_launch(const float* X, const float* Y, float* D, int* cl
     a.njt = static_cast<int>((M + kT - 1) / kT);
     a.nk = static_cast<int>((d + kKC - 1) / kKC);
     a.timeout_ns = static_cast<unsigned long long>(timeout_s * 1e9);
+    a.tiles = nullptr;
+    a.tile_count = nullptr;
     const int64_t tiles = B * a.nit * a.njt;
+    if (region && region->px && ws && tiles < (int64_t(1) << 31)) {
+        int* count = static_cast<int*>(ws);
+        int* list = count + 4;
+        const Lengths len{region->px, region->py, region->is32};
+        const int64_t bw = region->bw > N + M ? N + M : region->bw;
+        count_launch();
+        band_tile_list_kernel<<<1, 1024, 0, s>>>(len, a.B, a.N, a.M, bw, a.nit, a.njt, count, list);
+        a.tiles = list;
+        a.tile_count = count;
+    }
     const int grid = static_cast<int>(tiles < g_sm_count[dev] ? tiles : g_sm_count[dev]);
     count_launch();
     pairwise_l2_tc_kernel<<<grid, kDThreads, kDSmemBytes, s>>>(mx, my, md, a);

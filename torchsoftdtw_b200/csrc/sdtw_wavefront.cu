@@ -317,6 +317,36 @@ __global__ void sdtw_fill_r_kernel(T* R, int64_t total, int64_t slab)
         R[e] = (e % slab == 0) ? T(0) : INF;
 }
 
+// The part of R the strip-ticket backward reads, set to +inf (R[b, 0, 0] to 0), for an R that only that
+// backward reads: for strip s of pair b, the padded rows r0 .. r0 + rows (D rows r0 - 1 .. r0 + rows - 1) over
+// the 32-column chunks bwd_load_chunk loads, D columns [32 kmin, 32 k1 + 31] with kmin = (c_begin - 1) >> 5,
+// k1 = (c_end + 31) >> 5, clipped to the padding. The forward then writes its swept cells over it. One CTA
+// per strip; strips without cells (past the length, empty or invalid pairs) are not read and not filled.
+template <typename T>
+__global__ void sdtw_fill_r_band_kernel(T* R, Lengths len, int64_t N, int64_t M, int64_t bw, int S)
+{
+    const T INF = Num<T>::inf();
+    const int64_t b = blockIdx.x / S;
+    const int s = static_cast<int>(blockIdx.x % S);
+    const int64_t nx = len.x(b), ny = len.y(b);
+    if (nx <= 0 || nx > N || ny <= 0 || ny > M) return;
+    const int64_t r0 = 32 * static_cast<int64_t>(s);
+    if (r0 >= nx) return;
+    const int64_t rows = nx - r0 < 32 ? nx - r0 : 32;
+    int64_t lo, hi, lo1, hi1;
+    band_row_range(r0, nx, ny, bw, lo, hi);
+    band_row_range(r0 + rows - 1, nx, ny, bw, lo1, hi1);
+    const int64_t kmin = floor_div(lo - 1, 32), k1 = (hi1 + 31) >> 5;
+    const int64_t p0 = 32 * kmin + 1 > 0 ? 32 * kmin + 1 : 0;       // padded columns [p0, p1]
+    const int64_t p1 = 32 * k1 + 32 < M + 1 ? 32 * k1 + 32 : M + 1;
+    const int64_t pitch = M + 2, w = p1 - p0 + 1;
+    T* Rb = R + b * (N + 2) * pitch;
+    for (int64_t e = threadIdx.x; e < (rows + 1) * w; e += blockDim.x) {
+        const int64_t r = r0 + e / w, c = p0 + e % w;
+        Rb[r * pitch + c] = (r == 0 && c == 0) ? T(0) : INF;
+    }
+}
+
 // ==================================================================================================
 // Backward
 // ==================================================================================================
@@ -830,7 +860,7 @@ bool uses_tiles(const DeviceInfo& di, int64_t B, int64_t N, int64_t M)
 template <typename T>
 sdtw_status launch_forward(const void* D, int64_t B, int64_t N, int64_t M, const void* lx, const void* ly, int is32,
                            double gamma, int64_t bw, void* R, void* costs, void* ws, uint32_t* err,
-                           cudaStream_t stream, void* Rt = nullptr)
+                           cudaStream_t stream, void* Rt = nullptr, bool band_r = false)
 {
     const DeviceInfo* di = nullptr;
     cudaError_t e = device_info(di);
@@ -855,7 +885,12 @@ sdtw_status launch_forward(const void* D, int64_t B, int64_t N, int64_t M, const
     e = cudaMemsetAsync(static_cast<char*>(ws) + kHeader, 0xff, bnd_bytes(B, N, M, sizeof(T)), stream);
     if (e != cudaSuccess) return from_cuda(e);
     const int64_t slab = (N + 2) * (M + 2);
-    {
+    if (band_r && !use_warp_kernels<T>(*di, B, N, M) && choose_pair_warps<T>(*di, true, B, N, M) == 0) {
+        // R for the strip-ticket backward alone: only the chunks it loads.
+        count_launch();
+        sdtw_fill_r_band_kernel<T><<<static_cast<unsigned>(B * S), 256, 0, stream>>>(
+            static_cast<T*>(R), Lengths{lx, ly, is32}, N, M, clamp_bw(bw, N, M), static_cast<int>(S));
+    } else {
         const int64_t total = B * slab;
         const int threads = 256;
         const int64_t want = (total + threads - 1) / threads;
@@ -1059,6 +1094,25 @@ sdtw_status sdtw_forward_noalloc(sdtw_dtype dtype, const void* D, int64_t B, int
                                      err_word, s);
     return launch_forward<double>(D, B, N, M, lengths_x, lengths_y, lengths_int32, gamma, bandwidth, R, costs, ws,
                                   err_word, s);
+}
+
+sdtw_status sdtw_forward_band_r(sdtw_dtype dtype, const void* D, int64_t B, int64_t N, int64_t M,
+                                const void* lengths_x, const void* lengths_y, int lengths_int32, double gamma,
+                                int64_t bandwidth, void* R, void* costs, void* workspace, size_t workspace_bytes,
+                                uint32_t* err_word, void* stream)
+{
+    if (dtype != SDTW_F32 && dtype != SDTW_F64) return SDTW_EDTYPE;
+    if (!common_args_ok(B, N, M, gamma)) return SDTW_EINVAL;
+    if (B == 0) return SDTW_OK;
+    if (!lengths_x || !lengths_y || !R || !costs || !err_word || (N * M > 0 && !D)) return SDTW_EINVAL;
+    if (!workspace || workspace_bytes < sdtw_forward_workspace_bytes(B, N, M, dtype)) return SDTW_EWORKSPACE;
+    if (B * strips_of(N) >= (int64_t(1) << 31)) return SDTW_EINVAL;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (dtype == SDTW_F32)
+        return launch_forward<float>(D, B, N, M, lengths_x, lengths_y, lengths_int32, gamma, bandwidth, R, costs,
+                                     workspace, err_word, s, nullptr, true);
+    return launch_forward<double>(D, B, N, M, lengths_x, lengths_y, lengths_int32, gamma, bandwidth, R, costs,
+                                  workspace, err_word, s, nullptr, true);
 }
 
 sdtw_status sdtw_forward(sdtw_dtype dtype, const void* D, int64_t B, int64_t N, int64_t M, const void* lengths_x,

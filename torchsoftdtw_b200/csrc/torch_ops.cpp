@@ -57,7 +57,12 @@ at::ScalarType acc_type(at::ScalarType st)
 sdtw_dtype code_of(at::ScalarType st) { return st == at::kDouble ? SDTW_F64 : SDTW_F32; }
 
 // Lengths as the kernels read them: int32 or int64, contiguous, on D's device.
-Tensor prep_lengths(const Tensor& l) { return l.contiguous(); }
+// The kernels read both length arrays with one element type: when lengths_x and lengths_y differ (one int32,
+// one int64) both go to int64, as the reference converts each to int64 (softdtw.cpp:67-70).
+Tensor prep_lengths(const Tensor& l, const Tensor& other)
+{
+    return l.scalar_type() == other.scalar_type() ? l.contiguous() : l.to(at::kLong).contiguous();
+}
 
 // One sticky device error word per device, owned by this library for the process lifetime. It is created
 // by the first op call on the device, which must not be under CUDA-graph capture: a word allocated there
@@ -107,8 +112,9 @@ void maybe_sync_check(const Tensor& like, cudaStream_t stream)
                 (bits & SDTW_ERR_BAD_LENGTH) ? " (a length was outside [0, N] / [0, M])" : "");
 }
 
+// band_r: R is read by this library's backward alone (the module path), which needs only part of it.
 std::tuple<Tensor, Tensor> run_forward(const Tensor& Dacc, const Tensor& lx, const Tensor& ly, double gamma,
-                                       int64_t bandwidth)
+                                       int64_t bandwidth, bool band_r = false)
 {
     const int64_t B = Dacc.size(0), N = Dacc.size(1), M = Dacc.size(2);
     const auto st = Dacc.scalar_type();
@@ -118,9 +124,10 @@ std::tuple<Tensor, Tensor> run_forward(const Tensor& Dacc, const Tensor& lx, con
     const size_t wsb = sdtw_forward_workspace_bytes(B, N, M, code_of(st));
     Tensor ws = at::empty({static_cast<int64_t>(wsb)}, opts.dtype(at::kByte));
     cudaStream_t stream = at::cuda::getCurrentCUDAStream(Dacc.get_device()).stream();
-    check_status(sdtw_forward(code_of(st), Dacc.data_ptr(), B, N, M, lx.data_ptr(), ly.data_ptr(),
-                              lx.scalar_type() == at::kInt, gamma, bandwidth, R.data_ptr(), costs.data_ptr(),
-                              ws.data_ptr(), wsb, error_word(Dacc), stream),
+    check_status((band_r ? sdtw_forward_band_r : sdtw_forward)(code_of(st), Dacc.data_ptr(), B, N, M, lx.data_ptr(),
+                                                              ly.data_ptr(), lx.scalar_type() == at::kInt, gamma,
+                                                              bandwidth, R.data_ptr(), costs.data_ptr(), ws.data_ptr(),
+                                                              wsb, error_word(Dacc), stream),
                  "forward");
     maybe_sync_check(Dacc, stream);
     return {costs, R};
@@ -155,7 +162,7 @@ std::tuple<Tensor, Tensor> forward_cuda(const Tensor& D, const Tensor& lengths_x
     same_device(D, lengths_y, "lengths_y");
     const c10::cuda::CUDAGuard guard(D.device());
     const Tensor Dacc = D.to(acc_type(D.scalar_type())).contiguous();
-    return run_forward(Dacc, prep_lengths(lengths_x), prep_lengths(lengths_y), gamma, bandwidth);
+    return run_forward(Dacc, prep_lengths(lengths_x, lengths_y), prep_lengths(lengths_y, lengths_x), gamma, bandwidth);
 }
 
 Tensor backward_cuda(const Tensor& D, const Tensor& R, const Tensor& lengths_x, const Tensor& lengths_y,
@@ -171,7 +178,7 @@ Tensor backward_cuda(const Tensor& D, const Tensor& R, const Tensor& lengths_x, 
     const c10::cuda::CUDAGuard guard(D.device());
     const auto acc = acc_type(D.scalar_type());
     const Tensor Racc = R.to(acc).contiguous();
-    Tensor E = run_backward(Racc, prep_lengths(lengths_x), prep_lengths(lengths_y), gamma, bandwidth, N, M);
+    Tensor E = run_backward(Racc, prep_lengths(lengths_x, lengths_y), prep_lengths(lengths_y, lengths_x), gamma, bandwidth, N, M);
     if (E.scalar_type() != D.scalar_type()) E = E.to(D.scalar_type());
     return E;
 }
@@ -227,7 +234,8 @@ std::tuple<Tensor, Tensor> run_forward_module(const Tensor& Dacc, const Tensor& 
 {
     const int64_t B = Dacc.size(0), N = Dacc.size(1), M = Dacc.size(2);
     const auto st = Dacc.scalar_type();
-    if (B == 0 || N == 0 || M == 0 || !sdtw_r_tiled(B, N, M, code_of(st))) return run_forward(Dacc, lx, ly, gamma, bandwidth);
+    if (B == 0 || N == 0 || M == 0 || !sdtw_r_tiled(B, N, M, code_of(st)))
+        return run_forward(Dacc, lx, ly, gamma, bandwidth, true);
     auto opts = Dacc.options();
     const int64_t S = (N + 31) / 32, NBt = sdtw_r_tiles_elems(1, 32, M) / 1024;
     Tensor Rt = at::empty({B, S, NBt, 32, 32}, opts);
@@ -292,7 +300,7 @@ std::tuple<Tensor, Tensor, Tensor, Tensor> l2_forward_cuda(const Tensor& X, cons
     const Tensor Xc = X.to(acc).contiguous(), Yc = Y.to(acc).contiguous();
     const int64_t B = Xc.size(0), N = Xc.size(1), M = Yc.size(1), d = Xc.size(2);
     if (B > 0 && N > 0 && M > 0 && l2_fused(Xc, Yc)) {
-        const Tensor lx = prep_lengths(lengths_x), ly = prep_lengths(lengths_y);
+        const Tensor lx = prep_lengths(lengths_x, lengths_y), ly = prep_lengths(lengths_y, lengths_x);
         auto opts = Xc.options();
         const int64_t S = (N + 31) / 32, NBt = sdtw_r_tiles_elems(1, 32, M) / 1024;
         Tensor Rt = at::empty({B, S, NBt, 32, 32}, opts);
@@ -314,10 +322,21 @@ std::tuple<Tensor, Tensor, Tensor, Tensor> l2_forward_cuda(const Tensor& X, cons
     Tensor D = at::empty({B, N, M}, Xc.options());
     Tensor flags = at::empty({B}, Xc.options().dtype(at::kInt));
     cudaStream_t stream = at::cuda::getCurrentCUDAStream(X.get_device()).stream();
-    check_status(sdtw_pairwise_l2(code_of(acc), Xc.data_ptr(), Yc.data_ptr(), B, N, M, d, D.data_ptr(),
-                                  flags.data_ptr<int>(), stream),
-                 "pairwise_l2");
-    auto [costs, R] = run_forward_module(D, prep_lengths(lengths_x), prep_lengths(lengths_y), gamma, bandwidth);
+    const Tensor lx = prep_lengths(lengths_x, lengths_y), ly = prep_lengths(lengths_y, lengths_x);
+    if (bandwidth >= 0) {
+        // With a band the wavefronts read only the band's cells of D: compute only the tiles that hold them.
+        const size_t wsb = sdtw_pairwise_l2_band_workspace_bytes(B, N, M);
+        Tensor ws = at::empty({static_cast<int64_t>(wsb)}, Xc.options().dtype(at::kByte));
+        check_status(sdtw_pairwise_l2_band(code_of(acc), Xc.data_ptr(), Yc.data_ptr(), B, N, M, d, lx.data_ptr(),
+                                           ly.data_ptr(), lx.scalar_type() == at::kInt, bandwidth, D.data_ptr(),
+                                           flags.data_ptr<int>(), ws.data_ptr(), wsb, stream),
+                     "pairwise_l2_band");
+    } else {
+        check_status(sdtw_pairwise_l2(code_of(acc), Xc.data_ptr(), Yc.data_ptr(), B, N, M, d, D.data_ptr(),
+                                      flags.data_ptr<int>(), stream),
+                     "pairwise_l2");
+    }
+    auto [costs, R] = run_forward_module(D, lx, ly, gamma, bandwidth);
     return {costs, R, D, flags};
 }
 
@@ -341,8 +360,8 @@ std::tuple<Tensor, Tensor> l2_backward_cuda(const Tensor& X, const Tensor& Y, co
                        R.sizes() == at::IntArrayRef({B, (N + 31) / 32, sdtw_r_tiles_elems(1, 32, M) / 1024, 32, 32});
     TORCH_CHECK((tiled || R.sizes() == at::IntArrayRef({B, N + 2, M + 2})) && R.scalar_type() == acc,
                 "R has the wrong shape or dtype");
-    Tensor E = run_backward_module(R.contiguous(), prep_lengths(lengths_x), prep_lengths(lengths_y), gamma, bandwidth,
-                                   N, M);
+    const Tensor lx = prep_lengths(lengths_x, lengths_y), ly = prep_lengths(lengths_y, lengths_x);
+    Tensor E = run_backward_module(R.contiguous(), lx, ly, gamma, bandwidth, N, M);
     const Tensor g = grad_costs.to(acc).contiguous();
     // Gradients that are not requested come back as empty tensors.
     Tensor gX = need_x ? at::empty({B, N, d}, Xc.options()) : at::empty({0}, X.options());
@@ -360,11 +379,19 @@ std::tuple<Tensor, Tensor> l2_backward_cuda(const Tensor& X, const Tensor& Y, co
         Dg = E;
         flags = at::zeros({B}, flags.options());
     }
-    check_status(sdtw_grad_l2(code_of(acc), Xc.data_ptr(), Yc.data_ptr(), Dg.contiguous().data_ptr(), E.data_ptr(),
-                              g.data_ptr(), flags.data_ptr<int>(), B, N, M, d,
-                              need_x ? gX.data_ptr() : nullptr,
-                              need_y ? gY.data_ptr() : nullptr, stream),
-                 "grad_l2");
+    if (bandwidth >= 0) {
+        // E is zero outside the lengths and the band: the contraction skips the chunks that hold none of it.
+        check_status(sdtw_grad_l2_band(code_of(acc), Xc.data_ptr(), Yc.data_ptr(), Dg.contiguous().data_ptr(),
+                                       E.data_ptr(), g.data_ptr(), flags.data_ptr<int>(), B, N, M, d, lx.data_ptr(),
+                                       ly.data_ptr(), lx.scalar_type() == at::kInt, bandwidth,
+                                       need_x ? gX.data_ptr() : nullptr, need_y ? gY.data_ptr() : nullptr, stream),
+                     "grad_l2_band");
+    } else {
+        check_status(sdtw_grad_l2(code_of(acc), Xc.data_ptr(), Yc.data_ptr(), Dg.contiguous().data_ptr(), E.data_ptr(),
+                                  g.data_ptr(), flags.data_ptr<int>(), B, N, M, d, need_x ? gX.data_ptr() : nullptr,
+                                  need_y ? gY.data_ptr() : nullptr, stream),
+                     "grad_l2");
+    }
     if (need_x && gX.scalar_type() != X.scalar_type()) gX = gX.to(X.scalar_type());
     if (need_y && gY.scalar_type() != Y.scalar_type()) gY = gY.to(Y.scalar_type());
     return {gX, gY};
@@ -396,7 +423,8 @@ std::tuple<Tensor, Tensor, Tensor> dist_forward_cuda(const Tensor& X, const Tens
     check_status(sdtw_pairwise_dist(code_of(acc), static_cast<int>(kind), Xc.data_ptr(), Yc.data_ptr(), B, N, M, d,
                                     eps, D.data_ptr(), stream),
                  "pairwise_dist");
-    auto [costs, R] = run_forward(D, prep_lengths(lengths_x), prep_lengths(lengths_y), gamma, bandwidth);
+    auto [costs, R] = run_forward(D, prep_lengths(lengths_x, lengths_y), prep_lengths(lengths_y, lengths_x), gamma, bandwidth,
+                                  true);
     return {costs, R, D};
 }
 
@@ -414,7 +442,7 @@ std::tuple<Tensor, Tensor> dist_backward_cuda(const Tensor& X, const Tensor& Y, 
     TORCH_CHECK(D.sizes() == at::IntArrayRef({B, N, M}) && D.scalar_type() == acc, "D has the wrong shape or dtype");
     TORCH_CHECK(R.sizes() == at::IntArrayRef({B, N + 2, M + 2}) && R.scalar_type() == acc,
                 "R has the wrong shape or dtype");
-    Tensor E = run_backward(R.contiguous(), prep_lengths(lengths_x), prep_lengths(lengths_y), gamma, bandwidth, N, M);
+    Tensor E = run_backward(R.contiguous(), prep_lengths(lengths_x, lengths_y), prep_lengths(lengths_y, lengths_x), gamma, bandwidth, N, M);
     const Tensor g = grad_costs.to(acc).contiguous();
     Tensor gX = need_x ? at::empty({B, N, d}, Xc.options()) : at::empty({0}, X.options());
     Tensor gY = need_y ? at::empty({B, M, d}, Xc.options()) : at::empty({0}, Y.options());
@@ -445,7 +473,7 @@ std::tuple<Tensor, Tensor, Tensor> forward_x2_cuda(const Tensor& D, const Tensor
     same_device(D, lengths_y, "lengths_y");
     const c10::cuda::CUDAGuard guard(D.device());
     const Tensor Dc = D.to(at::kFloat).contiguous();
-    const Tensor lx = prep_lengths(lengths_x), ly = prep_lengths(lengths_y);
+    const Tensor lx = prep_lengths(lengths_x, lengths_y), ly = prep_lengths(lengths_y, lengths_x);
     const int64_t B = Dc.size(0), N = Dc.size(1), M = Dc.size(2);
     Tensor Rh = at::empty({B, N + 2, M + 2}, Dc.options());
     Tensor Rl = at::empty({B, N + 2, M + 2}, Dc.options());
@@ -476,7 +504,7 @@ Tensor backward_x2_cuda(const Tensor& D, const Tensor& R_hi, const Tensor& R_lo,
     same_device(D, lengths_y, "lengths_y");
     const c10::cuda::CUDAGuard guard(D.device());
     const Tensor Rh = R_hi.contiguous(), Rl = R_lo.contiguous();
-    const Tensor lx = prep_lengths(lengths_x), ly = prep_lengths(lengths_y);
+    const Tensor lx = prep_lengths(lengths_x, lengths_y), ly = prep_lengths(lengths_y, lengths_x);
     Tensor E = at::empty({B, N, M}, Rh.options());
     cudaStream_t stream = at::cuda::getCurrentCUDAStream(D.get_device()).stream();
     check_status(sdtw_backward_x2(Rh.data_ptr<float>(), Rl.data_ptr<float>(), B, N, M, lx.data_ptr(), ly.data_ptr(),
