@@ -537,7 +537,8 @@ def measured_traffic(w, world: int, name: str):
 #   pairwise : write D (X, Y reads are O((N+M)d/NM)) = 1
 #   grad     : read E (D only for pairs with a clamped cell) = 1
 ALGO_BYTES = {"sdtw_forward": 2, "sdtw_backward": 2, "sdtw_forward_tiles": 2, "sdtw_backward_tiles": 2,
-              "sdtw_pairwise_l2": 1, "sdtw_grad_l2": 1}
+              "sdtw_pairwise_l2": 1, "sdtw_grad_l2": 1, "sdtw_forward_band_r": 2, "sdtw_pairwise_l2_band": 1,
+              "sdtw_grad_l2_band": 1}
 
 
 def kernel_times(T, X, Y, lx, ly, w, dev, flush, reps: int = 20):
@@ -585,6 +586,27 @@ def kernel_times(T, X, Y, lx, ly, w, dev, flush, reps: int = 20):
                                                                        w.gamma, w.bandwidth, p(E), p(ws), wsb, p(err),
                                                                        sp)
         del calls["sdtw_forward"], calls["sdtw_backward"]
+    if w.bandwidth >= 0:
+        # With a band the module computes only the cost tiles and E chunks its wavefronts read, and (on the
+        # strip-ticket kernels) prefills only the part of R the backward loads: time those calls.
+        wsp = lib.sdtw_pairwise_l2_band_workspace_bytes(B, N, M)
+        wsbuf = torch.empty(wsp, device=dev, dtype=torch.uint8)
+        band = {
+            "sdtw_pairwise_l2_band": lambda: lib.sdtw_pairwise_l2_band(code, p(X), p(Y), B, N, M, d, p(lx), p(ly),
+                                                                       is32, w.bandwidth, p(D), p(flags),
+                                                                       p(wsbuf), wsp, sp),
+        }
+        for name in list(calls):
+            if name == "sdtw_forward":
+                band["sdtw_forward_band_r"] = lambda: lib.sdtw_forward_band_r(
+                    code, p(D), B, N, M, p(lx), p(ly), is32, w.gamma, w.bandwidth, p(R), p(costs), p(ws), wsf,
+                    p(err), sp)
+            elif name not in ("sdtw_pairwise_l2", "sdtw_grad_l2"):
+                band[name] = calls[name]
+        band["sdtw_grad_l2_band"] = lambda: lib.sdtw_grad_l2_band(code, p(X), p(Y), p(D), p(E), p(g), p(flags), B,
+                                                                  N, M, d, p(lx), p(ly), is32, w.bandwidth, p(gX),
+                                                                  None, sp)
+        calls = band
     out = {}
     for name, fn in calls.items():
         st = fn()

@@ -339,12 +339,10 @@ __global__ void sdtw_fill_r_band_kernel(T* R, Lengths len, int64_t N, int64_t M,
     const int64_t kmin = floor_div(lo - 1, 32), k1 = (hi1 + 31) >> 5;
     const int64_t p0 = 32 * kmin + 1 > 0 ? 32 * kmin + 1 : 0;       // padded columns [p0, p1]
     const int64_t p1 = 32 * k1 + 32 < M + 1 ? 32 * k1 + 32 : M + 1;
-    const int64_t pitch = M + 2, w = p1 - p0 + 1;
+    const int64_t pitch = M + 2;
     T* Rb = R + b * (N + 2) * pitch;
-    for (int64_t e = threadIdx.x; e < (rows + 1) * w; e += blockDim.x) {
-        const int64_t r = r0 + e / w, c = p0 + e % w;
-        Rb[r * pitch + c] = (r == 0 && c == 0) ? T(0) : INF;
-    }
+    for (int64_t r = r0; r <= r0 + rows; ++r)
+        for (int64_t c = p0 + threadIdx.x; c <= p1; c += blockDim.x) Rb[r * pitch + c] = (r == 0 && c == 0) ? T(0) : INF;
 }
 
 // ==================================================================================================
