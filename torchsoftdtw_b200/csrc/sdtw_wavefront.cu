@@ -362,7 +362,12 @@ struct BwdArgs {
     int inject_skip;
 };
 
-// The 8 backward steps tau = tau0 + 8Q + 7 down to tau0 + 8Q of one warp (group Q of the block at tau0).
+// The 8 backward steps tau = tau0 + 8Q + 7 down to tau0 + 8Q of one warp (group Q of the block at tau0). The
+// group's R values and lane 31's contributions are read from shared memory first and its E values and lane 0's
+// pushes written after (every position it reads is read before the group would overwrite it: step u reads
+// column c - 1 = base + u - 1, which step u - 1 overwrites later), so a step's dependency chain holds the
+// shuffle from the row below and no other shared-memory operation (fp32, 16 pairs of 4096 x 4096, band 256:
+// 1.25 ms against 1.35 with the accesses step by step).
 template <typename T, bool MASKED, int Q>
 __device__ __forceinline__ void bwd_group(T* rowA, T* rowB, const T* bndring, T* sendring, int tau0, int lane, int A,
                                           int Z, T k, T seed, T& upc, T& sendv, T& pend, T& acc)
@@ -371,19 +376,23 @@ __device__ __forceinline__ void bwd_group(T* rowA, T* rowB, const T* bndring, T*
     const int src = (lane + 1) & 31;
     const bool lane31 = lane == 31;
     const bool lane0 = lane == 0;
-    const int base = tau0 - lane;
+    const int base = tau0 - lane + 8 * Q;
     // Boundary values of lane 31's column c live at (c + 31) & 63, so a block reads them without wrapping.
-    const T* bndb = bndring + (tau0 & kSideMask);
+    const T* bndb = bndring + (tau0 & kSideMask) + 8 * Q;
+    T ra[8], rb[8], bv[8];
 #pragma unroll
-    for (int u = 8 * Q + 7; u >= 8 * Q; --u) {
-        const int c = base + u;
-        const int cm = (c - 1) & kRingMask;
-        const T rd = rowA[cm];  // R[i-1][c-1]
-        const T rl = rowB[cm];  // R[i][c-1]
-        const T ru = upc;       // R[i-1][c]
+    for (int j = 0; j < 8; ++j) {
+        ra[j] = rowA[(base + j - 1) & kRingMask];  // R[i-1][c-1]
+        rb[j] = rowB[(base + j - 1) & kRingMask];  // R[i][c-1]
+        bv[j] = bndb[j];                           // column tau0 + 8Q + j - 31
+    }
+#pragma unroll
+    for (int j = 7; j >= 0; --j) {
+        const T rd = ra[j];
+        const T rl = rb[j];
+        const T ru = upc;  // R[i-1][c]
         const T recvw = __shfl_sync(kFull, sendv, src);
-        const T bv = bndb[u];  // column tau0 + u - 31
-        const T recv = lane31 ? bv : recvw;
+        const T recv = lane31 ? bv[j] : recvw;
         const T Es = acc + recv;
         const T m = Num<T>::mn(Num<T>::mn(rd, ru), rl);
         const T mc = Num<T>::mn(m, big);
@@ -393,7 +402,7 @@ __device__ __forceinline__ void bwd_group(T* rowA, T* rowB, const T* bndring, T*
         T q = Es * Num<T>::rcp_((ed + eu) + el);
         T Eo = Es;
         if (MASKED) {
-            const int tau = tau0 + u;
+            const int tau = tau0 + 8 * Q + j;
             const bool valid = tau >= A && tau <= Z;
             q = valid ? q : T(0);
             acc = valid ? q * el : seed;
@@ -403,9 +412,15 @@ __device__ __forceinline__ void bwd_group(T* rowA, T* rowB, const T* bndring, T*
         }
         sendv = fma(q, eu, pend);
         pend = q * ed;
-        rowB[c & kRingMask] = Eo;
-        if (lane0) sendring[c & kSideMask] = sendv;
+        rb[j] = Eo;     // E[i][c], written back below
+        bv[j] = sendv;  // lane 0's push into column c of the row above
         upc = rd;
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) rowB[(base + j) & kRingMask] = rb[j];
+    if (lane0) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) sendring[(base + j) & kSideMask] = bv[j];
     }
 }
 
