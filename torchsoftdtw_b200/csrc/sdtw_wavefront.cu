@@ -131,7 +131,14 @@ __device__ __forceinline__ void fwd_store_chunk(const FwdArgs<T>& a, T* Rb, cons
     const int64_t pitch = a.M + 2;
     T* dst = Rb + static_cast<int64_t>(st.r0 + 1) * pitch + col + 1;
     const T* srcp = ring + (col & kRingMask);
-    for (int r = 0; r < st.rows; ++r) dst[r * pitch] = srcp[r * kRing];
+    if (st.rows == 32) {
+        // Unrolled, so the 32 shared-memory loads issue back to back instead of each store waiting for its
+        // own load (16 pairs of 4096 x 4096, band 256: the forward took 6% longer with the rolled loop).
+#pragma unroll
+        for (int r = 0; r < 32; ++r) dst[r * pitch] = srcp[r * kRing];
+    } else {
+        for (int r = 0; r < st.rows; ++r) dst[r * pitch] = srcp[r * kRing];
+    }
 }
 
 // Steps per boundary hand-over in the strip-ticket forward. Groups of 8 steps cut the lag between strips
