@@ -98,7 +98,22 @@ __device__ __forceinline__ void fwd_load_chunk(const FwdArgs<T>& a, const T* Db,
 {
     const int64_t M = a.M;
     const int col0 = 32 * kk;
-    if (a.vec) {
+    if (a.vec && rows == 32) {
+        // Full strip: lane l copies piece l % PPR of rows l / PPR, l / PPR + RPI, ...; one column and byte count
+        // per lane, so the loop is PPR copies with pointer increments (the general loop below recomputes the
+        // row, column and byte count of every piece, on each warp's path between blocks).
+        constexpr int EPP = 16 / sizeof(T);  // elements per 16-byte piece
+        constexpr int PPR = 32 / EPP;        // pieces per row of a chunk
+        constexpr int RPI = 32 / PPR;        // rows per warp-wide copy
+        const int col = col0 + (lane % PPR) * EPP;
+        const int64_t left = (M - col) * static_cast<int64_t>(sizeof(T));
+        const int bytes = left >= 16 ? 16 : (left > 0 ? static_cast<int>(left) : 0);
+        const int r = lane / PPR;
+        const T* src = Db + static_cast<int64_t>(r) * M + (bytes > 0 ? col : 0);
+        T* dst = ring + r * kRing + (col & kRingMask);
+#pragma unroll
+        for (int i = 0; i < PPR; ++i) cp_async_16(dst + i * RPI * kRing, src + i * RPI * M, bytes);
+    } else if (a.vec) {
         constexpr int EPP = 16 / sizeof(T);  // elements per 16-byte piece
         constexpr int PPR = 32 / EPP;        // pieces per row of a chunk
 #pragma unroll 4
